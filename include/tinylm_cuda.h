@@ -1,0 +1,163 @@
+/* tinylm_cuda.h -- C ABI of libtinylm_cuda, the B200 (sm_100a) implementation of
+ * tinylm-c's training-step hot path.
+ *
+ * Drop-in boundary.  Each compute entry point replaces one CPU primitive of the
+ * reference (tinylm.c) one for one, with the same argument order and meaning, so
+ * a call site changes only by name:
+ *
+ *   reference (tinylm.c)                          this library
+ *   mm(Y,X,W,M,K,N)              439-478   ->     tl_matmul(Y,X,W,M,K,N)
+ *   mm_bt(dX,dY,W,M,K,N)         480-508   ->     tl_matmul_bt(dX,dY,W,M,K,N)
+ *   mm_atb(dW,X,dY,M,K,N)        510-537   ->     tl_matmul_at(dW,X,dY,M,K,N)
+ *   global_gradnorm(G,n)        1171-1176  ->     tl_grad_norm(G,n,&norm)
+ *   adamw(P,G,M,V,n,lr,b1,b2,wd,t,gscale)
+ *                               1159-1170  ->     tl_adamw_step(...same...)
+ *   gnm>1 ? 1/gnm : 1      2630-2631, 4739 ->     tl_clip_adamw_step (norm+clip+AdamW,
+ *                                                  no host round trip)
+ *
+ * Conventions
+ *  - All matrices are fp32, row-major, densely packed (leading dimension = the
+ *    row length), exactly as the reference stores them.
+ *  - Every float pointer passed to a compute call is a DEVICE pointer (from
+ *    tl_alloc, cudaMalloc, or a framework allocator).  There is no CPU fallback:
+ *    a host pointer is rejected with TL_EPTR.
+ *  - Calls are asynchronous and ordered on the library stream of the current
+ *    device (tl_set_stream); tl_sync() is the only call that blocks, except the
+ *    few documented to read a result back into host memory.
+ *  - Every call returns TL_OK (0) or a negative TL_E* code and never exits the
+ *    process; tl_last_error() returns the message of the last failure on the
+ *    calling thread.  The reference had no error codes and called exit(1).
+ *  - One host thread drives one device; the library is not re-entrant across
+ *    threads sharing a device.
+ */
+#ifndef TINYLM_CUDA_H
+#define TINYLM_CUDA_H
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TL_OK        0
+#define TL_EINVAL   -1   /* bad shape, size or argument                       */
+#define TL_EALIGN   -2   /* pointer not aligned as the call requires          */
+#define TL_ECUDA    -3   /* CUDA runtime or driver error                      */
+#define TL_ENCCL    -4   /* NCCL error                                        */
+#define TL_ETIMEOUT -5   /* a bounded wait ran out                            */
+#define TL_ENOINIT  -6   /* tl_init / tl_dist_init not called for this device */
+#define TL_EPTR     -7   /* host pointer where a device pointer is required   */
+#define TL_ENOMEM   -8   /* device allocation failed                          */
+
+/* ---------------------------------------------------------------- runtime */
+/* Select `device`, create its library stream and its persistent workspace
+ * (norm partials).  Idempotent per device.  Replaces nothing in the reference
+ * (its buffers are host callocs, fz() tinylm.c:137). */
+int tl_init(int device);
+/* Use `stream` (a cudaStream_t; NULL = the library's own) for all later calls
+ * on the current device. */
+int tl_set_stream(void *stream);
+void *tl_get_stream(void);
+const char *tl_last_error(void);
+const char *tl_version(void);
+int tl_alloc(void **ptr, size_t bytes);
+int tl_free(void *ptr);
+int tl_memcpy_h2d(void *dst_dev, const void *src_host, size_t bytes);
+int tl_memcpy_d2h(void *dst_host, const void *src_dev, size_t bytes);
+int tl_memset(void *dst_dev, int value, size_t bytes);
+int tl_sync(void);
+
+/* Kernel tracing: when on, every library kernel launch is bracketed by CUDA
+ * events on its stream; tl_trace_get returns the summed device time (ms) and
+ * launch count per kernel name (it waits for pending events).  Names in
+ * launch order: tl_trace_names (comma separated).  The reference only has
+ * wall-clock timing (wtime, tinylm.c:139-145). */
+int tl_trace_enable(int on);
+int tl_trace_reset(void);
+int tl_trace_get(const char *name, double *total_ms, long long *count);
+int tl_trace_names(char *buf, size_t len);
+
+/* ------------------------------------------------------------------ GEMMs */
+/* Y[M,N] = X[M,K] @ W[K,N]  (overwrite, beta = 0).  tinylm.c:439-478 (mm). */
+int tl_matmul(float *Y, const float *X, const float *W, int M, int K, int N);
+/* dX[M,K] += dY[M,N] @ W[K,N]^T  (accumulate, beta = 1).  tinylm.c:480-508 (mm_bt). */
+int tl_matmul_bt(float *dX, const float *dY, const float *W, int M, int K, int N);
+/* dW[K,N] += X[M,K]^T @ dY[M,N]  (accumulate, beta = 1).  tinylm.c:510-537 (mm_atb). */
+int tl_matmul_at(float *dW, const float *X, const float *dY, int M, int K, int N);
+
+/* GEMM engine selection, for tests and benchmarks: 0 = automatic (tensor-core
+ * 3xTF32 where the shape allows, else CUDA-core fp32), 1 = CUDA-core fp32 only,
+ * 2 = tensor-core 3xTF32 only (TL_EINVAL where the shape does not allow it).
+ * No counterpart in the reference (its only engine switch is USE_BLAS,
+ * tinylm.c:29-31). */
+int tl_set_gemm_engine(int engine);
+/* Engine the last GEMM call on this thread ran on (1 or 2), 0 if none. */
+int tl_last_gemm_engine(void);
+
+/* -------------------------------------------------------------- optimizer */
+/* norm = sqrt(sum_i (double)G[i]^2), rounded to float.  tinylm.c:1171-1176.
+ * `norm_out` may be a device or a host pointer; a host pointer makes the call
+ * synchronous (it waits for the result). */
+int tl_grad_norm(const float *G, size_t n, float *norm_out);
+/* sumsq_dev[0] = sum_i (double)G[i]^2 (device double) -- the per-shard half of
+ * global_gradnorm, for sharded (ZeRO-1) norms. */
+int tl_grad_sumsq(const float *G, size_t n, double *sumsq_dev);
+/* From a device sum of squares: norm = sqrt(sumsq), gscale = norm > max_norm ?
+ * max_norm / norm : 1 (tinylm.c:2631 with the clip of 1.0 made a parameter).
+ * Either output pointer may be NULL. */
+int tl_clip_scale(const double *sumsq_dev, float max_norm, float *norm_dev, float *gscale_dev);
+
+/* AdamW with clip scale folded in; G is not modified.  tinylm.c:1159-1170.
+ * bc1 = 1-b1^t, bc2 = 1-b2^t in fp32; eps = 1e-8 added to sqrt(vhat);
+ * decoupled weight decay wd*P on every parameter. */
+int tl_adamw_step(float *P, const float *G, float *M, float *V, size_t n,
+                  float lr, float b1, float b2, float wd, int t, float gscale);
+/* Same, with the clip scale read from device memory (NULL = 1.0): no host sync. */
+int tl_adamw_step_dev(float *P, const float *G, float *M, float *V, size_t n,
+                      float lr, float b1, float b2, float wd, int t,
+                      const float *gscale_dev);
+/* The whole optimizer step of train_loop (tinylm.c:2630-2633) on the device:
+ * norm -> clip scale (max_norm; the reference hard-codes 1.0) -> AdamW.
+ * norm_dev (device, may be NULL) receives the pre-clip norm. */
+int tl_clip_adamw_step(float *P, const float *G, float *M, float *V, size_t n,
+                       float lr, float b1, float b2, float wd, int t,
+                       float max_norm, float *norm_dev);
+
+/* ------------------------------------------- data parallel + ZeRO-1 (NCCL) */
+/* No counterpart in the reference (it has no distributed code); this is the
+ * multi-GPU form of the optimizer step above.
+ *
+ * Shard layout: the flat buffer of n floats is padded to n_pad, a multiple of
+ * world*4096 (TL_ZERO1_ALIGN); rank r owns [r*n_pad/world, (r+1)*n_pad/world).
+ * Buffers given to tl_zero1_step hold n_pad floats for P and G (the pad is kept
+ * zero) and n_pad/world floats for M and V (this rank's shard). */
+#define TL_ZERO1_ALIGN 4096
+size_t tl_zero1_padded(size_t n, int world);
+/* 128-byte NCCL unique id; rank 0 creates it and the caller ships it to the
+ * other ranks (e.g. over torch.distributed or a file). */
+int tl_dist_unique_id(void *uid128);
+/* Blocking communicator set-up for this process's current device. */
+int tl_dist_init(int rank, int world, const void *uid128);
+int tl_dist_finalize(void);
+/* One ZeRO-1 optimizer step over the padded flat buffers:
+ *   ReduceScatter(G, avg) -> shard sum of squares -> AllReduce(sum) -> clip ->
+ *   AdamW on this rank's shard of P/M/V -> AllGather(P).
+ * Averaging, not summing, because each rank's loss is its local mean
+ * (tinylm.c:1079 scales dlogits by 1/N_local).  G's own shard is overwritten
+ * with the averaged gradient; the rest of G is left as is. */
+int tl_zero1_step(float *P, float *G, float *M_shard, float *V_shard, size_t n,
+                  float lr, float b1, float b2, float wd, int t, float max_norm,
+                  float *norm_dev);
+/* Plain collectives on the library communicator (fp32, in place / out of place). */
+int tl_dist_allreduce_f32(float *buf, size_t count, int average);
+int tl_dist_allreduce_f64(double *buf, size_t count);
+/* Wait for the library stream with a host-side deadline (timeout_ms <= 0: the
+ * TL_DIST_TIMEOUT_MS environment value, default 120000).  A communicator error
+ * or an expired deadline aborts the communicator and returns TL_ENCCL /
+ * TL_ETIMEOUT instead of hanging. */
+int tl_dist_sync(int timeout_ms);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TINYLM_CUDA_H */

@@ -1,0 +1,91 @@
+"""Parity of the three GEMM primitives (CUDA, through the C ABI) against the
+reference's own outputs and a double-accumulated oracle.  Metric and bound:
+max|err| / mean|ref| <= 1e-4 (the reference selftest's metric, tinylm.c:4778)."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from helpers import GEMM_REL_TOL, gemm_rel
+from test_oracle import regen_gemm_inputs
+from tinylm_c_b200 import TLError, ops
+
+pytestmark = pytest.mark.gpu
+ENGINES = {"auto": 0, "cuda_core": 1}
+
+
+def dev(a, device):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(device)
+
+
+@pytest.fixture(params=list(ENGINES))
+def engine(request, cuda):
+    ops.set_gemm_engine(ENGINES[request.param])
+    yield request.param
+    ops.set_gemm_engine(0)
+
+
+@pytest.mark.parametrize("name", ["gemm_selftest", "gemm_accum", "gemm_aligned"])
+def test_gemms_match_reference_fixture(cuda, golden, engine, name):
+    z = golden(name)
+    M, K, N, X, W, dY, dX0, dW0 = regen_gemm_inputs(z)
+    tX, tW, tdY = dev(X, cuda), dev(W, cuda), dev(dY, cuda)
+    Y = torch.full((M * N,), float("nan"), device=cuda)
+    dX, dW = dev(dX0, cuda), dev(dW0, cuda)
+    ops.mm(Y, tX, tW, M, K, N)
+    ops.mm_bt(dX, tdY, tW, M, K, N)
+    ops.mm_atb(dW, tX, tdY, M, K, N)
+    torch.cuda.synchronize()
+    # truth: double accumulation
+    Y64 = np.empty(M * N, np.float32); oracle.mm(Y64, X, W, M, K, N, acc64=True)
+    dX64 = dX0.copy(); oracle.mm_bt(dX64, dY, W, M, K, N, acc64=True)
+    dW64 = dW0.copy(); oracle.mm_atb(dW64, X, dY, M, K, N, acc64=True)
+    for got, fix, truth in ((Y, z["Y"], Y64), (dX, z["dX"], dX64), (dW, z["dW"], dW64)):
+        g = got.cpu().numpy()
+        assert np.isfinite(g).all()
+        assert gemm_rel(g, fix) <= GEMM_REL_TOL
+        assert gemm_rel(g, truth) <= GEMM_REL_TOL
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 1, 1), (5, 3, 2), (128, 64, 96), (130, 68, 100), (1000, 36, 72),
+                                   (64, 2816, 32), (300, 256, 2048)])
+def test_gemm_shapes_vs_oracle(cuda, engine, M, K, N):
+    rng = np.random.default_rng(M * 31 + K * 7 + N)
+    X = rng.standard_normal(M * K, dtype=np.float32)
+    W = rng.standard_normal(K * N, dtype=np.float32) * np.float32(0.02)
+    dY = rng.standard_normal(M * N, dtype=np.float32)
+    dX0 = rng.standard_normal(M * K, dtype=np.float32)
+    dW0 = rng.standard_normal(K * N, dtype=np.float32)
+    Y = torch.empty(M * N, device=cuda)
+    dX, dW = dev(dX0, cuda), dev(dW0, cuda)
+    ops.mm(Y, dev(X, cuda), dev(W, cuda), M, K, N)
+    ops.mm_bt(dX, dev(dY, cuda), dev(W, cuda), M, K, N)
+    ops.mm_atb(dW, dev(X, cuda), dev(dY, cuda), M, K, N)
+    torch.cuda.synchronize()
+    Y64 = np.empty(M * N, np.float32); oracle.mm(Y64, X, W, M, K, N, acc64=True)
+    dX64 = dX0.copy(); oracle.mm_bt(dX64, dY, W, M, K, N, acc64=True)
+    dW64 = dW0.copy(); oracle.mm_atb(dW64, X, dY, M, K, N, acc64=True)
+    assert gemm_rel(Y.cpu().numpy(), Y64) <= GEMM_REL_TOL
+    assert gemm_rel(dX.cpu().numpy(), dX64) <= GEMM_REL_TOL
+    assert gemm_rel(dW.cpu().numpy(), dW64) <= GEMM_REL_TOL
+
+
+def test_gemm_empty_dims(cuda):
+    Y = torch.full((12,), 5.0, device=cuda)
+    z = torch.zeros(1, device=cuda)
+    ops.mm(Y, z, z, 3, 0, 4)            # empty reduction: mm overwrites with zeros
+    dX = torch.full((12,), 5.0, device=cuda)
+    ops.mm_bt(dX, z, z, 3, 4, 0)        # accumulate forms leave the output alone
+    ops.mm_atb(dX, z, z, 0, 3, 4)
+    ops.mm(z, z, z, 0, 4, 4)            # no rows: nothing to do
+    torch.cuda.synchronize()
+    assert torch.all(Y == 0) and torch.all(dX == 5)
+
+
+def test_gemm_rejects_host_memory(cuda):
+    Y = torch.zeros(4)
+    with pytest.raises(ValueError):
+        ops.mm(Y, Y, Y, 2, 2, 2)
+    with pytest.raises(TLError):
+        X = np.zeros(4, np.float32)
+        ops.mm(torch.zeros(4, device=cuda), X.ctypes.data, X.ctypes.data, 2, 2, 2)

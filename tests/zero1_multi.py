@@ -1,0 +1,64 @@
+"""Worker for the multi-GPU ZeRO-1 parity test (run by torchrun, one rank per
+GPU).  Each rank holds its own local gradient; after one tl_zero1_step every
+rank's full P must equal the single-rank oracle applied to the averaged
+gradient (the reference semantics of one big batch, tinylm.c:1079)."""
+import datetime
+import os
+import sys
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "tests"))
+import oracle  # noqa: E402
+from helpers import assert_adamw_close  # noqa: E402
+from tinylm_c_b200.zero1 import Zero1, zero1_layout  # noqa: E402
+
+LR, B1, B2, WD = 3e-4, 0.9, 0.95, 0.1
+
+
+def main():
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=60))
+    n = 3 * 4096 * world + 777                     # ragged: needs padding
+    p, _, m, v = oracle.adamw_inputs(n, seed=1)
+    grads = [oracle.adamw_inputs(n, seed=100 + r)[1] * np.float32(40.0) for r in range(world)]
+    gavg = (np.sum(np.stack(grads).astype(np.float64), axis=0) / world).astype(np.float32)
+    z = Zero1(n, rank, world, local)
+    n_pad, shard = zero1_layout(n, world)
+    lo = rank * shard
+    P = torch.zeros(n_pad, device=dev); P[:n] = torch.from_numpy(p)
+    G = torch.zeros(n_pad, device=dev); G[:n] = torch.from_numpy(grads[rank])
+    mp = np.zeros(n_pad, np.float32); mp[:n] = m
+    vp = np.zeros(n_pad, np.float32); vp[:n] = v
+    M = torch.from_numpy(mp[lo:lo + shard].copy()).to(dev)
+    V = torch.from_numpy(vp[lo:lo + shard].copy()).to(dev)
+    norm = torch.zeros(1, device=dev)
+    z.step(P, G, M, V, LR, B1, B2, WD, 2, 1.0, norm)
+    z.sync(60000)
+    gn = oracle.grad_norm(gavg)
+    assert abs(norm.item() - gn) <= 1e-6 * gn, (norm.item(), gn)
+    ref = [p.copy(), gavg.copy(), m.copy(), v.copy()]
+    oracle.adamw(*ref, LR, B1, B2, WD, 2, oracle.clip_scale(gn))
+    # averaging in fp32 across ranks may differ from the float64 mean by an ulp of g
+    Pg = P[:n].cpu().numpy()
+    err = np.abs(Pg.astype(np.float64) - ref[0])
+    assert err.max() <= 1e-6 * np.maximum(np.abs(ref[0]), np.abs(p)).max(), err.max()
+    hi = min(lo + shard, n)
+    if hi > lo:
+        assert_adamw_close(M[:hi - lo].cpu().numpy(), ref[2][lo:hi], m[lo:hi], "M shard")
+    z.close()
+    dist.barrier()
+    dist.destroy_process_group()
+    if rank == 0:
+        print("ZERO1_OK")
+
+
+if __name__ == "__main__":
+    main()

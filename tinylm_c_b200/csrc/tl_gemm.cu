@@ -1,0 +1,57 @@
+// tl_gemm.cu -- C-ABI entry points of the three GEMM primitives and engine choice.
+#include "tl_gemm.cuh"
+
+namespace tl {
+
+static thread_local int g_engine_pref = 0;   // 0 auto, 1 CUDA-core, 2 tensor-core
+static thread_local int g_engine_last = 0;
+
+static int gemm_entry(GemmOp op, float *C, const float *A, const float *B, int M, int K, int N,
+                      const char *names) {
+  TL_REQUIRE_CTX(c);
+  if (M < 0 || K < 0 || N < 0) return set_error(TL_EINVAL, "negative GEMM dimension (M=%d K=%d N=%d)", M, K, N);
+  int I, J, R;
+  gemm_dims(op, M, K, N, &I, &J, &R);
+  if (I == 0 || J == 0) return TL_OK;
+  int rc;
+  if ((rc = check_device_ptr(C, "output"))) return rc;
+  if (R > 0) {
+    if ((rc = check_device_ptr(A, "first operand"))) return rc;
+    if ((rc = check_device_ptr(B, "second operand"))) return rc;
+  }
+  (void)names;
+  if (R == 0) {  // empty reduction: mm writes zeros, the accumulating forms do nothing
+    g_engine_last = 1;
+    if (op == GemmOp::NN) TL_TRY_CUDA(cudaMemsetAsync(C, 0, sizeof(float) * (size_t)I * J, c->stream));
+    return TL_OK;
+  }
+  const bool tc_ok = gemm_tc_supported(op, C, A, B, M, K, N);
+  if (g_engine_pref == 2 && !tc_ok)
+    return set_error(TL_EINVAL, "tensor-core engine forced but shape/alignment unsupported (M=%d K=%d N=%d)", M, K, N);
+  if (tc_ok && g_engine_pref != 1) {
+    g_engine_last = 2;
+    return gemm_tc(c, op, C, A, B, M, K, N);
+  }
+  g_engine_last = 1;
+  return gemm_simt(c, op, C, A, B, M, K, N);
+}
+
+}  // namespace tl
+
+using namespace tl;
+
+TL_API int tl_matmul(float *Y, const float *X, const float *W, int M, int K, int N) {
+  return gemm_entry(GemmOp::NN, Y, X, W, M, K, N, "Y,X,W");
+}
+TL_API int tl_matmul_bt(float *dX, const float *dY, const float *W, int M, int K, int N) {
+  return gemm_entry(GemmOp::NT, dX, dY, W, M, K, N, "dX,dY,W");
+}
+TL_API int tl_matmul_at(float *dW, const float *X, const float *dY, int M, int K, int N) {
+  return gemm_entry(GemmOp::TN, dW, X, dY, M, K, N, "dW,X,dY");
+}
+TL_API int tl_set_gemm_engine(int engine) {
+  if (engine < 0 || engine > 2) return set_error(TL_EINVAL, "engine must be 0, 1 or 2");
+  g_engine_pref = engine;
+  return TL_OK;
+}
+TL_API int tl_last_gemm_engine(void) { return g_engine_last; }

@@ -1,0 +1,28 @@
+// tl_gemm.cuh -- shared declarations of the GEMM engines.
+#pragma once
+#include "tl_common.cuh"
+
+namespace tl {
+
+// The three reference primitives as one C[I,J] (=|+=) sum_r A(i,r) B(r,j).
+enum class GemmOp {
+  NN,  // mm     (tinylm.c:439-478):  Y[M,N]  = X[M,K]   @ W[K,N]
+  NT,  // mm_bt  (tinylm.c:480-508):  dX[M,K] += dY[M,N] @ W[K,N]^T
+  TN,  // mm_atb (tinylm.c:510-537):  dW[K,N] += X[M,K]^T @ dY[M,N]
+};
+
+inline void gemm_dims(GemmOp op, int M, int K, int N, int *I, int *J, int *R) {
+  switch (op) {
+    case GemmOp::NN: *I = M; *J = N; *R = K; break;
+    case GemmOp::NT: *I = M; *J = K; *R = N; break;
+    case GemmOp::TN: *I = K; *J = N; *R = M; break;
+  }
+}
+
+int gemm_simt(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, int M, int K, int N);
+// Returns TL_EINVAL (without launching) when the shape or alignment is not
+// supported by the tensor-core engine.
+bool gemm_tc_supported(GemmOp op, const float *C, const float *A, const float *B, int M, int K, int N);
+int gemm_tc(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, int M, int K, int N);
+
+}  // namespace tl

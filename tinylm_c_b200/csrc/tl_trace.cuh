@@ -1,0 +1,19 @@
+// tl_trace.cuh -- RAII bracket that times one kernel launch when tracing is on.
+#pragma once
+#include "tl_common.cuh"
+
+namespace tl {
+bool trace_on();
+class TraceScope {
+ public:
+  TraceScope(DeviceCtx *c, const char *name);
+  ~TraceScope();
+  TraceScope(const TraceScope &) = delete;
+  TraceScope &operator=(const TraceScope &) = delete;
+
+ private:
+  DeviceCtx *c_ = nullptr;
+  const char *name_ = nullptr;
+  cudaEvent_t a_ = nullptr;
+};
+}  // namespace tl
