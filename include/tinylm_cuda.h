@@ -54,8 +54,10 @@ extern "C" {
  * (norm partials).  Idempotent per device.  Replaces nothing in the reference
  * (its buffers are host callocs, fz() tinylm.c:137). */
 int tl_init(int device);
-/* Use `stream` (a cudaStream_t; NULL = the library's own) for all later calls
- * on the current device. */
+/* Use `stream` (a cudaStream_t) for all later calls on the current device.
+ * NULL selects the CUDA legacy default stream (the stream torch uses unless
+ * told otherwise).  Until the first call the library uses its own
+ * non-blocking stream, created by tl_init. */
 int tl_set_stream(void *stream);
 void *tl_get_stream(void);
 const char *tl_last_error(void);
@@ -66,6 +68,10 @@ int tl_memcpy_h2d(void *dst_dev, const void *src_host, size_t bytes);
 int tl_memcpy_d2h(void *dst_host, const void *src_dev, size_t bytes);
 int tl_memset(void *dst_dev, int value, size_t bytes);
 int tl_sync(void);
+/* Wait for the stream, then report (and clear) the device error word that
+ * bounded waits inside library kernels set when they give up: TL_ETIMEOUT if
+ * any kernel since the last call returned early, else TL_OK. */
+int tl_device_status(void);
 
 /* Kernel tracing: when on, every library kernel launch is bracketed by CUDA
  * events on its stream; tl_trace_get returns the summed device time (ms) and

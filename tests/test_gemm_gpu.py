@@ -8,10 +8,15 @@ import torch
 import oracle
 from helpers import GEMM_REL_TOL, gemm_rel
 from test_oracle import regen_gemm_inputs
-from tinylm_c_b200 import TLError, ops
+from tinylm_c_b200 import TLError, _lib, ops
 
 pytestmark = pytest.mark.gpu
 ENGINES = {"auto": 0, "cuda_core": 1}
+
+
+def device_ok():
+    """No bounded device-side wait expired in any kernel since the last check."""
+    _lib.check(_lib.lib().tl_device_status())
 
 
 def dev(a, device):
@@ -36,6 +41,7 @@ def test_gemms_match_reference_fixture(cuda, golden, engine, name):
     ops.mm_bt(dX, tdY, tW, M, K, N)
     ops.mm_atb(dW, tX, tdY, M, K, N)
     torch.cuda.synchronize()
+    device_ok()
     # truth: double accumulation
     Y64 = np.empty(M * N, np.float32); oracle.mm(Y64, X, W, M, K, N, acc64=True)
     dX64 = dX0.copy(); oracle.mm_bt(dX64, dY, W, M, K, N, acc64=True)
@@ -62,6 +68,7 @@ def test_gemm_shapes_vs_oracle(cuda, engine, M, K, N):
     ops.mm_bt(dX, dev(dY, cuda), dev(W, cuda), M, K, N)
     ops.mm_atb(dW, dev(X, cuda), dev(dY, cuda), M, K, N)
     torch.cuda.synchronize()
+    device_ok()
     Y64 = np.empty(M * N, np.float32); oracle.mm(Y64, X, W, M, K, N, acc64=True)
     dX64 = dX0.copy(); oracle.mm_bt(dX64, dY, W, M, K, N, acc64=True)
     dW64 = dW0.copy(); oracle.mm_atb(dW64, X, dY, M, K, N, acc64=True)
@@ -89,3 +96,72 @@ def test_gemm_rejects_host_memory(cuda):
     with pytest.raises(TLError):
         X = np.zeros(4, np.float32)
         ops.mm(torch.zeros(4, device=cuda), X.ctypes.data, X.ctypes.data, 2, 2, 2)
+
+
+@pytest.mark.parametrize("M,K,N", [(128, 32, 128), (256, 64, 256), (130, 68, 100), (1000, 36, 72), (257, 1024, 2816)])
+def test_tensor_core_engine_forced(cuda, M, K, N):
+    """The tcgen05 3xTF32 engine alone (engine 2) on aligned shapes, including
+    partial tiles in every dimension."""
+    ops.set_gemm_engine(2)
+    try:
+        rng = np.random.default_rng(M + K + N)
+        X = rng.standard_normal(M * K, dtype=np.float32)
+        W = rng.standard_normal(K * N, dtype=np.float32) * np.float32(0.02)
+        dY = rng.standard_normal(M * N, dtype=np.float32)
+        dX0 = rng.standard_normal(M * K, dtype=np.float32)
+        dW0 = rng.standard_normal(K * N, dtype=np.float32)
+        Y = torch.full((M * N,), float("nan"), device=cuda)
+        dX, dW = dev(dX0, cuda), dev(dW0, cuda)
+        ops.mm(Y, dev(X, cuda), dev(W, cuda), M, K, N)
+        assert ops.last_gemm_engine() == 2
+        ops.mm_bt(dX, dev(dY, cuda), dev(W, cuda), M, K, N)
+        assert ops.last_gemm_engine() == 2
+        ops.mm_atb(dW, dev(X, cuda), dev(dY, cuda), M, K, N)
+        assert ops.last_gemm_engine() == 2
+        torch.cuda.synchronize()
+        device_ok()
+    finally:
+        ops.set_gemm_engine(0)
+    Xd, Wd, dYd = (a.astype(np.float64) for a in (X, W, dY))
+    Y64 = (Xd.reshape(M, K) @ Wd.reshape(K, N)).ravel()
+    dX64 = dX0 + (dYd.reshape(M, N) @ Wd.reshape(K, N).T).ravel()
+    dW64 = dW0 + (Xd.reshape(M, K).T @ dYd.reshape(M, N)).ravel()
+    assert gemm_rel(Y.cpu().numpy(), Y64) <= GEMM_REL_TOL
+    assert gemm_rel(dX.cpu().numpy(), dX64) <= GEMM_REL_TOL
+    assert gemm_rel(dW.cpu().numpy(), dW64) <= GEMM_REL_TOL
+
+
+def test_tensor_core_engine_rejects_unaligned(cuda):
+    ops.set_gemm_engine(2)
+    try:
+        z = torch.zeros(201 * 259, device=cuda)
+        with pytest.raises(TLError):
+            ops.mm(z, z, z, 201, 131, 259)      # K=131: rows not 16-byte multiples
+    finally:
+        ops.set_gemm_engine(0)
+
+
+@pytest.mark.parametrize("M,K,N", [(16384, 1024, 1024), (16384, 256, 2816), (65536, 512, 256)])
+def test_gemm_sweep_shapes_sampled(cuda, M, K, N):
+    """BASELINE config-3 shapes at full size, checked on sampled rows/columns
+    against float64 (rows of Y and dX, columns of dW, are independent)."""
+    rng = np.random.default_rng(3)
+    X = torch.randn(M * K, device=cuda, generator=torch.Generator(device=cuda).manual_seed(1))
+    W = torch.randn(K * N, device=cuda, generator=torch.Generator(device=cuda).manual_seed(2)) * 0.02
+    dY = torch.randn(M * N, device=cuda, generator=torch.Generator(device=cuda).manual_seed(3))
+    Y = torch.empty(M * N, device=cuda)
+    dX = torch.zeros(M * K, device=cuda)
+    dW = torch.zeros(K * N, device=cuda)
+    ops.mm(Y, X, W, M, K, N)
+    ops.mm_bt(dX, dY, W, M, K, N)
+    ops.mm_atb(dW, X, dY, M, K, N)
+    torch.cuda.synchronize()
+    device_ok()
+    rows = np.sort(rng.choice(M, 64, replace=False))
+    cols = np.sort(rng.choice(N, 16, replace=False))
+    Xh = X.view(M, K).double().cpu().numpy()
+    Wh = W.view(K, N).double().cpu().numpy()
+    dYh = dY.view(M, N).double().cpu().numpy()
+    assert gemm_rel(Y.view(M, N)[rows].cpu().numpy(), Xh[rows] @ Wh) <= GEMM_REL_TOL
+    assert gemm_rel(dX.view(M, K)[rows].cpu().numpy(), dYh[rows] @ Wh.T) <= GEMM_REL_TOL
+    assert gemm_rel(dW.view(K, N)[:, cols].cpu().numpy(), Xh.T @ dYh[:, cols]) <= GEMM_REL_TOL

@@ -26,6 +26,7 @@ struct DeviceCtx {
   unsigned int *norm_ticket = nullptr; // last-block-done counter
   double *sumsq = nullptr;             // [1] scratch for tl_grad_norm
   float *scalars = nullptr;            // [4] scratch: norm, gscale
+  int *err_flag = nullptr;             // device error word set by bounded waits
 };
 
 DeviceCtx *ctx();                          // context of the current device, or null

@@ -1,10 +1,420 @@
-// tl_gemm_tc.cu -- tensor-core (tcgen05, 3xTF32) GEMM engine.  Placeholder
-// until the engine lands: reports every shape as unsupported.
+// tl_gemm_tc.cu -- tensor-core GEMM engine: tcgen05 (kind::tf32) with 3xTF32
+// split accumulation, TMA-staged tiles, accumulator in TMEM (sm_100a).
+//
+// The three reference primitives (tinylm.c:439-537) in one kernel family:
+//   C[I,J] (=|+=) sum_r A(i,r) B(r,j)
+// with A K-major (reduction contiguous: mm, mm_bt) or MN-major (mm_atb), and B
+// MN-major (mm, mm_atb) or K-major (mm_bt).  tcgen05 reads both majors for tf32,
+// so no operand is transposed in memory.
+//
+// 3xTF32: every fp32 operand x is split into hi = tf32(x) (round to nearest)
+// and lo = x - hi (exact in fp32), and the tile product is accumulated as
+// lo*hi + hi*lo + hi*hi in fp32 in TMEM.  The dropped lo*lo term and the tf32
+// rounding of lo leave a relative error near 2^-21 per product, i.e. fp32-level
+// results from the tf32 tensor pipe.
+//
+// CTA roles (192 threads):
+//   warp 0      TMA producer: raw fp32 tiles of A and B -> shared memory stage
+//   warp 1      TMEM owner and MMA issuer (one elected thread)
+//   warps 2..5  split warpgroup: hi written in place over the raw tile, lo into
+//               its own buffer; afterwards the epilogue (TMEM -> registers ->
+//               global, beta = 0 or 1)
+// Pipeline per stage: full (TMA bytes landed) -> ready (hi/lo written) ->
+// empty (MMAs that read the stage finished, via tcgen05.commit).
+//
+// Every mbarrier wait is bounded: on expiry the thread records an error code
+// in the context's device error word, raises a CTA-wide abort flag and the CTA
+// winds down (the MMA thread still waits, bounded, for its own MMAs; TMEM is
+// always released).
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include "tl_gemm.cuh"
+#include "tl_trace.cuh"
 
 namespace tl {
-bool gemm_tc_supported(GemmOp, const float *, const float *, const float *, int, int, int) { return false; }
-int gemm_tc(DeviceCtx *, GemmOp, float *, const float *, const float *, int, int, int) {
-  return set_error(TL_EINVAL, "tensor-core engine not built");
+namespace tc {
+
+constexpr int BM = 128, BN = 128, BK = 32, STAGES = 3;
+constexpr int TILE_A = BM * BK * 4;                  // 16 KB
+constexpr int TILE_B = BN * BK * 4;                  // 16 KB
+constexpr int OFF_AHI = 0, OFF_ALO = TILE_A, OFF_BHI = 2 * TILE_A, OFF_BLO = 2 * TILE_A + TILE_B;
+constexpr int STAGE_BYTES = 2 * (TILE_A + TILE_B);   // 64 KB
+constexpr int TX_BYTES = TILE_A + TILE_B;            // raw bytes TMA lands per stage
+constexpr int NUM_THREADS = 192;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
+constexpr int TMEM_COLS = BN;                        // fp32 accumulator 128 lanes x BN columns
+constexpr long long WAIT_LIMIT_CYCLES = 4000000000LL;  // ~2 s at 1.9 GHz
+
+// --------------------------------------------------------------- PTX helpers
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("{ .reg .b64 st; mbarrier.arrive.shared::cta.b64 st, [%0]; }" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("{ .reg .b64 st; mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1; }" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait.  Returns false (and raises the abort flag) on expiry or when
+// another thread of the CTA has already aborted.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort_flag,
+                                          int *err, int code) {
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (*abort_flag) return false;
+    if (clock64() - t0 > WAIT_LIMIT_CYCLES) {
+      *abort_flag = 1;
+      atomicExch(err, code);
+      return false;
+    }
+  }
+  return true;
+}
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, uint32_t bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{ .reg .pred p; setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p; }" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+// Shared-memory matrix descriptor, 128-byte swizzle (sm_100 layout: version 1
+// at bits 46-47, swizzle mode 2 at bits 61-63).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+// Instruction descriptor: D f32, A/B tf32, M=128, N=BN, majors as given.
+__host__ __device__ constexpr uint32_t make_idesc(bool a_mn, bool b_mn) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) |
+         ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+__device__ __forceinline__ float tf32_hi(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+struct Params {
+  float *C;
+  int I, J, R, ldc, beta;
+  int *err;
+};
+
+template <bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
+  // bars[0..S): full, [S..2S): ready, [2S..3S): empty, [3S]: acc_full
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * STAGES + 1);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int i0 = blockIdx.y * BM, j0 = blockIdx.x * BN;
+  const int nk = (p.R + BK - 1) / BK;
+  const uint32_t smem_base = smem_u32(smem);
+  auto bar_full = [&](int s) { return smem_u32(&bars[s]); };
+  auto bar_ready = [&](int s) { return smem_u32(&bars[STAGES + s]); };
+  auto bar_empty = [&](int s) { return smem_u32(&bars[2 * STAGES + s]); };
+  const uint32_t bar_acc = smem_u32(&bars[3 * STAGES]);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; s++) {
+      mbar_init(bar_full(s), 1);
+      mbar_init(bar_ready(s), 4);
+      mbar_init(bar_empty(s), 1);
+    }
+    mbar_init(bar_acc, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int issued = 0;
+      for (int kb = 0; kb < nk; kb++) {
+        const int s = kb % STAGES, u = kb / STAGES;
+        if (u > 0 && !mbar_wait(bar_empty(s), (u - 1) & 1, abort_flag, p.err, 1)) break;
+        issued = kb + 1;
+        const uint32_t st = smem_base + s * STAGE_BYTES;
+        mbar_arrive_expect_tx(bar_full(s), TX_BYTES);
+        const int k0 = kb * BK;
+        if (A_MN) {
+#pragma unroll
+          for (int b = 0; b < BM / 32; b++) tma_load_2d(st + OFF_AHI + b * 4096, &tmA, bar_full(s), i0 + 32 * b, k0);
+        } else {
+          tma_load_2d(st + OFF_AHI, &tmA, bar_full(s), k0, i0);
+        }
+        if (B_MN) {
+#pragma unroll
+          for (int b = 0; b < BN / 32; b++) tma_load_2d(st + OFF_BHI + b * 4096, &tmB, bar_full(s), j0 + 32 * b, k0);
+        } else {
+          tma_load_2d(st + OFF_BHI, &tmB, bar_full(s), k0, j0);
+        }
+      }
+      // No copy may still be landing when the CTA exits: wait (bounded) for
+      // the last load issued into each stage.  On the normal path these have
+      // all been consumed already and the waits return at once.
+      for (int kb = issued > STAGES ? issued - STAGES : 0; kb < issued; kb++) {
+        const long long t0 = clock64();
+        while (!mbar_try_wait(bar_full(kb % STAGES), (kb / STAGES) & 1)) {
+          if (clock64() - t0 > WAIT_LIMIT_CYCLES) { atomicExch(p.err, 6); break; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc(A_MN, B_MN);
+      uint32_t acc = 0;
+      for (int kb = 0; kb < nk; kb++) {
+        const int s = kb % STAGES, u = kb / STAGES;
+        if (!mbar_wait(bar_ready(s), u & 1, abort_flag, p.err, 2)) break;
+        tc_fence_after();
+        const uint32_t st = smem_base + s * STAGE_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < BK / 8; kk++) {
+          // K-major: advance 32 bytes inside the swizzle atom; MN-major: one
+          // 8-row group (1 KB) per tf32 MMA-K step.  MN-major atoms along M/N
+          // sit 4 KB apart (one TMA box of 32 x 32 floats).
+          const uint32_t a_off = A_MN ? kk * 1024 : kk * 32;
+          const uint32_t b_off = B_MN ? kk * 1024 : kk * 32;
+          const uint32_t a_lbo = A_MN ? 4096 : 16, b_lbo = B_MN ? 4096 : 16;
+          const uint64_t a_hi = smem_desc(st + OFF_AHI + a_off, a_lbo, 1024);
+          const uint64_t a_lo = smem_desc(st + OFF_ALO + a_off, a_lbo, 1024);
+          const uint64_t b_hi = smem_desc(st + OFF_BHI + b_off, b_lbo, 1024);
+          const uint64_t b_lo = smem_desc(st + OFF_BLO + b_off, b_lbo, 1024);
+          tc_mma(tmem, a_lo, b_hi, idesc, acc);
+          tc_mma(tmem, a_hi, b_lo, idesc, 1);
+          tc_mma(tmem, a_hi, b_hi, idesc, 1);
+          acc = 1;
+        }
+        tc_commit(bar_empty(s));
+      }
+      // Always commit and wait for this thread's own MMAs, so TMEM is idle
+      // before it is released (also on the abort path).
+      tc_commit(bar_acc);
+      const long long t0 = clock64();
+      while (!mbar_try_wait(bar_acc, 0)) {
+        if (clock64() - t0 > WAIT_LIMIT_CYCLES) {
+          *abort_flag = 1;
+          atomicExch(p.err, 3);
+          break;
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------ split warpgroup + epilogue
+    const int t = threadIdx.x - 64;  // 0..127
+    bool ok = true;
+    for (int kb = 0; kb < nk && ok; kb++) {
+      const int s = kb % STAGES, u = kb / STAGES;
+      if (!mbar_wait(bar_full(s), u & 1, abort_flag, p.err, 4)) { ok = false; break; }
+      uint8_t *st = smem + s * STAGE_BYTES;
+      // A tile then B tile: 2 x 1024 float4 of raw data, 16 per thread.
+#pragma unroll 4
+      for (int e = 0; e < 16; e++) {
+        const int idx = e * 128 + t;                    // 0..2047
+        const int off = idx < 1024 ? OFF_AHI + idx * 16 : OFF_BHI + (idx - 1024) * 16;
+        float4 *src = reinterpret_cast<float4 *>(st + off);
+        float4 *dlo = reinterpret_cast<float4 *>(st + off + (idx < 1024 ? TILE_A : TILE_B));
+        float4 x = *src, hi, lo;
+        hi.x = tf32_hi(x.x); hi.y = tf32_hi(x.y); hi.z = tf32_hi(x.z); hi.w = tf32_hi(x.w);
+        lo.x = x.x - hi.x; lo.y = x.y - hi.y; lo.z = x.z - hi.z; lo.w = x.w - hi.w;
+        *src = hi;
+        *dlo = lo;
+      }
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_ready(s));
+    }
+    // epilogue
+    if (ok && mbar_wait(bar_acc, 0, abort_flag, p.err, 5)) {
+      tc_fence_after();
+      const int q = warp & 3;
+      const int row = i0 + q * 32 + lane;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; c++) {
+        uint32_t v[32];
+        const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + c * 32;
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+            "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+            : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+              "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]),
+              "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]),
+              "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]),
+              "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+            : "r"(taddr));
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        if (row < p.I) {
+          const int col0 = j0 + c * 32;
+          float *dst = p.C + (size_t)row * p.ldc + col0;
+          if (col0 + 32 <= p.J) {
+#pragma unroll
+            for (int e = 0; e < 32; e += 4) {
+              float4 o = make_float4(__uint_as_float(v[e]), __uint_as_float(v[e + 1]), __uint_as_float(v[e + 2]),
+                                     __uint_as_float(v[e + 3]));
+              float4 *d4 = reinterpret_cast<float4 *>(dst + e);
+              if (p.beta) {
+                const float4 old = *d4;
+                o.x += old.x; o.y += old.y; o.z += old.z; o.w += old.w;
+              }
+              *d4 = o;
+            }
+          } else {
+#pragma unroll
+            for (int e = 0; e < 32; e++) {
+              if (col0 + e < p.J) {
+                const float o = __uint_as_float(v[e]);
+                dst[e] = p.beta ? dst[e] + o : o;
+              }
+            }
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+  }
+}
+
+// ------------------------------------------------------------------- host
+static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+static int get_encoder() {
+  if (g_encode) return TL_OK;
+  void *fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+  if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn)
+    return set_error(TL_ECUDA, "cuTensorMapEncodeTiled not available from the driver");
+  g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  return TL_OK;
+}
+
+// 2D fp32 map over a row-major [outer][inner] array with row stride `ld` floats.
+static int make_map(CUtensorMap *m, const float *ptr, uint64_t inner, uint64_t outer, uint64_t ld, uint32_t box_inner,
+                    uint32_t box_outer) {
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {ld * 4};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(ptr), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(TL_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return TL_OK;
+}
+
+template <bool A_MN, bool B_MN>
+static int launch(DeviceCtx *c, const CUtensorMap &ma, const CUtensorMap &mb, const Params &p) {
+  static bool attr_set[kMaxDevices] = {};
+  if (!attr_set[c->device]) {
+    TL_TRY_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<A_MN, B_MN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     SMEM_BYTES));
+    attr_set[c->device] = true;
+  }
+  dim3 grid((p.J + BN - 1) / BN, (p.I + BM - 1) / BM);
+  TraceScope ts(c, "gemm_tc");
+  gemm_tc_kernel<A_MN, B_MN><<<grid, NUM_THREADS, SMEM_BYTES, c->stream>>>(ma, mb, p);
+  TL_TRY_CUDA(cudaGetLastError());
+  return TL_OK;
+}
+
+}  // namespace tc
+
+bool gemm_tc_supported(GemmOp op, const float *C, const float *A, const float *B, int M, int K, int N) {
+  (void)op;
+  const uintptr_t al = reinterpret_cast<uintptr_t>(C) | reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B);
+  if (al & 15) return false;             // TMA needs 16-byte aligned bases
+  if ((K & 3) || (N & 3)) return false;  // and row strides that are multiples of 16 bytes
+  if (M < 1 || K < 1 || N < 1) return false;
+  int I, J, R;
+  gemm_dims(op, M, K, N, &I, &J, &R);
+  if ((I + tc::BM - 1) / tc::BM > 65535) return false;
+  return true;
+}
+
+int gemm_tc(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, int M, int K, int N) {
+  int rc;
+  if ((rc = tc::get_encoder())) return rc;
+  int I, J, R;
+  gemm_dims(op, M, K, N, &I, &J, &R);
+  tc::Params p;
+  p.C = C; p.I = I; p.J = J; p.R = R; p.err = c->err_flag;
+  CUtensorMap ma, mb;
+  switch (op) {
+    case GemmOp::NN:  // A = X[M,K] K-major; B = W[K,N] MN-major
+      p.ldc = N; p.beta = 0;
+      if ((rc = tc::make_map(&ma, A, K, M, K, 32, tc::BM))) return rc;
+      if ((rc = tc::make_map(&mb, B, N, K, N, 32, 32))) return rc;
+      return tc::launch<false, true>(c, ma, mb, p);
+    case GemmOp::NT:  // A = dY[M,N] K-major; B(r=n, j=k) = W[k*N+n] K-major
+      p.ldc = K; p.beta = 1;
+      if ((rc = tc::make_map(&ma, A, N, M, N, 32, tc::BM))) return rc;
+      if ((rc = tc::make_map(&mb, B, N, K, N, 32, tc::BN))) return rc;
+      return tc::launch<false, false>(c, ma, mb, p);
+    case GemmOp::TN:  // A(i=k, r=m) = X[m*K+k] MN-major; B = dY[M,N] MN-major
+      p.ldc = N; p.beta = 1;
+      if ((rc = tc::make_map(&ma, A, K, M, K, 32, 32))) return rc;
+      if ((rc = tc::make_map(&mb, B, N, M, N, 32, 32))) return rc;
+      return tc::launch<true, true>(c, ma, mb, p);
+  }
+  return set_error(TL_EINVAL, "unknown GEMM op");
+}
+
 }  // namespace tl

@@ -70,6 +70,8 @@ TL_API int tl_init(int device) {
   TL_TRY_CUDA(cudaMemset(c.norm_ticket, 0, sizeof(unsigned int)));
   TL_TRY_CUDA(cudaMalloc(&c.sumsq, sizeof(double) * 2));
   TL_TRY_CUDA(cudaMalloc(&c.scalars, sizeof(float) * 4));
+  TL_TRY_CUDA(cudaMalloc(&c.err_flag, sizeof(int)));
+  TL_TRY_CUDA(cudaMemset(c.err_flag, 0, sizeof(int)));
   TL_TRY_CUDA(cudaDeviceSynchronize());
   c.ready = true;
   return TL_OK;
@@ -77,7 +79,7 @@ TL_API int tl_init(int device) {
 
 TL_API int tl_set_stream(void *stream) {
   TL_REQUIRE_CTX(c);
-  c->stream = stream ? (cudaStream_t)stream : c->own_stream;
+  c->stream = (cudaStream_t)stream;  // NULL is the CUDA legacy default stream
   return TL_OK;
 }
 
@@ -123,5 +125,17 @@ TL_API int tl_memset(void *dst, int value, size_t bytes) {
 TL_API int tl_sync(void) {
   TL_REQUIRE_CTX(c);
   TL_TRY_CUDA(cudaStreamSynchronize(c->stream));
+  return TL_OK;
+}
+
+TL_API int tl_device_status(void) {
+  TL_REQUIRE_CTX(c);
+  TL_TRY_CUDA(cudaStreamSynchronize(c->stream));
+  int code = 0;
+  TL_TRY_CUDA(cudaMemcpy(&code, c->err_flag, sizeof(int), cudaMemcpyDeviceToHost));
+  if (code) {
+    TL_TRY_CUDA(cudaMemset(c->err_flag, 0, sizeof(int)));
+    return set_error(TL_ETIMEOUT, "a bounded device-side wait expired (site %d); the kernel returned early", code);
+  }
   return TL_OK;
 }
