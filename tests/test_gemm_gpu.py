@@ -79,7 +79,7 @@ def test_gemm_shapes_vs_oracle(cuda, engine, M, K, N):
 
 def test_gemm_empty_dims(cuda):
     Y = torch.full((12,), 5.0, device=cuda)
-    z = torch.zeros(1, device=cuda)
+    z = torch.zeros(16, device=cuda)
     ops.mm(Y, z, z, 3, 0, 4)            # empty reduction: mm overwrites with zeros
     dX = torch.full((12,), 5.0, device=cuda)
     ops.mm_bt(dX, z, z, 3, 4, 0)        # accumulate forms leave the output alone

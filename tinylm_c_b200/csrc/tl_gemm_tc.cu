@@ -13,14 +13,17 @@
 // rounding of lo leave a relative error near 2^-21 per product, i.e. fp32-level
 // results from the tf32 tensor pipe.
 //
-// CTA roles (192 threads):
+// CTA roles (320 threads):
 //   warp 0      TMA producer: raw fp32 tiles of A and B -> shared memory stage
 //   warp 1      TMEM owner and MMA issuer (one elected thread)
 //   warps 2..5  split warpgroup: hi written in place over the raw tile, lo into
-//               its own buffer; afterwards the epilogue (TMEM -> registers ->
-//               global, beta = 0 or 1)
+//               its own buffer
+//   warps 6..9  accumulator warpgroup: every CHUNK_KB k-blocks the TMEM
+//               accumulator (double buffered) is added into fp32 registers;
+//               finally the epilogue (registers -> global, beta = 0 or 1)
 // Pipeline per stage: full (TMA bytes landed) -> ready (hi/lo written) ->
-// empty (MMAs that read the stage finished, via tcgen05.commit).
+// empty (MMAs that read the stage finished, via tcgen05.commit); per TMEM
+// buffer: accf (chunk finished) -> acce (chunk drained).
 //
 // Every mbarrier wait is bounded: on expiry the thread records an error code
 // in the context's device error word, raises a CTA-wide abort flag and the CTA
@@ -40,9 +43,10 @@ constexpr int TILE_B = BN * BK * 4;                  // 16 KB
 constexpr int OFF_AHI = 0, OFF_ALO = TILE_A, OFF_BHI = 2 * TILE_A, OFF_BLO = 2 * TILE_A + TILE_B;
 constexpr int STAGE_BYTES = 2 * (TILE_A + TILE_B);   // 64 KB
 constexpr int TX_BYTES = TILE_A + TILE_B;            // raw bytes TMA lands per stage
-constexpr int NUM_THREADS = 192;
+constexpr int NUM_THREADS = 320;
+constexpr int CHUNK_KB = 4;                          // k-blocks per TMEM chunk (K = 128)
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
-constexpr int TMEM_COLS = BN;                        // fp32 accumulator 128 lanes x BN columns
+constexpr int TMEM_COLS = 2 * BN;                    // two fp32 accumulators, 128 lanes x BN columns
 constexpr long long WAIT_LIMIT_CYCLES = 4000000000LL;  // ~2 s at 1.9 GHz
 
 // --------------------------------------------------------------- PTX helpers
@@ -107,15 +111,23 @@ __device__ __forceinline__ void tc_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
 
-// Shared-memory matrix descriptor, 128-byte swizzle (sm_100 layout: version 1
-// at bits 46-47, swizzle mode 2 at bits 61-63).
-__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+// Shared-memory matrix descriptor (sm_100 layout: version 1 at bits 46-47,
+// layout type at bits 61-63).  Two layouts are used:
+//  K-major operands:  128-byte swizzle (type 2), 16-byte chunks XOR row%8;
+//                     8-row groups 1 KB apart (SBO), LBO unused.
+//  MN-major operands: 128-byte swizzle on a 32-byte base (type 1), 32-byte
+//                     chunks XOR row%4 -- the only MN-major layout tcgen05
+//                     accepts for tf32; 4-row K groups 512 B apart (SBO),
+//                     32-element MN chunks 4 KB apart (LBO).
+constexpr uint32_t LAYOUT_SW128 = 2, LAYOUT_SW128_BASE32B = 1;
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo_bytes, uint32_t sbo_bytes,
+                                              uint32_t layout) {
   uint64_t d = 0;
   d |= (uint64_t)((addr >> 4) & 0x3FFF);
   d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16;
   d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFF) << 32;
   d |= (uint64_t)1 << 46;
-  d |= (uint64_t)2 << 61;
+  d |= (uint64_t)layout << 61;
   return d;
 }
 
@@ -143,18 +155,21 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
-  // bars[0..S): full, [S..2S): ready, [2S..3S): empty, [3S]: acc_full
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * STAGES + 1);
+  // bars: full[S], ready[S], empty[S], accf[2] (chunk in TMEM buffer b is
+  // complete), acce[2] (TMEM buffer b drained into registers)
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * STAGES + 4);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int i0 = blockIdx.y * BM, j0 = blockIdx.x * BN;
   const int nk = (p.R + BK - 1) / BK;
+  const int nchunks = (nk + CHUNK_KB - 1) / CHUNK_KB;
   const uint32_t smem_base = smem_u32(smem);
   auto bar_full = [&](int s) { return smem_u32(&bars[s]); };
   auto bar_ready = [&](int s) { return smem_u32(&bars[STAGES + s]); };
   auto bar_empty = [&](int s) { return smem_u32(&bars[2 * STAGES + s]); };
-  const uint32_t bar_acc = smem_u32(&bars[3 * STAGES]);
+  auto bar_accf = [&](int b) { return smem_u32(&bars[3 * STAGES + b]); };
+  auto bar_acce = [&](int b) { return smem_u32(&bars[3 * STAGES + 2 + b]); };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; s++) {
@@ -162,7 +177,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       mbar_init(bar_ready(s), 4);
       mbar_init(bar_empty(s), 1);
     }
-    mbar_init(bar_acc, 1);
+    for (int b = 0; b < 2; b++) {
+      mbar_init(bar_accf(b), 1);
+      mbar_init(bar_acce(b), 4);
+    }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -215,50 +233,62 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     // ---------------------------------------------------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = make_idesc(A_MN, B_MN);
-      uint32_t acc = 0;
-      for (int kb = 0; kb < nk; kb++) {
+      int chunk = 0, kin = 0, last_committed = -1;
+      bool ok = true;
+      for (int kb = 0; kb < nk && ok; kb++) {
         const int s = kb % STAGES, u = kb / STAGES;
+        const int b = chunk & 1;
+        // A TMEM buffer is reused two chunks later, once it has been drained.
+        if (kin == 0 && chunk >= 2 && !mbar_wait(bar_acce(b), ((chunk >> 1) - 1) & 1, abort_flag, p.err, 7)) break;
         if (!mbar_wait(bar_ready(s), u & 1, abort_flag, p.err, 2)) break;
         tc_fence_after();
         const uint32_t st = smem_base + s * STAGE_BYTES;
+        const uint32_t d = tmem + b * BN;
 #pragma unroll
         for (int kk = 0; kk < BK / 8; kk++) {
-          // K-major: advance 32 bytes inside the swizzle atom; MN-major: one
-          // 8-row group (1 KB) per tf32 MMA-K step.  MN-major atoms along M/N
-          // sit 4 KB apart (one TMA box of 32 x 32 floats).
+          // K-major: advance 32 bytes inside the swizzle atom; MN-major: eight
+          // K rows (1 KB) per tf32 MMA-K step.  MN-major atoms along M/N sit
+          // 4 KB apart (one TMA box of 32 x 32 floats).
           const uint32_t a_off = A_MN ? kk * 1024 : kk * 32;
           const uint32_t b_off = B_MN ? kk * 1024 : kk * 32;
-          const uint32_t a_lbo = A_MN ? 4096 : 16, b_lbo = B_MN ? 4096 : 16;
-          const uint64_t a_hi = smem_desc(st + OFF_AHI + a_off, a_lbo, 1024);
-          const uint64_t a_lo = smem_desc(st + OFF_ALO + a_off, a_lbo, 1024);
-          const uint64_t b_hi = smem_desc(st + OFF_BHI + b_off, b_lbo, 1024);
-          const uint64_t b_lo = smem_desc(st + OFF_BLO + b_off, b_lbo, 1024);
-          tc_mma(tmem, a_lo, b_hi, idesc, acc);
-          tc_mma(tmem, a_hi, b_lo, idesc, 1);
-          tc_mma(tmem, a_hi, b_hi, idesc, 1);
-          acc = 1;
+          constexpr uint32_t a_lbo = A_MN ? 4096 : 16, b_lbo = B_MN ? 4096 : 16;
+          constexpr uint32_t a_sbo = A_MN ? 512 : 1024, b_sbo = B_MN ? 512 : 1024;
+          constexpr uint32_t a_lay = A_MN ? LAYOUT_SW128_BASE32B : LAYOUT_SW128;
+          constexpr uint32_t b_lay = B_MN ? LAYOUT_SW128_BASE32B : LAYOUT_SW128;
+          const uint64_t a_hi = smem_desc(st + OFF_AHI + a_off, a_lbo, a_sbo, a_lay);
+          const uint64_t a_lo = smem_desc(st + OFF_ALO + a_off, a_lbo, a_sbo, a_lay);
+          const uint64_t b_hi = smem_desc(st + OFF_BHI + b_off, b_lbo, b_sbo, b_lay);
+          const uint64_t b_lo = smem_desc(st + OFF_BLO + b_off, b_lbo, b_sbo, b_lay);
+          tc_mma(d, a_lo, b_hi, idesc, (kin > 0 || kk > 0) ? 1u : 0u);
+          tc_mma(d, a_hi, b_lo, idesc, 1);
+          tc_mma(d, a_hi, b_hi, idesc, 1);
         }
         tc_commit(bar_empty(s));
-      }
-      // Always commit and wait for this thread's own MMAs, so TMEM is idle
-      // before it is released (also on the abort path).
-      tc_commit(bar_acc);
-      const long long t0 = clock64();
-      while (!mbar_try_wait(bar_acc, 0)) {
-        if (clock64() - t0 > WAIT_LIMIT_CYCLES) {
-          *abort_flag = 1;
-          atomicExch(p.err, 3);
-          break;
+        if (++kin == CHUNK_KB || kb == nk - 1) {
+          tc_commit(bar_accf(b));
+          last_committed = chunk;
+          chunk++;
+          kin = 0;
         }
       }
+      // Always leave with this thread's MMAs finished, so TMEM is idle before
+      // it is released (also on the abort path).
+      if (kin > 0 || last_committed < chunk - 1 || last_committed < 0) {
+        tc_commit(bar_accf(chunk & 1));
+        last_committed = chunk;
+      }
+      const int b = last_committed & 1;
+      const long long t0 = clock64();
+      while (!mbar_try_wait(bar_accf(b), (last_committed >> 1) & 1)) {
+        if (clock64() - t0 > WAIT_LIMIT_CYCLES) { *abort_flag = 1; atomicExch(p.err, 3); break; }
+      }
     }
-  } else {
-    // ------------------------------------------ split warpgroup + epilogue
+  } else if (warp < 6) {
+    // ---------------------------------------------------- split warpgroup
     const int t = threadIdx.x - 64;  // 0..127
-    bool ok = true;
-    for (int kb = 0; kb < nk && ok; kb++) {
+    for (int kb = 0; kb < nk; kb++) {
       const int s = kb % STAGES, u = kb / STAGES;
-      if (!mbar_wait(bar_full(s), u & 1, abort_flag, p.err, 4)) { ok = false; break; }
+      if (!mbar_wait(bar_full(s), u & 1, abort_flag, p.err, 4)) break;
       uint8_t *st = smem + s * STAGE_BYTES;
       // A tile then B tile: 2 x 1024 float4 of raw data, 16 per thread.
 #pragma unroll 4
@@ -277,15 +307,25 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_ready(s));
     }
-    // epilogue
-    if (ok && mbar_wait(bar_acc, 0, abort_flag, p.err, 5)) {
+  } else {
+    // ---------------------------------- fp32 accumulation + epilogue warps
+    // The tensor pipe adds into TMEM with truncation, so a long reduction
+    // kept there loses bits in proportion to its length.  Each chunk of
+    // CHUNK_KB k-blocks is therefore drained into fp32 registers and summed
+    // with round-to-nearest adds here.
+    const int q = warp & 3;
+    float acc[BN];
+#pragma unroll
+    for (int e = 0; e < BN; e++) acc[e] = 0.0f;
+    bool ok = true;
+    for (int c = 0; c < nchunks; c++) {
+      const int b = c & 1;
+      if (!mbar_wait(bar_accf(b), (c >> 1) & 1, abort_flag, p.err, 5)) { ok = false; break; }
       tc_fence_after();
-      const int q = warp & 3;
-      const int row = i0 + q * 32 + lane;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; c++) {
+#pragma unroll
+      for (int cc = 0; cc < BN / 32; cc++) {
         uint32_t v[32];
-        const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + c * 32;
+        const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + b * BN + cc * 32;
         asm volatile(
             "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
             "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
@@ -296,29 +336,32 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
               "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
             : "r"(taddr));
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-        if (row < p.I) {
-          const int col0 = j0 + c * 32;
-          float *dst = p.C + (size_t)row * p.ldc + col0;
-          if (col0 + 32 <= p.J) {
 #pragma unroll
-            for (int e = 0; e < 32; e += 4) {
-              float4 o = make_float4(__uint_as_float(v[e]), __uint_as_float(v[e + 1]), __uint_as_float(v[e + 2]),
-                                     __uint_as_float(v[e + 3]));
-              float4 *d4 = reinterpret_cast<float4 *>(dst + e);
-              if (p.beta) {
-                const float4 old = *d4;
-                o.x += old.x; o.y += old.y; o.z += old.z; o.w += old.w;
-              }
-              *d4 = o;
-            }
-          } else {
+        for (int e = 0; e < 32; e++) acc[cc * 32 + e] += __uint_as_float(v[e]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_acce(b));
+    }
+    if (ok) {
+      const int row = i0 + q * 32 + lane;
+      if (row < p.I) {
+        float *dst = p.C + (size_t)row * p.ldc + j0;
+        if (j0 + BN <= p.J) {
 #pragma unroll
-            for (int e = 0; e < 32; e++) {
-              if (col0 + e < p.J) {
-                const float o = __uint_as_float(v[e]);
-                dst[e] = p.beta ? dst[e] + o : o;
-              }
+          for (int e = 0; e < BN; e += 4) {
+            float4 o = make_float4(acc[e], acc[e + 1], acc[e + 2], acc[e + 3]);
+            float4 *d4 = reinterpret_cast<float4 *>(dst + e);
+            if (p.beta) {
+              const float4 old = *d4;
+              o.x += old.x; o.y += old.y; o.z += old.z; o.w += old.w;
             }
+            *d4 = o;
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < BN; e++) {
+            if (j0 + e < p.J) dst[e] = p.beta ? dst[e] + acc[e] : acc[e];
           }
         }
       }
@@ -347,14 +390,18 @@ static int get_encoder() {
 }
 
 // 2D fp32 map over a row-major [outer][inner] array with row stride `ld` floats.
+// K-major tiles use the 16-byte-chunk 128B swizzle, MN-major tiles the
+// 32-byte-chunk one (matching the descriptor layouts above).
 static int make_map(CUtensorMap *m, const float *ptr, uint64_t inner, uint64_t outer, uint64_t ld, uint32_t box_inner,
-                    uint32_t box_outer) {
+                    uint32_t box_outer, bool mn_major) {
   cuuint64_t dims[2] = {inner, outer};
   cuuint64_t strides[1] = {ld * 4};
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(ptr), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error(TL_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   return TL_OK;
@@ -400,18 +447,18 @@ int gemm_tc(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, i
   switch (op) {
     case GemmOp::NN:  // A = X[M,K] K-major; B = W[K,N] MN-major
       p.ldc = N; p.beta = 0;
-      if ((rc = tc::make_map(&ma, A, K, M, K, 32, tc::BM))) return rc;
-      if ((rc = tc::make_map(&mb, B, N, K, N, 32, 32))) return rc;
+      if ((rc = tc::make_map(&ma, A, K, M, K, 32, tc::BM, false))) return rc;
+      if ((rc = tc::make_map(&mb, B, N, K, N, 32, 32, true))) return rc;
       return tc::launch<false, true>(c, ma, mb, p);
     case GemmOp::NT:  // A = dY[M,N] K-major; B(r=n, j=k) = W[k*N+n] K-major
       p.ldc = K; p.beta = 1;
-      if ((rc = tc::make_map(&ma, A, N, M, N, 32, tc::BM))) return rc;
-      if ((rc = tc::make_map(&mb, B, N, K, N, 32, tc::BN))) return rc;
+      if ((rc = tc::make_map(&ma, A, N, M, N, 32, tc::BM, false))) return rc;
+      if ((rc = tc::make_map(&mb, B, N, K, N, 32, tc::BN, false))) return rc;
       return tc::launch<false, false>(c, ma, mb, p);
     case GemmOp::TN:  // A(i=k, r=m) = X[m*K+k] MN-major; B = dY[M,N] MN-major
       p.ldc = N; p.beta = 1;
-      if ((rc = tc::make_map(&ma, A, K, M, K, 32, 32))) return rc;
-      if ((rc = tc::make_map(&mb, B, N, M, N, 32, 32))) return rc;
+      if ((rc = tc::make_map(&ma, A, K, M, K, 32, 32, true))) return rc;
+      if ((rc = tc::make_map(&mb, B, N, M, N, 32, 32, true))) return rc;
       return tc::launch<true, true>(c, ma, mb, p);
   }
   return set_error(TL_EINVAL, "unknown GEMM op");

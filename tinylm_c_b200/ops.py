@@ -60,6 +60,8 @@ def _ptr(t, name, numel=None):
 
 
 def _prep(t):
+    if isinstance(t, torch.Tensor) and not t.is_cuda:
+        raise ValueError("CPU tensor given; libtinylm_cuda computes on the GPU only")
     idx = t.device.index if isinstance(t, torch.Tensor) else torch.cuda.current_device()
     if idx not in _inited:
         init(idx)
