@@ -105,6 +105,16 @@ int tl_last_gemm_engine(void);
  * `norm_out` may be a device or a host pointer; a host pointer makes the call
  * synchronous (it waits for the result). */
 int tl_grad_norm(const float *G, size_t n, float *norm_out);
+/* The same norm for callers that cannot allocate device memory (a framework
+ * whose allocator owns the whole GPU, a runtime with a fixed memory budget):
+ * no cudaMalloc, no tl_init needed.  No counterpart in the reference.  Uses a
+ * scratch array compiled into the library (128 KiB per device that loads it,
+ * held until exit), so n <= 2^30 elements; larger n returns TL_EINVAL.
+ * norm_dev is a device float; stream a cudaStream_t (NULL = legacy default).
+ * The first call on a device looks up the scratch address, so make it before
+ * any stream capture.  Calls share the scratch: calls that overlap on the GPU
+ * race and must be serialised by the caller. */
+int tl_grad_norm_noalloc(const float *G, size_t n, float *norm_dev, void *stream);
 /* sumsq_dev[0] = sum_i (double)G[i]^2 (device double) -- the per-shard half of
  * global_gradnorm, for sharded (ZeRO-1) norms. */
 int tl_grad_sumsq(const float *G, size_t n, double *sumsq_dev);

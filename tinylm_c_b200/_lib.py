@@ -45,6 +45,7 @@ SIGNATURES = {
     "tl_last_gemm_engine": (_c_int, []),
     "tl_grad_norm": (_c_int, [_c_void_p, _c_size, _c_void_p]),
     "tl_grad_sumsq": (_c_int, [_c_void_p, _c_size, _c_void_p]),
+    "tl_grad_norm_noalloc": (_c_int, [_c_void_p, _c_size, _c_void_p, _c_void_p]),
     "tl_clip_scale": (_c_int, [_c_void_p, _c_float, _c_void_p, _c_void_p]),
     "tl_adamw_step": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_size,
                                _c_float, _c_float, _c_float, _c_float, _c_int, _c_float]),
