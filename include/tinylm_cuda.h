@@ -139,6 +139,34 @@ int tl_clip_adamw_step(float *P, const float *G, float *M, float *V, size_t n,
                        float lr, float b1, float b2, float wd, int t,
                        float max_norm, float *norm_dev);
 
+/* ------------------------------------------------ device training step */
+/* The reference's whole step -- forward (tinylm.c:968-1029), backward
+ * (1072-1154, MTP heads 1036-1069), norm, clip, AdamW (2628-2633) -- on the
+ * device, for dense configurations (no MoE, no QK-norm; T <= 256, head_dim <=
+ * 64).  P/G/M/V use the reference's flat layout (map_weights, 361-393).
+ * cfg8 = {V, D, L, H, KV, F, T, n_mtp}.  Activations are allocated once, for
+ * `micro_batch` sequences; a batch B (a multiple of it) runs as consecutive
+ * micro-batches accumulating into G, every logits gradient scaled by 1/(B*T).
+ * Token arrays are device int32: tok/tgt [B*T], tgt_mtp [n_mtp][B*T]. */
+int tl_model_create(const int *cfg8, int micro_batch, void **handle);
+size_t tl_model_nparams(void *handle);
+int tl_model_destroy(void *handle);
+/* param_count (tinylm.c:345-358) of a dense configuration (0 if invalid). */
+size_t tl_model_param_count(const int *cfg8);
+/* init_params (tinylm.c:395-419) into a HOST buffer of tl_model_param_count
+ * floats, reference generator seeded as TINYLM_SEED does (tinylm.c:4809-4811).
+ * Host only (no GPU needed). */
+int tl_model_init_params(const int *cfg8, float *P_host, unsigned long long seed);
+/* Loss only (mean cross-entropy, as forward() returns). */
+int tl_model_forward(void *handle, const float *P, const int *tok, const int *tgt, int B, float *loss_dev);
+/* G += gradients of the batch; loss_dev (may be NULL) = mean loss. */
+int tl_model_forward_backward(void *handle, const float *P, float *G, const int *tok, const int *tgt,
+                              const int *tgt_mtp, int B, float *loss_dev);
+/* memset(G) -> forward/backward -> norm -> clip(max_norm) -> AdamW(lr, 0.9,
+ * 0.95, 0.1, t): one step of train_loop / cmd_bench (tinylm.c:2627-2633). */
+int tl_model_step(void *handle, float *P, float *G, float *M, float *V, const int *tok, const int *tgt,
+                  const int *tgt_mtp, int B, float lr, int t, float max_norm, float *loss_dev, float *norm_dev);
+
 /* ------------------------------------------- data parallel + ZeRO-1 (NCCL) */
 /* No counterpart in the reference (it has no distributed code); this is the
  * multi-GPU form of the optimizer step above.

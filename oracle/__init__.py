@@ -99,6 +99,8 @@ def ref():
         L.tlref_model_logits.restype = _fp
         L.tlref_model_forward.argtypes = [ctypes.c_void_p]
         L.tlref_model_forward.restype = _f
+        L.tlref_model_fwd_bwd.argtypes = [ctypes.c_void_p]
+        L.tlref_model_fwd_bwd.restype = _f
         L.tlref_model_step.argtypes = [ctypes.c_void_p, _f, _i, ctypes.POINTER(_f)]
         L.tlref_model_step.restype = _f
         L.tlref_model_free.argtypes = [ctypes.c_void_p]

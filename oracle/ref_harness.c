@@ -77,6 +77,10 @@ TLREF_API void *tlref_model_new(const int *cfg7, int n_mtp, int B, unsigned long
     c->n_mtp = n_mtp;
     cfg_derive(c);
     g_rng = (uint64_t)seed | 1ULL;
+    /* rope_init caches its table by position count only (tinylm.c:615), so a
+     * second model with another head size in the same process would index a
+     * stale table; drop it first (a CLI process only ever builds one model). */
+    free(rope_cos); free(rope_sin); rope_cos = rope_sin = NULL; rope_max = 0;
     rope_init(c, c->T);
     r->np = param_count(c);
     r->P = fz(r->np); r->G = fz(r->np); r->M = fz(r->np); r->V = fz(r->np);
@@ -113,6 +117,15 @@ TLREF_API float tlref_model_forward(void *h)
 {
     RefModel *r = (RefModel *)h;
     return forward(&r->c, &r->w, r->a, r->tok, r->tgt);
+}
+/* forward + memset(G) + backward only (the gradient stays in G); returns the loss. */
+TLREF_API float tlref_model_fwd_bwd(void *h)
+{
+    RefModel *r = (RefModel *)h;
+    float loss = forward(&r->c, &r->w, r->a, r->tok, r->tgt);
+    memset(r->G, 0, sizeof(float) * r->np);
+    backward(&r->c, &r->w, &r->gr, r->a, r->tok, r->tgt, r->tgt_mtp);
+    return loss;
 }
 /* One step exactly as cmd_bench 4736-4740; returns the loss, writes the grad norm. */
 TLREF_API float tlref_model_step(void *h, float lr, int t, float *gnorm_out)

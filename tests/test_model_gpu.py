@@ -1,0 +1,154 @@
+"""The whole training step on the GPU (tl_model_*) against the reference:
+10-step losses and grad norms of BASELINE config 1 (m1, n_mtp=2, B=8) and the
+nano preset from the committed fixtures, and the gradient of one backward
+against the reference leg run live.  Loss tolerance 1e-4 (north star)."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from tinylm_c_b200 import _lib, model, ops
+
+pytestmark = pytest.mark.gpu
+LOSS_ATOL = 1e-4
+GNORM_RTOL = 1e-4
+
+
+def run_steps(cuda, z, preset, micro_batch, steps):
+    n_mtp = int(z["n_mtp"][0])
+    B = int(z["B"][0])
+    c = model.cfg8(preset, n_mtp)
+    m = model.Model(c, micro_batch, 0)
+    P = model.init_params(c, int(z["seed"][0])).to(cuda)
+    n = P.numel()
+    G = torch.zeros(n, device=cuda)
+    M = torch.zeros(n, device=cuda)
+    V = torch.zeros(n, device=cuda)
+    tok = torch.from_numpy(z["tok"]).to(cuda)
+    tgt = torch.from_numpy(z["tgt"]).to(cuda)
+    mtp = torch.from_numpy(np.ascontiguousarray(z["mtp"])).to(cuda) if n_mtp else None
+    loss = torch.zeros(1, device=cuda)
+    norm = torch.zeros(1, device=cuda)
+    losses, norms = [], []
+    for it in range(steps):
+        m.step(P, G, M, V, tok, tgt, mtp, B, 3e-4, it + 1, 1.0, loss, norm)
+        losses.append(loss.item())
+        norms.append(norm.item())
+    _lib.check(_lib.lib().tl_device_status())
+    m.close()
+    return np.array(losses), np.array(norms), P
+
+
+@pytest.mark.parametrize("name,preset,micro", [("train_nano", "nano", 2), ("train_nano", "nano", 1),
+                                                ("train_m1", "m1", 8), ("train_m1", "m1", 4)])
+def test_ten_steps_match_reference(cuda, golden, name, preset, micro):
+    z = golden(name)
+    losses, norms, _ = run_steps(cuda, z, preset, micro, 10)
+    np.testing.assert_allclose(losses, z["losses"], rtol=0, atol=LOSS_ATOL)
+    np.testing.assert_allclose(norms, z["gnorms"], rtol=GNORM_RTOL)
+
+
+@pytest.mark.skipif(not oracle.has_ref(), reason="reference leg not built")
+@pytest.mark.parametrize("preset,n_mtp,B", [("nano", 0, 2), ("m1", 2, 2)])
+def test_gradient_matches_reference_leg(cuda, preset, n_mtp, B):
+    """One forward/backward from the reference's own parameters and tokens:
+    every parameter tensor's gradient within 1e-4 relative (L2)."""
+    R = oracle.ref()
+    R.tlref_init(8, 0)
+    cfg = list(model.PRESETS[preset])
+    h = R.tlref_model_new((oracle._i * 7)(*cfg), n_mtp, B, 0)
+    try:
+        n = R.tlref_model_nparams(h)
+        N = B * 256
+        P = torch.from_numpy(np.ctypeslib.as_array(R.tlref_model_buf(h, 0), shape=(n,)).copy()).to(cuda)
+        tok = torch.from_numpy(np.ctypeslib.as_array(R.tlref_model_tokens(h, 0), shape=(N,)).copy()).to(cuda)
+        tgt = torch.from_numpy(np.ctypeslib.as_array(R.tlref_model_tokens(h, 1), shape=(N,)).copy()).to(cuda)
+        mtp = None
+        if n_mtp:
+            mtp = torch.from_numpy(np.stack([np.ctypeslib.as_array(R.tlref_model_tokens(h, 2 + k), shape=(N,))
+                                             for k in range(n_mtp)]).astype(np.int32)).to(cuda)
+        loss_ref = R.tlref_model_fwd_bwd(h)
+        Gr = np.ctypeslib.as_array(R.tlref_model_buf(h, 1), shape=(n,)).copy()
+    finally:
+        R.tlref_model_free(h)
+    m = model.Model(model.cfg8(preset, n_mtp), B, 0)
+    G = torch.zeros(n, device=cuda)
+    loss = torch.zeros(1, device=cuda)
+    m.forward_backward(P, G, tok, tgt, mtp, B, loss)
+    torch.cuda.synchronize()
+    _lib.check(_lib.lib().tl_device_status())
+    m.close()
+    assert abs(loss.item() - loss_ref) <= LOSS_ATOL
+    g = G.cpu().numpy().astype(np.float64)
+    V, D, L, H, KV, F, T = cfg
+    KD = KV * D // H
+    sizes = [("emb", V * D)]
+    for l in range(L):
+        sizes += [(f"an1.{l}", D), (f"wq.{l}", D * D), (f"wk.{l}", D * KD), (f"wv.{l}", D * KD), (f"wo.{l}", D * D),
+                  (f"an2.{l}", D), (f"w1.{l}", D * F), (f"w3.{l}", D * F), (f"w2.{l}", F * D)]
+    sizes += [("nf", D)] + [(f"mtp.{k}", D * D) for k in range(n_mtp)]
+    off = 0
+    for name, sz in sizes:
+        a, b = g[off:off + sz], Gr[off:off + sz].astype(np.float64)
+        rel = np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30)
+        assert rel <= 1e-4, (name, rel)
+        off += sz
+    assert off == n
+
+
+def test_micro_batching_changes_only_rounding(cuda):
+    """B=4 as one micro-batch or as four: same loss and gradient up to rounding."""
+    c = model.cfg8("nano", 0)
+    P = model.init_params(c, 7).to(cuda)
+    n = P.numel()
+    g = torch.Generator(device=cuda).manual_seed(3)
+    tok = torch.randint(0, 512, (4 * 256,), generator=g, device=cuda, dtype=torch.int32)
+    tgt = torch.randint(0, 512, (4 * 256,), generator=g, device=cuda, dtype=torch.int32)
+    out = []
+    for mb in (4, 1):
+        m = model.Model(c, mb, 0)
+        G = torch.zeros(n, device=cuda)
+        loss = torch.zeros(1, device=cuda)
+        m.forward_backward(P, G, tok, tgt, None, 4, loss)
+        torch.cuda.synchronize()
+        out.append((loss.item(), G.clone()))
+        m.close()
+    assert out[0][0] == pytest.approx(out[1][0], abs=1e-6)
+    rel = (out[0][1] - out[1][1]).norm() / out[0][1].norm()
+    assert rel.item() < 1e-5
+
+
+def test_scaled_config_one_step(cuda):
+    """BASELINE config 5 shape (188.8 M parameters) runs one step at batch 1:
+    initial loss near ln(8192) + var(logits)/2 (logit std ~ 0.02*sqrt(1024)),
+    finite gradient norm."""
+    c = model.cfg8("scaled", 0)
+    m = model.Model(c, 1, 0)
+    P = model.init_params(c, 0).to(cuda)
+    n = P.numel()
+    assert n == 188777472
+    G, M, V = (torch.zeros(n, device=cuda) for _ in range(3))
+    g = torch.Generator(device=cuda).manual_seed(5)
+    tok = torch.randint(0, 8192, (256,), generator=g, device=cuda, dtype=torch.int32)
+    tgt = torch.randint(0, 8192, (256,), generator=g, device=cuda, dtype=torch.int32)
+    loss = torch.zeros(1, device=cuda)
+    norm = torch.zeros(1, device=cuda)
+    m.step(P, G, M, V, tok, tgt, None, 1, 3e-4, 1, 1.0, loss, norm)
+    torch.cuda.synchronize()
+    _lib.check(_lib.lib().tl_device_status())
+    m.close()
+    assert 9.0 < loss.item() < 9.6
+    assert np.isfinite(norm.item()) and norm.item() > 0
+
+
+def test_bad_tokens_are_reported(cuda):
+    c = model.cfg8("nano", 0)
+    m = model.Model(c, 1, 0)
+    P = model.init_params(c, 0).to(cuda)
+    G = torch.zeros(P.numel(), device=cuda)
+    tok = torch.full((256,), 9999, device=cuda, dtype=torch.int32)
+    tgt = torch.zeros(256, device=cuda, dtype=torch.int32)
+    m.forward_backward(P, G, tok, tgt, None, 1)
+    rc = _lib.lib().tl_device_status()
+    m.close()
+    assert rc == _lib.TL_EINVAL

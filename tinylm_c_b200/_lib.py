@@ -54,6 +54,16 @@ SIGNATURES = {
     "tl_clip_adamw_step": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_size,
                                     _c_float, _c_float, _c_float, _c_float, _c_int, _c_float,
                                     _c_void_p]),
+    "tl_model_create": (_c_int, [ctypes.POINTER(_c_int), _c_int, ctypes.POINTER(_c_void_p)]),
+    "tl_model_nparams": (_c_size, [_c_void_p]),
+    "tl_model_destroy": (_c_int, [_c_void_p]),
+    "tl_model_param_count": (_c_size, [ctypes.POINTER(_c_int)]),
+    "tl_model_init_params": (_c_int, [ctypes.POINTER(_c_int), _c_void_p, ctypes.c_ulonglong]),
+    "tl_model_forward": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_int, _c_void_p]),
+    "tl_model_forward_backward": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
+                                           _c_int, _c_void_p]),
+    "tl_model_step": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
+                               _c_void_p, _c_int, _c_float, _c_int, _c_float, _c_void_p, _c_void_p]),
     "tl_zero1_padded": (_c_size, [_c_size, _c_int]),
     "tl_dist_unique_id": (_c_int, [_c_void_p]),
     "tl_dist_init": (_c_int, [_c_int, _c_int, _c_void_p]),

@@ -25,6 +25,21 @@ static int gemm_entry(GemmOp op, float *C, const float *A, const float *B, int M
     if (op == GemmOp::NN) TL_TRY_CUDA(cudaMemsetAsync(C, 0, sizeof(float) * (size_t)I * J, c->stream));
     return TL_OK;
   }
+  return gemm_run(c, op, C, A, B, M, K, N);
+}
+
+}  // namespace tl
+
+// Engine choice without argument checks, for callers inside the library that
+// have validated their buffers once (the device training step).
+int tl::gemm_run(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, int M, int K, int N) {
+  int I, J, R;
+  gemm_dims(op, M, K, N, &I, &J, &R);
+  if (I == 0 || J == 0) return TL_OK;
+  if (R == 0) {
+    if (op == GemmOp::NN) TL_TRY_CUDA(cudaMemsetAsync(C, 0, sizeof(float) * (size_t)I * J, c->stream));
+    return TL_OK;
+  }
   const bool tc_ok = gemm_tc_supported(op, C, A, B, M, K, N);
   if (g_engine_pref == 2 && !tc_ok)
     return set_error(TL_EINVAL, "tensor-core engine forced but shape/alignment unsupported (M=%d K=%d N=%d)", M, K, N);
@@ -35,8 +50,6 @@ static int gemm_entry(GemmOp op, float *C, const float *A, const float *B, int M
   g_engine_last = 1;
   return gemm_simt(c, op, C, A, B, M, K, N);
 }
-
-}  // namespace tl
 
 using namespace tl;
 

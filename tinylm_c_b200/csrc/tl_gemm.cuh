@@ -19,6 +19,7 @@ inline void gemm_dims(GemmOp op, int M, int K, int N, int *I, int *J, int *R) {
   }
 }
 
+int gemm_run(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, int M, int K, int N);
 int gemm_simt(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, int M, int K, int N);
 // Returns TL_EINVAL (without launching) when the shape or alignment is not
 // supported by the tensor-core engine.

@@ -135,6 +135,8 @@ TL_API int tl_device_status(void) {
   TL_TRY_CUDA(cudaMemcpy(&code, c->err_flag, sizeof(int), cudaMemcpyDeviceToHost));
   if (code) {
     TL_TRY_CUDA(cudaMemset(c->err_flag, 0, sizeof(int)));
+    if (code >= 100)
+      return set_error(TL_EINVAL, "a device-side input check failed (code %d: token id outside [0, V))", code);
     return set_error(TL_ETIMEOUT, "a bounded device-side wait expired (site %d); the kernel returned early", code);
   }
   return TL_OK;
