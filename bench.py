@@ -1,22 +1,27 @@
 """Benchmark of tinylm-c's training-step hot path on B200 (libtinylm_cuda).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload adamw|gemm]
+                    [--workload train|train_m1|train_m8|adamw]
 
-Default workload: the fused AdamW + global-norm clip step
-over flat fp32 buffers p, g, m, v of 2^28 elements each (p~N(0,0.02),
-g~N(0,1e-3), m~N(0,1e-4), v=|N(0,1e-6)|, t counting up from 100, lr 3e-4,
-betas 0.9/0.95, wd 0.1, clip 1.0).  One step = sum of squares of G -> clip scale
--> AdamW, 32 algorithmic bytes per element.  With N > 1 GPUs (torchrun, one
-process per GPU) one step is the ZeRO-1 optimizer step over the same 2^28
-buffer: ReduceScatter(G, avg) -> shard norm -> AllReduce -> AdamW on the 1/N
-shard -> AllGather(P); total work is fixed, so scaling is "strong".
+Default workload: BASELINE config 5, the scaled tiny Llama (V 8192, D 1024,
+16 layers, 16 heads / 4 KV heads, SwiGLU 2816, ctx 256, fp32, 188.8 M params)
+trained on a global batch of 512x256 uniform random tokens: one step =
+forward + backward + global-norm clip + AdamW, data parallel over N GPUs (one
+process per GPU, torchrun) with a ZeRO-1 optimizer step (reduce-scatter of G,
+sharded AdamW, all-gather of P over NCCL).  Global batch fixed across N:
+scaling is "strong".  Metric: train tokens/s (whole job).  The same line
+carries the second half of BASELINE's metric, the fused AdamW+clip HBM GB/s
+(config 2: 2^28 fp32 params; at N=1 measured in the same run).
 
-Rank 0 prints ONE JSON line.  `value` is device-timed with inputs resident in
-HBM; `e2e` is the same metric through the C ABI with pinned host buffers and
-the host<->device copies inside the timed region.  `--impl reference` times the
-reference's own CPU implementation (tinylm.c adamw + global_gradnorm, compiled
-by oracle/Makefile) on the host cores.
+Other workloads: train_m1 (config 1: m1 preset, n_mtp=2, batch 8), train_m8
+(config 4: m8, batch 64), adamw (config 2 alone; ZeRO-1 with N > 1).
+
+Rank 0 prints ONE JSON line.  `value` is device-timed (CUDA events, max over
+ranks) with inputs resident in HBM; `e2e` is the same metric through the
+library's API with the step's input (tokens, or the gradient for adamw) copied
+from pinned host memory and the result (loss / norm) read back every step.
+`--impl reference` times the reference's own CPU implementation (tinylm.c
+compiled unmodified by oracle/Makefile) on the host cores.
 """
 import argparse
 import ctypes
@@ -31,25 +36,36 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-N_ELEMS = 1 << 28
-LR, B1, B2, WD, MAX_NORM, T0 = 3e-4, 0.9, 0.95, 0.1, 1.0, 100
-BYTES_PER_ELEM = 32          # norm reads G (4) + AdamW reads P,G,M,V and writes P,M,V (28)
-ADAMW_BYTES_PER_ELEM = 28
-NORM_BYTES_PER_ELEM = 4
-METRIC = "fused AdamW+clip HBM GB/s (fp32, 2^28 params)"
-GEMM_METRIC = "GEMM GFLOP/s (fp32 3xTF32)"
+T_CTX = 256
+LR, B1, B2, WD, MAX_NORM = 3e-4, 0.9, 0.95, 0.1, 1.0
+ADAMW_N = 1 << 28
+ADAMW_T0 = 100
+BYTES_PER_PARAM = 32          # norm reads G (4) + AdamW reads P,G,M,V and writes P,M,V (28)
+ADAMW_BYTES = 28
+NORM_BYTES = 4
+TRAIN_METRIC = "train tokens/s (fwd+bwd+AdamW)"
+ADAMW_METRIC = "fused AdamW+clip HBM GB/s (fp32, 2^28 params)"
+
+# name -> (preset, n_mtp, global batch, micro-batch cap, CPU-baseline batch, BASELINE config)
+TRAIN = {
+    "train": ("scaled", 0, 512, 64, 2, "config5_scaled_tiny_llama"),
+    "train_m1": ("m1", 2, 8, 8, 8, "config1_m1_nmtp2_b8"),
+    "train_m8": ("m8", 0, 64, 64, 8, "config4_m8_b64"),
+}
 
 
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["adamw", "gemm"], default="adamw")
-    ap.add_argument("--n", type=int, default=N_ELEMS, help="elements per buffer (default 2^28)")
+    ap.add_argument("--workload", choices=list(TRAIN) + ["adamw"], default="train")
+    ap.add_argument("--n", type=int, default=ADAMW_N, help="adamw workload: elements per buffer")
+    ap.add_argument("--batch", type=int, default=0, help="train workloads: global batch (0 = the config's)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-adamw-line", action="store_true", help="train: skip the config-2 AdamW sub-measurement")
     return ap.parse_args()
 
 
@@ -133,23 +149,102 @@ def measured_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
         with open(p) as f:
-            d = json.load(f)
-        return d, "measured"
-    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+            return json.load(f), "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
 
 
-def committed_traffic(kernel, workload):
+def committed_traffic(key):
     """dram bytes per launch from the committed ncu summary, if any."""
     p = os.path.join(ROOT, "profiles", "traffic.json")
     if not os.path.exists(p):
         return None
     with open(p) as f:
-        d = json.load(f)
-    e = d.get(f"{workload}:{kernel}")
-    return e
+        return json.load(f).get(key)
 
 
-# ----------------------------------------------------------- reference (CPU)
+def gemm_flops_per_token(cfg):
+    """fp32 FLOPs of all GEMMs per token of one training step: 6 x the
+    GEMM-held parameters (each weight: one forward and two backward GEMMs),
+    plus the MTP heads (tinylm.c:1036-1069)."""
+    V, D, L, H, KV, F, T, n_mtp = cfg
+    KD = KV * (D // H)
+    per = 6 * (L * (2 * D * D + 2 * D * KD + 3 * D * F) + D * V)
+    per += n_mtp * (6 * D * D + 6 * D * V)
+    return per
+
+
+# ------------------------------------------------------------------ helpers
+class Run:
+    """Per-process GPU context: device, optional NCCL process group, library."""
+
+    def __init__(self, rank, world, local):
+        import torch
+        from tinylm_c_b200 import _lib, ops
+        self.torch, self.ops, self.L, self._lib = torch, ops, _lib.lib(), _lib
+        self.rank, self.world, self.local = rank, world, local
+        self.dev = torch.device("cuda", local)
+        torch.cuda.set_device(self.dev)
+        if world > 1:
+            import datetime
+            import torch.distributed as dist
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=self.dev)
+        ops.init(local)
+        self.stream = torch.cuda.current_stream(self.dev)
+
+    def barrier(self):
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+        self.torch.cuda.synchronize()
+
+    def max_over_ranks(self, x):
+        if self.world == 1:
+            return x
+        import torch.distributed as dist
+        t = self.torch.tensor([x], device=self.dev, dtype=self.torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.item()
+
+    def timed(self, step, steps, t0):
+        """K steps between barriers; device time from CUDA events on the
+        launching stream, max over ranks; per-kernel times from the tracer."""
+        torch, L = self.torch, self.L
+        L.tl_trace_reset()
+        L.tl_trace_enable(1)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(gpu_uuid(torch, self.dev)) as clk:
+            self.barrier()
+            e0.record(self.stream)
+            for i in range(steps):
+                step(t0 + i)
+            e1.record(self.stream)
+            self.barrier()
+        L.tl_trace_enable(0)
+        ms = self.max_over_ranks(e0.elapsed_time(e1))
+        return ms / steps, self.kernels(steps), clk.summary()
+
+    def kernels(self, steps):
+        L, _lib = self.L, self._lib
+        out = {}
+        names = ctypes.create_string_buffer(8192)
+        _lib.check(L.tl_trace_names(names, 8192))
+        for nm in filter(None, names.value.decode().split(",")):
+            tot, cnt = ctypes.c_double(0), ctypes.c_longlong(0)
+            _lib.check(L.tl_trace_get(nm.encode(), ctypes.byref(tot), ctypes.byref(cnt)))
+            out[nm] = {"ms_per_step": round(tot.value / steps, 4), "launches": cnt.value,
+                       "ms_per_launch": round(tot.value / max(1, cnt.value), 5)}
+        return out
+
+    def status(self):
+        self._lib.check(self.L.tl_device_status())
+
+    def close(self):
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+            dist.destroy_process_group()
+
+
 def cpu_threads():
     try:
         return len(os.sched_getaffinity(0))
@@ -157,10 +252,35 @@ def cpu_threads():
         return os.cpu_count() or 1
 
 
-def run_reference_adamw(n, steps, warmup):
-    """The reference's own adamw + global_gradnorm (tinylm.c:1159-1176), compiled
-    unmodified, on all host threads; one step = norm + clip + AdamW on n elements."""
-    import numpy as np
+# ------------------------------------------------------ reference CPU arm
+def reference_train(wl, steps, warmup):
+    """The reference's own forward/backward/norm/AdamW (tinylm.c:4736-4740),
+    compiled unmodified, on all host threads, at a CPU-sized batch."""
+    import oracle
+    from tinylm_c_b200 import model
+    preset, n_mtp, _, _, B, _ = TRAIN[wl]
+    R = oracle.ref()
+    threads = cpu_threads()
+    R.tlref_init(threads, 0)
+    cfg = list(model.PRESETS[preset])
+    h = R.tlref_model_new((oracle._i * 7)(*cfg), n_mtp, B, 0)
+    times = []
+    gn = oracle._f(0.0)
+    try:
+        for it in range(warmup + steps):
+            t0 = time.perf_counter()
+            R.tlref_model_step(h, LR, it + 1, ctypes.byref(gn))
+            dt = time.perf_counter() - t0
+            if it >= warmup:
+                times.append(dt)
+    finally:
+        R.tlref_model_free(h)
+    sec = statistics.median(times)
+    return B * T_CTX / sec, sec, threads, B
+
+
+def reference_adamw(n, steps, warmup):
+    """The reference's own adamw + global_gradnorm (tinylm.c:1159-1176)."""
     import oracle
     R = oracle.ref()
     threads = cpu_threads()
@@ -172,211 +292,233 @@ def run_reference_adamw(n, steps, warmup):
         t0 = time.perf_counter()
         gn = R.tlref_gradnorm(fp(g), n)
         gs = 1.0 / gn if gn > 1.0 else 1.0
-        R.tlref_adamw(fp(p), fp(g), fp(m), fp(v), n, LR, B1, B2, WD, T0 + it, gs)
+        R.tlref_adamw(fp(p), fp(g), fp(m), fp(v), n, LR, B1, B2, WD, ADAMW_T0 + it, gs)
         dt = time.perf_counter() - t0
         if it >= warmup:
             times.append(dt)
     sec = statistics.median(times)
-    return n * BYTES_PER_ELEM / sec / 1e9, sec, threads
+    return n * BYTES_PER_PARAM / sec / 1e9, sec, threads
 
 
-def cpu_baseline_adamw(n_full):
-    """Bounded sample for the GPU arm's line: the reference at the full n for a
-    few steps (memory-bound; per-step cost does not depend on the step count)."""
-    steps = int(os.environ.get("TL_CPU_BASELINE_STEPS", "5"))
-    gbs, sec, threads = run_reference_adamw(n_full, steps, 1)
-    return {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "reference",
-            "sample": f"tinylm.c adamw+global_gradnorm (oracle/_ref), n=2^{n_full.bit_length() - 1}, "
-                      f"median of {steps} steps after 1 warm-up, OMP threads={threads}",
-            "ms_per_step": round(sec * 1e3, 3)}
+# ---------------------------------------------------------- train workloads
+def run_train(args, rk):
+    torch, ops = rk.torch, rk.ops
+    from tinylm_c_b200 import model
+    preset, n_mtp, B_glob, mb_cap, _, cfg_name = TRAIN[args.workload]
+    if args.batch:
+        B_glob = args.batch
+    world, rank = rk.world, rk.rank
+    if B_glob % world:
+        raise SystemExit(f"global batch {B_glob} not divisible by {world} ranks")
+    B = B_glob // world
+    mb = min(B, mb_cap)
+    while B % mb:
+        mb -= 1
+    cfg = model.cfg8(preset, n_mtp)
+    m = model.Model(cfg, mb, rk.local)
+    n = m.nparams
+    P0 = model.init_params(cfg, 0)
+    dev = rk.dev
+    if world == 1:
+        n_pad, shard = n, n
+        P = P0.to(dev)
+        G = torch.zeros(n, device=dev)
+    else:
+        from tinylm_c_b200.zero1 import Zero1
+        z = Zero1(n, rank, world, rk.local)
+        n_pad, shard = z.n_pad, z.shard
+        P = torch.zeros(n_pad, device=dev)
+        P[:n] = P0.to(dev)
+        G = torch.zeros(n_pad, device=dev)
+    del P0
+    M = torch.zeros(shard, device=dev)
+    V = torch.zeros(shard, device=dev)
+    Vocab = cfg[0]
+    N = B * T_CTX
+    gen = torch.Generator(device=dev).manual_seed(1000 + rank)
+    tok = torch.randint(0, Vocab, (N,), generator=gen, device=dev, dtype=torch.int32)
+    tgt = torch.randint(0, Vocab, (N,), generator=gen, device=dev, dtype=torch.int32)
+    mtp = torch.randint(0, Vocab, (n_mtp, N), generator=gen, device=dev, dtype=torch.int32) if n_mtp else None
+    loss = torch.zeros(1, device=dev)
+    norm = torch.zeros(1, device=dev)
 
+    if world == 1:
+        def step(t):
+            m.step(P, G, M, V, tok, tgt, mtp, B, LR, t, MAX_NORM, loss, norm)
+    else:
+        def step(t):
+            G.zero_()
+            m.forward_backward(P, G, tok, tgt, mtp, B, loss)
+            z.step(P, G, M, V, LR, B1, B2, WD, t, MAX_NORM, norm)
 
-# ------------------------------------------------------------- our arm (GPU)
-def run_ours_adamw(args, rank, world, local):
-    import torch
-    from tinylm_c_b200 import _lib, ops
-    dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
+    for i in range(args.warmup):
+        step(1 + i)
+    rk.torch.cuda.synchronize()
+    rk.status()
+    t0 = 1 + args.warmup
+    ms_step, kernels, clocks = rk.timed(step, args.steps, t0)
+    rk.status()
+    value = B_glob * T_CTX / (ms_step * 1e-3)
+    loss_val = loss.item()
+
+    # ---- end to end: tokens from pinned host memory, loss read back, every step
+    e2e = None
+    if not args.no_e2e:
+        steps = max(1, min(args.steps, 5))
+        hs = [x.cpu().pin_memory() for x in (tok, tgt) + ((mtp,) if n_mtp else ())]
+        ds = [tok, tgt] + ([mtp] if n_mtp else [])
+        hloss = torch.zeros(1).pin_memory()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        rk.barrier()
+        e0.record(rk.stream)
+        t1 = t0 + args.steps
+        for i in range(steps):
+            for d, h in zip(ds, hs):
+                d.copy_(h, non_blocking=True)
+            step(t1 + i)
+            hloss.copy_(loss, non_blocking=True)
+        e1.record(rk.stream)
+        rk.barrier()
+        ms = rk.max_over_ranks(e0.elapsed_time(e1)) / steps
+        e2e = {"value": round(B_glob * T_CTX / (ms * 1e-3), 1), "unit": "tokens/s",
+               "h2d_bytes_per_step": sum(h.numel() * 4 for h in hs) * world, "d2h_bytes_per_step": 4,
+               "steps": steps, "ms_per_step": round(ms, 3),
+               "path": "pinned host tokens -> tl_model_step (N=1) / tl_model_forward_backward + tl_zero1_step -> host loss"}
+
+    # ---- roofline of the dominant kernel (the tensor-core GEMM)
+    peaks, peak_kind = measured_peaks()
+    gflop_tok = gemm_flops_per_token(tuple(cfg))
+    gemm = kernels.get("gemm_tc", {"ms_per_step": 0.0, "launches": 0})
+    flops_rank = gflop_tok * N
+    achieved = flops_rank / (gemm["ms_per_step"] * 1e-3) / 1e12 if gemm["ms_per_step"] else None
+    bf16 = peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops"))
+    peak = bf16 / 6.0
+    roofline = {"kernel": "gemm_tc (tcgen05 3xTF32)", "bound": "tensor", "unit": "TFLOP/s",
+                "achieved": round(achieved, 2) if achieved else None, "peak": round(peak, 1),
+                "peak_source": f"{peak_kind} bf16 sustained {bf16} TFLOP/s / 6 (tf32 = bf16/2; 3 tf32 MMAs per fp32 product)",
+                "frac": round(achieved / peak, 4) if achieved else None,
+                "traffic": None, "algorithmic_flops_per_step": flops_rank,
+                "gemm_share_of_step": round(gemm["ms_per_step"] / ms_step, 4) if ms_step else None}
+    tr = committed_traffic(f"{args.workload}:gemm_tc")
+    if tr:
+        roofline["traffic"] = tr.get("bytes_per_step")
+        roofline["traffic_source"] = tr.get("source")
+    launches = sum(k["launches"] for k in kernels.values())
+
+    adam_line = None
+    if kernels.get("adamw_vec", {}).get("ms_per_launch"):
+        a = kernels["adamw_vec"]["ms_per_launch"]
+        adam_line = {"in_step_adamw_gbs": round(shard * ADAMW_BYTES / (a * 1e-3) / 1e9, 1),
+                     "params_per_rank": shard}
+    m.close()
+    del P, G, M, V
     if world > 1:
-        import datetime
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
-    ops.init(local)
-    L = _lib.lib()
-    n = args.n
-    gen = torch.Generator(device=dev)
-    gen.manual_seed(1234 + rank)
-    stream = torch.cuda.current_stream(dev)
+        z.close()
+    torch.cuda.empty_cache()
 
+    out = None
+    if rank == 0:
+        out = {"metric": TRAIN_METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
+               "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 3),
+               "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+               "data": "synthetic (uniform random token ids, seeded); weights from the reference's seeded init_params",
+               "config": {"workload": cfg_name, "model": preset, "n_params": n, "n_mtp": n_mtp,
+                          "global_batch": B_glob, "seq_len": T_CTX, "micro_batch": mb,
+                          "parallelism": "single" if world == 1 else f"dp{world}_zero1",
+                          "gemm_gflop_per_token": round(gflop_tok / 1e9, 4),
+                          "l2": "per-step working set >> 126 MB L2 (no flush needed)"},
+               "e2e": e2e, "roofline": roofline, "clocks": clocks, "gpu_launches": launches,
+               "loss": round(loss_val, 5), "kernels": kernels}
+        if adam_line:
+            out["fused_adamw"] = adam_line
+    return out
+
+
+# --------------------------------------------------------------- adamw (cfg 2)
+def run_adamw(args, rk, n):
+    torch, ops = rk.torch, rk.ops
+    world, rank, dev = rk.world, rk.rank, rk.dev
+    gen = torch.Generator(device=dev).manual_seed(1234 + rank)
     if world == 1:
         p = torch.randn(n, device=dev, generator=gen) * 0.02
         g = torch.randn(n, device=dev, generator=gen) * 1e-3
         m = torch.randn(n, device=dev, generator=gen) * 1e-4
         v = (torch.randn(n, device=dev, generator=gen) * 1e-6).abs()
+        shard = n
         norm = torch.zeros(1, device=dev)
 
         def step(t):
             ops.clip_adamw(p, g, m, v, n, LR, B1, B2, WD, t, MAX_NORM, norm)
-        shard_n = n
     else:
         from tinylm_c_b200.zero1 import Zero1
-        z = Zero1(n, rank, world, local)
-        shard_n = z.shard
+        z = Zero1(n, rank, world, rk.local)
+        shard = z.shard
         p = torch.zeros(z.n_pad, device=dev)
         g = torch.zeros(z.n_pad, device=dev)
         p[:n] = torch.randn(n, device=dev, generator=torch.Generator(device=dev).manual_seed(1234)) * 0.02
         g[:n] = torch.randn(n, device=dev, generator=gen) * 1e-3
-        m = torch.randn(z.shard, device=dev, generator=gen) * 1e-4
-        v = (torch.randn(z.shard, device=dev, generator=gen) * 1e-6).abs()
+        m = torch.randn(shard, device=dev, generator=gen) * 1e-4
+        v = (torch.randn(shard, device=dev, generator=gen) * 1e-6).abs()
         norm = torch.zeros(1, device=dev)
 
         def step(t):
             z.step(p, g, m, v, LR, B1, B2, WD, t, MAX_NORM, norm)
+    for i in range(args.warmup):
+        step(ADAMW_T0 + i)
     torch.cuda.synchronize()
+    t0 = ADAMW_T0 + args.warmup
+    ms_step, kernels, clocks = rk.timed(step, args.steps, t0)
+    rk.status()
+    value = n * BYTES_PER_PARAM / (ms_step * 1e-3) / 1e9
 
-    t = T0
-    for _ in range(args.warmup):
-        step(t)
-        t += 1
-    torch.cuda.synchronize()
-
-    def barrier():
-        if world > 1:
-            import torch.distributed as dist
-            dist.barrier()
-        torch.cuda.synchronize()
-
-    L.tl_trace_reset()
-    L.tl_trace_enable(1)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(gpu_uuid(torch, dev)) as clk:
-        barrier()
-        e0.record(stream)
-        for _ in range(args.steps):
-            step(t)
-            t += 1
-        e1.record(stream)
-        barrier()
-    L.tl_trace_enable(0)
-    ms = e0.elapsed_time(e1)
-    kernels = {}
-    names = ctypes.create_string_buffer(4096)
-    _lib.check(L.tl_trace_names(names, 4096))
-    for nm in filter(None, names.value.decode().split(",")):
-        tot, cnt = ctypes.c_double(0), ctypes.c_longlong(0)
-        _lib.check(L.tl_trace_get(nm.encode(), ctypes.byref(tot), ctypes.byref(cnt)))
-        kernels[nm] = {"ms_total": tot.value, "launches": cnt.value}
-    if world > 1:
-        import torch.distributed as dist
-        tt = torch.tensor([ms], device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        ms = tt.item()
-    ms_step = ms / args.steps
-    value = n * BYTES_PER_ELEM / (ms_step * 1e-3) / 1e9
-
-    # ---- end to end through the C ABI with pinned host buffers
     e2e = None
     if not args.no_e2e:
-        e2e = e2e_adamw(args, torch, ops, dev, stream, world, rank, n, shard_n, p, g, m, v, norm, step, t)
+        steps = max(1, min(args.steps, 5))
+        hg = g.cpu().pin_memory()
+        hnorm = torch.zeros(1).pin_memory()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        rk.barrier()
+        e0.record(rk.stream)
+        for i in range(steps):
+            g.copy_(hg, non_blocking=True)
+            step(t0 + args.steps + i)
+            hnorm.copy_(norm, non_blocking=True)
+        e1.record(rk.stream)
+        rk.barrier()
+        ms = rk.max_over_ranks(e0.elapsed_time(e1)) / steps
+        e2e = {"value": round(n * BYTES_PER_PARAM / (ms * 1e-3) / 1e9, 3), "unit": "GB/s",
+               "h2d_bytes_per_step": g.numel() * 4 * world, "d2h_bytes_per_step": 4, "steps": steps,
+               "ms_per_step": round(ms, 3),
+               "path": "pinned host G -> tl_clip_adamw_step / tl_zero1_step -> host norm; P,M,V resident"}
 
-    # ---- roofline of the dominant kernel
     peaks, peak_kind = measured_peaks()
-    adam = kernels.get("adamw_vec", {"ms_total": 0, "launches": 0})
-    adam_ms = adam["ms_total"] / max(1, adam["launches"])
-    adam_elems = shard_n
-    achieved = adam_elems * ADAMW_BYTES_PER_ELEM / (adam_ms * 1e-3) / 1e9 if adam_ms > 0 else None
-    norm_k = kernels.get("sumsq", {"ms_total": 0, "launches": 0})
-    norm_ms = norm_k["ms_total"] / max(1, norm_k["launches"])
-    roofline = {"kernel": "adamw_vec", "bound": "hbm", "achieved": round(achieved, 1) if achieved else None,
-                "peak": peaks["hbm_gbs"], "peak_source": peak_kind, "unit": "GB/s",
-                "frac": round(achieved / peaks["hbm_gbs"], 4) if achieved else None,
-                "traffic": None, "algorithmic_bytes": adam_elems * ADAMW_BYTES_PER_ELEM,
-                "ms_per_launch": round(adam_ms, 4),
-                "sumsq": {"achieved": round(shard_n * NORM_BYTES_PER_ELEM / (norm_ms * 1e-3) / 1e9, 1)
-                          if norm_ms > 0 else None, "ms_per_launch": round(norm_ms, 4)}}
-    tr = committed_traffic("adamw_vec", "adamw" if world == 1 else f"adamw_zero1_{world}")
+    adam = kernels.get("adamw_vec", {"ms_per_launch": 0})
+    a_ms = adam["ms_per_launch"]
+    achieved = shard * ADAMW_BYTES / (a_ms * 1e-3) / 1e9 if a_ms else None
+    nk = kernels.get("sumsq", {"ms_per_launch": 0})
+    roofline = {"kernel": "adamw_vec", "bound": "hbm", "unit": "GB/s",
+                "achieved": round(achieved, 1) if achieved else None, "peak": peaks["hbm_gbs"],
+                "peak_source": f"{peak_kind} HBM copy", "frac": round(achieved / peaks["hbm_gbs"], 4) if achieved else None,
+                "traffic": None, "algorithmic_bytes": shard * ADAMW_BYTES,
+                "sumsq_gbs": round(shard * NORM_BYTES / (nk["ms_per_launch"] * 1e-3) / 1e9, 1) if nk["ms_per_launch"] else None}
+    tr = committed_traffic("adamw:adamw_vec" if world == 1 else f"adamw_zero1_{world}:adamw_vec")
     if tr:
         roofline["traffic"] = tr.get("bytes_per_launch")
         roofline["traffic_source"] = tr.get("source")
-
     launches = sum(k["launches"] for k in kernels.values())
-    out = None
-    if rank == 0:
-        clocks = clk.summary()
-        out = {"metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
-               "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
-               "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-               "data": "synthetic (seeded normals with config-2 distributions)",
-               "config": {"workload": "config2_fused_adamw_clip" if world == 1 else "config2_zero1_adamw",
-                          "n_params": n, "bytes_per_param": BYTES_PER_ELEM, "t_start": T0,
-                          "parallelism": "single" if world == 1 else f"zero1_dp{world}",
-                          "l2": "inputs 4 GiB >> 126 MB L2 (no flush needed)"},
-               "e2e": e2e, "roofline": roofline, "clocks": clocks, "gpu_launches": launches,
-               "kernels": kernels}
     if world > 1:
-        import torch.distributed as dist
         z.close()
-        dist.barrier()
-        dist.destroy_process_group()
-    return out
-
-
-def e2e_adamw(args, torch, ops, dev, stream, world, rank, n, shard_n, p, g, m, v, norm, step, t):
-    """Same step through the C ABI with the step's input in host memory.
-
-    Per step the input is the fresh gradient G (a training loop produces one per
-    step) and the result is the global norm: G goes host->device from pinned
-    memory, the optimizer step runs (tl_clip_adamw_step, or tl_zero1_step with
-    N ranks), and the norm comes back.  P, M and V are optimizer state and stay
-    resident, as they do in any GPU training run.  `all_host` repeats the
-    measurement with P, M and V also copied in and out every step (the literal
-    host-buffer form of the reference's adamw() call)."""
-    steps = max(1, min(args.steps, int(os.environ.get("TL_E2E_STEPS", "5"))))
-    hg = g.cpu().pin_memory()
-    hnorm = torch.zeros(1).pin_memory()
-    if world == 1:
-        state = [(p, p.cpu().pin_memory()), (m, m.cpu().pin_memory()), (v, v.cpu().pin_memory())]
-    else:
-        lo = rank * shard_n
-        ps = p[lo:lo + shard_n]
-        state = [(ps, ps.cpu().pin_memory()), (m, m.cpu().pin_memory()), (v, v.cpu().pin_memory())]
-
-    def timed(all_host):
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        if world > 1:
-            import torch.distributed as dist
-            dist.barrier()
-        torch.cuda.synchronize()
-        e0.record(stream)
-        for i in range(steps):
-            g.copy_(hg, non_blocking=True)
-            if all_host:
-                for d, h in state:
-                    d.copy_(h, non_blocking=True)
-            step(t + i)
-            if all_host:
-                for d, h in state:
-                    h.copy_(d, non_blocking=True)
-            hnorm.copy_(norm, non_blocking=True)
-        e1.record(stream)
-        torch.cuda.synchronize()
-        ms = e0.elapsed_time(e1)
-        if world > 1:
-            import torch.distributed as dist
-            tt = torch.tensor([ms], device=dev)
-            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-            ms = tt.item()
-        return ms / steps
-
-    ms_g = timed(False)
-    ms_all = timed(True)
-    st_bytes = sum(d.numel() * 4 for d, _ in state)
-    gb = lambda ms: round(n * BYTES_PER_ELEM / (ms * 1e-3) / 1e9, 3)
-    return {"value": gb(ms_g), "unit": "GB/s", "h2d_bytes_per_step": g.numel() * 4, "d2h_bytes_per_step": 4,
-            "steps": steps, "ms_per_step": round(ms_g, 3),
-            "path": "pinned host G -> tl_clip_adamw_step / tl_zero1_step -> host norm; P,M,V resident",
-            "all_host": {"value": gb(ms_all), "ms_per_step": round(ms_all, 3),
-                         "h2d_bytes_per_step": g.numel() * 4 + st_bytes, "d2h_bytes_per_step": st_bytes + 4}}
+    del p, g, m, v
+    torch.cuda.empty_cache()
+    return {"metric": ADAMW_METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded normals with config-2 distributions)",
+            "config": {"workload": "config2_fused_adamw_clip" if world == 1 else "config2_zero1_adamw",
+                       "n_params": n, "bytes_per_param": BYTES_PER_PARAM, "t_start": ADAMW_T0,
+                       "parallelism": "single" if world == 1 else f"zero1_dp{world}",
+                       "l2": "inputs 4 GiB >> 126 MB L2 (no flush needed)"},
+            "e2e": e2e, "roofline": roofline, "clocks": clocks, "gpu_launches": launches, "kernels": kernels}
 
 
 def main():
@@ -385,32 +527,63 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return 0
-        if args.workload != "adamw":
-            emit({"impl": "reference", "unavailable": "reference arm implemented for the adamw workload only"})
-            return 0
         import oracle
         if not oracle.has_ref():
             emit({"impl": "reference", "unavailable": "oracle/_ref/libtlref.so not built (needs the reference sources at build time)"})
             return 0
-        gbs, sec, threads = run_reference_adamw(args.n, args.steps, args.warmup)
-        emit({"impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s",
-              "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(sec * 1e3, 3),
+        if args.workload == "adamw":
+            gbs, sec, threads = reference_adamw(args.n, args.steps, args.warmup)
+            emit({"impl": "reference", "metric": ADAMW_METRIC, "value": round(gbs, 3), "unit": "GB/s",
+                  "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(sec * 1e3, 3),
+                  "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+                  "data": "synthetic (numpy default_rng(0), config-2 distributions)",
+                  "config": {"workload": "config2_fused_adamw_clip", "n_params": args.n,
+                             "parallelism": f"cpu_omp{threads}"},
+                  "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "reference",
+                                   "sample": f"tinylm.c adamw+global_gradnorm, n={args.n}, median of {args.steps} steps"},
+                  "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
+            return 0
+        tps, sec, threads, B = reference_train(args.workload, args.steps, args.warmup)
+        preset, n_mtp, B_glob, _, _, cfg_name = TRAIN[args.workload]
+        emit({"impl": "reference", "metric": TRAIN_METRIC, "value": round(tps, 2), "unit": "tokens/s",
+              "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(sec * 1e3, 2),
               "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-              "data": "synthetic (numpy default_rng(0), config-2 distributions)",
-              "config": {"workload": "config2_fused_adamw_clip", "n_params": args.n,
-                         "bytes_per_param": BYTES_PER_ELEM, "t_start": T0, "parallelism": f"cpu_omp{threads}"},
-              "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "reference",
-                               "sample": f"tinylm.c adamw+global_gradnorm on the full n, median of {args.steps} steps"},
-              "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
+              "data": "synthetic (reference xorshift tokens, seed 0)",
+              "config": {"workload": cfg_name, "model": preset, "n_mtp": n_mtp, "global_batch": B_glob,
+                         "seq_len": T_CTX, "parallelism": f"cpu_omp{threads}"},
+              "cpu_baseline": {"value": round(tps, 2), "unit": "tokens/s", "cores": threads, "kind": "reference",
+                               "sample": f"tinylm.c forward+backward+gradnorm+adamw at batch {B}x{T_CTX} "
+                                         f"(per-token work of the config), median of {args.steps} steps"},
+              "e2e": {"value": round(tps, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
         return 0
 
-    out = run_ours_adamw(args, rank, world, local)
-    if rank == 0 and out is not None:
-        if world == 1 and not args.no_cpu_baseline:
-            import torch
-            torch.cuda.empty_cache()
-            out["cpu_baseline"] = cpu_baseline_adamw(args.n)
+    rk = Run(rank, world, local)
+    if args.workload == "adamw":
+        out = run_adamw(args, rk, args.n)
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            steps = int(os.environ.get("TL_CPU_BASELINE_STEPS", "5"))
+            gbs, sec, threads = reference_adamw(args.n, steps, 1)
+            out["cpu_baseline"] = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "reference",
+                                   "sample": f"tinylm.c adamw+global_gradnorm (oracle/_ref), n={args.n}, median of {steps} steps"}
+    else:
+        out = run_train(args, rk)
+        if world == 1 and not args.no_adamw_line:
+            a = run_adamw(argparse.Namespace(warmup=3, steps=20, no_e2e=True), rk, ADAMW_N)
+            if rank == 0:
+                out.setdefault("fused_adamw", {}).update(
+                    {"config2_gbs": a["value"], "config2_adamw_kernel_gbs": a["roofline"]["achieved"],
+                     "config2_frac_of_hbm": a["roofline"]["frac"], "config2_ms_per_step": a["ms_per_step"],
+                     "metric": ADAMW_METRIC})
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            steps = int(os.environ.get("TL_CPU_BASELINE_STEPS", "1"))
+            tps, sec, threads, B = reference_train(args.workload, steps, 1)
+            out["cpu_baseline"] = {"value": round(tps, 2), "unit": "tokens/s", "cores": threads, "kind": "reference",
+                                   "sample": f"tinylm.c step at batch {B}x{T_CTX} (same per-token work), "
+                                             f"median of {steps} step(s) after 1 warm-up",
+                                   "s_per_step": round(sec, 3)}
+    if rank == 0:
         emit(out)
+    rk.close()
     return 0
 
 

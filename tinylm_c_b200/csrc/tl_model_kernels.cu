@@ -9,6 +9,7 @@
 // Reductions that feed parameters (RMSNorm gains) and the loss use a fixed
 // order, so they do not depend on scheduling.
 #include "tl_model.cuh"
+#include "tl_trace.cuh"
 
 namespace tl {
 namespace mk {
@@ -493,22 +494,26 @@ int mk_setup(int device) {
 #define MK_LAUNCH_CHECK() TL_TRY_CUDA(cudaGetLastError())
 
 int k_embed_fwd(DeviceCtx *c, const float *emb, const int *tok, float *out, int N, int D, int V) {
+  TraceScope ts(c, "k_embed_fwd");
   mk::embed_fwd_kernel<<<N, 128, 0, c->stream>>>(emb, tok, out, N, D, V, c->err_flag);
   MK_LAUNCH_CHECK();
   return TL_OK;
 }
 int k_embed_bwd(DeviceCtx *c, float *gemb, const int *tok, const float *dout, int N, int D, int V) {
+  TraceScope ts(c, "k_embed_bwd");
   mk::embed_bwd_kernel<<<N, 128, 0, c->stream>>>(gemb, tok, dout, N, D, V);
   MK_LAUNCH_CHECK();
   return TL_OK;
 }
 int k_rmsnorm_fwd(DeviceCtx *c, const float *x, const float *g, float *out, float *rinv, int rows, int D) {
+  TraceScope ts(c, "k_rmsnorm_fwd");
   mk::rmsnorm_fwd_kernel<<<(rows + 7) / 8, 256, 0, c->stream>>>(x, g, out, rinv, rows, D);
   MK_LAUNCH_CHECK();
   return TL_OK;
 }
 int k_rmsnorm_bwd(DeviceCtx *c, const float *x, const float *g, const float *rinv, const float *dy, float *dx,
                   float *dg, float *part, int part_rows, int rows, int D) {
+  TraceScope ts(c, "k_rmsnorm_bwd");
   int nb = (rows + 7) / 8;
   if (nb > part_rows) nb = part_rows;
   mk::rmsnorm_bwd_kernel<<<nb, 256, sizeof(float) * 8 * D, c->stream>>>(x, g, rinv, dy, dx, part, rows, D);
@@ -518,53 +523,63 @@ int k_rmsnorm_bwd(DeviceCtx *c, const float *x, const float *g, const float *rin
   return TL_OK;
 }
 int k_rope(DeviceCtx *c, float *buf, const float *cosT, const float *sinT, int rows, int nh, int hd, int T, int back) {
+  TraceScope ts(c, "k_rope");
   const size_t n = (size_t)rows * nh * (hd / 2);
   mk::rope_kernel<<<grid_for(n, 256, 16, c->num_sms), 256, 0, c->stream>>>(buf, cosT, sinT, rows, nh, hd, T, back);
   MK_LAUNCH_CHECK();
   return TL_OK;
 }
 int k_add(DeviceCtx *c, float *y, const float *x, size_t n) {
+  TraceScope ts(c, "k_add");
   mk::add_inplace_kernel<<<grid_for(n, 256, 16, c->num_sms), 256, 0, c->stream>>>(y, x, n);
   MK_LAUNCH_CHECK();
   return TL_OK;
 }
 int k_swiglu_fwd(DeviceCtx *c, const float *g, const float *u, float *act, size_t n) {
+  TraceScope ts(c, "k_swiglu_fwd");
   mk::swiglu_fwd_kernel<<<grid_for(n, 256, 16, c->num_sms), 256, 0, c->stream>>>(g, u, act, n);
   MK_LAUNCH_CHECK();
   return TL_OK;
 }
 int k_swiglu_bwd(DeviceCtx *c, const float *g, const float *u, const float *dact, float *dg, float *du, size_t n) {
+  TraceScope ts(c, "k_swiglu_bwd");
   mk::swiglu_bwd_kernel<<<grid_for(n, 256, 16, c->num_sms), 256, 0, c->stream>>>(g, u, dact, dg, du, n);
   MK_LAUNCH_CHECK();
   return TL_OK;
 }
 int k_mtp_hk(DeviceCtx *c, const float *fn, const float *t1, float *hk, size_t n) {
+  TraceScope ts(c, "k_mtp_hk");
   mk::mtp_hk_kernel<<<grid_for(n, 256, 16, c->num_sms), 256, 0, c->stream>>>(fn, t1, hk, n);
   MK_LAUNCH_CHECK();
   return TL_OK;
 }
 int k_mtp_bwd(DeviceCtx *c, const float *t1, const float *dhk, float *dfn, float *dt1, size_t n) {
+  TraceScope ts(c, "k_mtp_bwd");
   mk::mtp_bwd_kernel<<<grid_for(n, 256, 16, c->num_sms), 256, 0, c->stream>>>(t1, dhk, dfn, dt1, n);
   MK_LAUNCH_CHECK();
   return TL_OK;
 }
 int k_softmax_ce(DeviceCtx *c, float *logits, const int *tgt, int N, int V, float scale, double *loss_rows) {
+  TraceScope ts(c, "k_softmax_ce");
   mk::softmax_ce_kernel<<<N, 256, 0, c->stream>>>(logits, tgt, V, scale, loss_rows);
   MK_LAUNCH_CHECK();
   return TL_OK;
 }
 int k_loss_sum(DeviceCtx *c, const double *rows, int N, double *acc) {
+  TraceScope ts(c, "k_loss_sum");
   mk::loss_sum_kernel<<<1, 1024, 0, c->stream>>>(rows, N, acc);
   MK_LAUNCH_CHECK();
   return TL_OK;
 }
 int k_loss_final(DeviceCtx *c, const double *acc, double denom, float *out) {
+  TraceScope ts(c, "k_loss_final");
   mk::loss_final_kernel<<<1, 1, 0, c->stream>>>(acc, denom, out);
   MK_LAUNCH_CHECK();
   return TL_OK;
 }
 int k_attn_fwd(DeviceCtx *c, const float *q, const float *k, const float *v, float *out, float *lse, int B, int T,
                int H, int KV, int hd) {
+  TraceScope ts(c, "k_attn_fwd");
   const float scale = 1.0f / sqrtf((float)hd);
   mk::attn_fwd_kernel<<<B * H, 512, attn_smem_fwd(T, hd), c->stream>>>(q, k, v, out, lse, T, H, KV, hd, scale);
   MK_LAUNCH_CHECK();
@@ -572,6 +587,7 @@ int k_attn_fwd(DeviceCtx *c, const float *q, const float *k, const float *v, flo
 }
 int k_attn_bwd(DeviceCtx *c, const float *q, const float *k, const float *v, const float *out, const float *dout,
                const float *lse, float *Drow, float *dq, float *dk, float *dv, int B, int T, int H, int KV, int hd) {
+  TraceScope ts(c, "k_attn_bwd");
   const float scale = 1.0f / sqrtf((float)hd);
   mk::attn_bwd_dq_kernel<<<B * H, 256, attn_smem_dq(T, hd), c->stream>>>(q, k, v, out, dout, lse, dq, Drow, T, H,
                                                                          KV, hd, scale);
