@@ -35,6 +35,9 @@ import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
+# NCCL prints its version banner on stdout unless told otherwise; rank 0's
+# stdout must carry exactly one JSON line.
+os.environ.setdefault("NCCL_DEBUG", "WARN")
 
 T_CTX = 256
 LR, B1, B2, WD, MAX_NORM = 3e-4, 0.9, 0.95, 0.1, 1.0
