@@ -63,12 +63,14 @@ def parse():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=list(TRAIN) + ["adamw"], default="train")
+    ap.add_argument("--workload", choices=list(TRAIN) + ["adamw", "gemm"], default="train")
     ap.add_argument("--n", type=int, default=ADAMW_N, help="adamw workload: elements per buffer")
     ap.add_argument("--batch", type=int, default=0, help="train workloads: global batch (0 = the config's)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-adamw-line", action="store_true", help="train: skip the config-2 AdamW sub-measurement")
+    ap.add_argument("--shape", default="", help="gemm workload: one M,K,N instead of the sweep")
+    ap.add_argument("--op", default="all", choices=["all", "mm", "mm_bt", "mm_atb"], help="gemm workload: primitive")
     return ap.parse_args()
 
 
@@ -524,6 +526,102 @@ def run_adamw(args, rk, n):
             "e2e": e2e, "roofline": roofline, "clocks": clocks, "gpu_launches": launches, "kernels": kernels}
 
 
+# ------------------------------------------------------------- gemm (cfg 3)
+GEMM_SWEEP_M = (16384, 65536)
+GEMM_SWEEP_KN = (256, 512, 1024, 2816)
+GEMM_METRIC = "GEMM fp32 TFLOP/s (3xTF32 tensor cores), BASELINE config-3 sweep"
+
+
+def gemm_shapes(args):
+    if args.shape:
+        M, K, N = (int(x) for x in args.shape.split(","))
+        return [(M, K, N)]
+    return [(M, K, N) for M in GEMM_SWEEP_M for K in GEMM_SWEEP_KN for N in GEMM_SWEEP_KN]
+
+
+def run_gemm(args, rk):
+    """X@W, X@W^T, X^T@W over the config-3 sweep (X~N(0,1), W~N(0,0.02),
+    dY~N(0,1)); per shape and primitive: warm-up, then K timed calls."""
+    torch, ops = rk.torch, rk.ops
+    dev = rk.dev
+    ops_sel = ["mm", "mm_bt", "mm_atb"] if args.op == "all" else [args.op]
+    results = []
+    tot_flop = tot_ms = 0.0
+    launches = 0
+    clocks_all = []
+    for (M, K, N) in gemm_shapes(args):
+        g = torch.Generator(device=dev).manual_seed(M + K + N)
+        X = torch.randn(M * K, device=dev, generator=g)
+        W = torch.randn(K * N, device=dev, generator=g) * 0.02
+        dY = torch.randn(M * N, device=dev, generator=g)
+        out = {"mm": torch.empty(M * N, device=dev), "mm_bt": torch.zeros(M * K, device=dev),
+               "mm_atb": torch.zeros(K * N, device=dev)}
+        fns = {"mm": lambda: ops.mm(out["mm"], X, W, M, K, N),
+               "mm_bt": lambda: ops.mm_bt(out["mm_bt"], dY, W, M, K, N),
+               "mm_atb": lambda: ops.mm_atb(out["mm_atb"], X, dY, M, K, N)}
+        for op in ops_sel:
+            for _ in range(args.warmup):
+                fns[op]()
+            torch.cuda.synchronize()
+            ms, kernels, clocks = rk.timed(lambda t, f=fns[op]: f(), args.steps, 0)
+            rk.status()
+            flop = 2.0 * M * K * N
+            results.append({"op": op, "M": M, "K": K, "N": N, "ms": round(ms, 4),
+                            "tflops": round(flop / (ms * 1e-3) / 1e12, 2),
+                            "engine": ops.last_gemm_engine()})
+            tot_flop += flop
+            tot_ms += ms
+            launches += sum(k["launches"] for k in kernels.values())
+            if clocks.get("sm_mhz"):
+                clocks_all.append(clocks)
+        del X, W, dY, out
+        torch.cuda.empty_cache()
+    peaks, peak_kind = measured_peaks()
+    bf16 = peaks.get("bf16_tflops", 0)
+    peak = bf16 / 6.0
+    agg = tot_flop / (tot_ms * 1e-3) / 1e12
+    best = max(results, key=lambda r: r["tflops"])
+    return {"metric": GEMM_METRIC, "value": round(agg, 2), "unit": "TFLOP/s", "n_gpus": rk.world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(tot_ms / max(1, len(results)), 4),
+            "higher_is_better": True, "scaling": "replicas", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (X~N(0,1), W~N(0,0.02), dY~N(0,1), seeded)",
+            "config": {"workload": "config3_gemm_sweep" if not args.shape else "config3_gemm_one",
+                       "shapes": len(results), "value_is": "total FLOP / total time over the sweep"},
+            "roofline": {"kernel": "gemm_tc (tcgen05 3xTF32)", "bound": "tensor", "unit": "TFLOP/s",
+                         "achieved": round(agg, 2), "best_shape": best, "peak": round(peak, 1),
+                         "peak_source": f"{peak_kind} bf16 burst {bf16} TFLOP/s / 6 (tf32 = bf16/2; 3 tf32 MMAs per fp32 product)",
+                         "frac": round(agg / peak, 4) if peak else None, "traffic": None},
+            "clocks": clocks_all[-1] if clocks_all else {}, "gpu_launches": launches, "sweep": results}
+
+
+def reference_gemm(args):
+    """The reference's mm/mm_bt/mm_atb (tinylm.c:439-537) on a row sample of
+    the sweep (M scaled down to 1024 rows; per-row work identical)."""
+    import numpy as np
+    import oracle
+    R = oracle.ref()
+    threads = cpu_threads()
+    R.tlref_init(threads, 0)
+    tot_flop = tot_s = 0.0
+    shapes = gemm_shapes(args)
+    for (M, K, N) in shapes[: (1 if args.shape else len(shapes))]:
+        Ms = min(M, 1024)
+        rng = np.random.default_rng(0)
+        X = rng.standard_normal(Ms * K, dtype=np.float32)
+        W = rng.standard_normal(K * N, dtype=np.float32) * np.float32(0.02)
+        dY = rng.standard_normal(Ms * N, dtype=np.float32)
+        Y = np.empty(Ms * N, np.float32); dX = np.zeros(Ms * K, np.float32); dW = np.zeros(K * N, np.float32)
+        fp = oracle.fptr
+        for fn in (lambda: R.tlref_mm(fp(Y), fp(X), fp(W), Ms, K, N),
+                   lambda: R.tlref_mm_bt(fp(dX), fp(dY), fp(W), Ms, K, N),
+                   lambda: R.tlref_mm_atb(fp(dW), fp(X), fp(dY), Ms, K, N)):
+            t0 = time.perf_counter()
+            fn()
+            tot_s += time.perf_counter() - t0
+            tot_flop += 2.0 * Ms * K * N
+    return tot_flop / tot_s / 1e12, threads
+
+
 def main():
     args = parse()
     rank, world, local = dist_env()
@@ -533,6 +631,16 @@ def main():
         import oracle
         if not oracle.has_ref():
             emit({"impl": "reference", "unavailable": "oracle/_ref/libtlref.so not built (needs the reference sources at build time)"})
+            return 0
+        if args.workload == "gemm":
+            tf, threads = reference_gemm(args)
+            emit({"impl": "reference", "metric": GEMM_METRIC, "value": round(tf, 4), "unit": "TFLOP/s",
+                  "n_gpus": world, "steps": 1, "warmup": 0, "higher_is_better": True, "scaling": "replicas",
+                  "vs_baseline": None, "dtype": "f32", "data": "synthetic (numpy default_rng(0))",
+                  "config": {"workload": "config3_gemm_sweep", "parallelism": f"cpu_omp{threads}"},
+                  "cpu_baseline": {"value": round(tf, 4), "unit": "TFLOP/s", "cores": threads, "kind": "reference",
+                                   "sample": "tinylm.c mm/mm_bt/mm_atb on every sweep shape with M cut to 1024 rows"},
+                  "e2e": {"value": round(tf, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
             return 0
         if args.workload == "adamw":
             gbs, sec, threads = reference_adamw(args.n, args.steps, args.warmup)
@@ -561,7 +669,13 @@ def main():
         return 0
 
     rk = Run(rank, world, local)
-    if args.workload == "adamw":
+    if args.workload == "gemm":
+        out = run_gemm(args, rk)
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            tf, threads = reference_gemm(args)
+            out["cpu_baseline"] = {"value": round(tf, 4), "unit": "TFLOP/s", "cores": threads, "kind": "reference",
+                                   "sample": "tinylm.c mm/mm_bt/mm_atb with M cut to 1024 rows"}
+    elif args.workload == "adamw":
         out = run_adamw(args, rk, args.n)
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
             steps = int(os.environ.get("TL_CPU_BASELINE_STEPS", "5"))

@@ -27,7 +27,10 @@ struct DeviceCtx {
   double *sumsq = nullptr;             // [1] scratch for tl_grad_norm
   float *scalars = nullptr;            // [4] scratch: norm, gscale
   int *err_flag = nullptr;             // device error word set by bounded waits
+  float *gemm_ws = nullptr;            // split-K partial outputs
+  size_t gemm_ws_floats = 0;
 };
+constexpr size_t kGemmWorkspaceFloats = 16u << 20;  // 64 MiB
 
 DeviceCtx *ctx();                          // context of the current device, or null
 int set_error(int code, const char *fmt, ...);

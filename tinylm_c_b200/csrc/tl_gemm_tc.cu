@@ -30,6 +30,7 @@
 // winds down (the MMA thread still waits, bounded, for its own MMAs; TMEM is
 // always released).
 #include <cuda.h>
+#include <algorithm>
 #include <cudaTypedefs.h>
 #include "tl_gemm.cuh"
 #include "tl_trace.cuh"
@@ -146,6 +147,8 @@ __device__ __forceinline__ float tf32_hi(float x) {
 struct Params {
   float *C;
   int I, J, R, ldc, beta;
+  int kb_per_split;      // k-blocks per CTA along grid z (split-K)
+  size_t split_stride;   // floats between the partial outputs of consecutive splits
   int *err;
 };
 
@@ -162,8 +165,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int i0 = blockIdx.y * BM, j0 = blockIdx.x * BN;
-  const int nk = (p.R + BK - 1) / BK;
+  // Split-K: CTA z reduces k-blocks [kb0, kb0 + nk) and writes its own
+  // output slice (a partial when the grid has more than one z).
+  const int nk_all = (p.R + BK - 1) / BK;
+  const int kb0 = blockIdx.z * p.kb_per_split;
+  const int nk = max(0, min(nk_all - kb0, p.kb_per_split));
   const int nchunks = (nk + CHUNK_KB - 1) / CHUNK_KB;
+  float *const Cout = p.C + (size_t)blockIdx.z * p.split_stride;
   const uint32_t smem_base = smem_u32(smem);
   auto bar_full = [&](int s) { return smem_u32(&bars[s]); };
   auto bar_ready = [&](int s) { return smem_u32(&bars[STAGES + s]); };
@@ -205,7 +213,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         issued = kb + 1;
         const uint32_t st = smem_base + s * STAGE_BYTES;
         mbar_arrive_expect_tx(bar_full(s), TX_BYTES);
-        const int k0 = kb * BK;
+        const int k0 = (kb0 + kb) * BK;
         if (A_MN) {
 #pragma unroll
           for (int b = 0; b < BM / 32; b++) tma_load_2d(st + OFF_AHI + b * 4096, &tmA, bar_full(s), i0 + 32 * b, k0);
@@ -346,7 +354,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     if (ok) {
       const int row = i0 + q * 32 + lane;
       if (row < p.I) {
-        float *dst = p.C + (size_t)row * p.ldc + j0;
+        float *dst = Cout + (size_t)row * p.ldc + j0;
         if (j0 + BN <= p.J) {
 #pragma unroll
           for (int e = 0; e < BN; e += 4) {
@@ -407,15 +415,37 @@ static int make_map(CUtensorMap *m, const float *ptr, uint64_t inner, uint64_t o
   return TL_OK;
 }
 
+// C[i, j] = beta*C[i, j] + sum_z ws[z][i][j], partials summed in z order.
+__global__ void splitk_reduce_kernel(float *__restrict__ C, int ldc, int beta, const float *__restrict__ ws,
+                                     int splits, int I, int J) {
+  const size_t total4 = (size_t)I * J / 4;
+  const size_t stride = (size_t)I * J;
+  for (size_t q = (size_t)blockIdx.x * blockDim.x + threadIdx.x; q < total4; q += (size_t)gridDim.x * blockDim.x) {
+    const size_t e = q * 4;
+    const int i = (int)(e / J), j = (int)(e % J);
+    float4 acc = reinterpret_cast<const float4 *>(ws)[q];
+    for (int z = 1; z < splits; z++) {
+      const float4 w = reinterpret_cast<const float4 *>(ws + z * stride)[q];
+      acc.x += w.x; acc.y += w.y; acc.z += w.z; acc.w += w.w;
+    }
+    float4 *dst = reinterpret_cast<float4 *>(C + (size_t)i * ldc + j);
+    if (beta) {
+      const float4 o = *dst;
+      acc.x += o.x; acc.y += o.y; acc.z += o.z; acc.w += o.w;
+    }
+    *dst = acc;
+  }
+}
+
 template <bool A_MN, bool B_MN>
-static int launch(DeviceCtx *c, const CUtensorMap &ma, const CUtensorMap &mb, const Params &p) {
+static int launch(DeviceCtx *c, const CUtensorMap &ma, const CUtensorMap &mb, const Params &p, int splits) {
   static bool attr_set[kMaxDevices] = {};
   if (!attr_set[c->device]) {
     TL_TRY_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<A_MN, B_MN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      SMEM_BYTES));
     attr_set[c->device] = true;
   }
-  dim3 grid((p.J + BN - 1) / BN, (p.I + BM - 1) / BM);
+  dim3 grid((p.J + BN - 1) / BN, (p.I + BM - 1) / BM, splits);
   TraceScope ts(c, "gemm_tc");
   gemm_tc_kernel<A_MN, B_MN><<<grid, NUM_THREADS, SMEM_BYTES, c->stream>>>(ma, mb, p);
   TL_TRY_CUDA(cudaGetLastError());
@@ -443,25 +473,64 @@ int gemm_tc(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, i
   gemm_dims(op, M, K, N, &I, &J, &R);
   tc::Params p;
   p.C = C; p.I = I; p.J = J; p.R = R; p.err = c->err_flag;
+  // Split-K when the output has too few tiles to fill the GPU (e.g. weight
+  // gradients of narrow layers, whose reduction runs over all tokens): each
+  // split gets at least one TMEM chunk of k-blocks, partials go to the
+  // context's workspace and a fixed-order reduction adds them into C.
+  const int tiles = ((I + tc::BM - 1) / tc::BM) * ((J + tc::BN - 1) / tc::BN);
+  const int nk = (R + tc::BK - 1) / tc::BK;
+  int splits = 1;
+  if (tiles < c->num_sms && c->gemm_ws) {
+    splits = c->num_sms / tiles;
+    splits = std::min(splits, nk / tc::CHUNK_KB);
+    splits = std::min(splits, 16);
+    const size_t cap = c->gemm_ws_floats / ((size_t)I * J);
+    splits = (int)std::min<size_t>((size_t)splits, cap);
+    if (splits < 2) splits = 1;
+  }
+  int kb_per = nk;
+  if (splits > 1) {
+    kb_per = (nk + splits - 1) / splits;
+    kb_per = (kb_per + tc::CHUNK_KB - 1) / tc::CHUNK_KB * tc::CHUNK_KB;
+    splits = (nk + kb_per - 1) / kb_per;
+  }
+  p.kb_per_split = kb_per;
+  int out_ldc = 0, out_beta = 0;
   CUtensorMap ma, mb;
   switch (op) {
     case GemmOp::NN:  // A = X[M,K] K-major; B = W[K,N] MN-major
-      p.ldc = N; p.beta = 0;
+      out_ldc = N; out_beta = 0;
       if ((rc = tc::make_map(&ma, A, K, M, K, 32, tc::BM, false))) return rc;
       if ((rc = tc::make_map(&mb, B, N, K, N, 32, 32, true))) return rc;
-      return tc::launch<false, true>(c, ma, mb, p);
+      break;
     case GemmOp::NT:  // A = dY[M,N] K-major; B(r=n, j=k) = W[k*N+n] K-major
-      p.ldc = K; p.beta = 1;
+      out_ldc = K; out_beta = 1;
       if ((rc = tc::make_map(&ma, A, N, M, N, 32, tc::BM, false))) return rc;
       if ((rc = tc::make_map(&mb, B, N, K, N, 32, tc::BN, false))) return rc;
-      return tc::launch<false, false>(c, ma, mb, p);
+      break;
     case GemmOp::TN:  // A(i=k, r=m) = X[m*K+k] MN-major; B = dY[M,N] MN-major
-      p.ldc = N; p.beta = 1;
+      out_ldc = N; out_beta = 1;
       if ((rc = tc::make_map(&ma, A, K, M, K, 32, 32, true))) return rc;
       if ((rc = tc::make_map(&mb, B, N, M, N, 32, 32, true))) return rc;
-      return tc::launch<true, true>(c, ma, mb, p);
+      break;
   }
-  return set_error(TL_EINVAL, "unknown GEMM op");
+  if (splits > 1) {
+    p.C = c->gemm_ws; p.ldc = J; p.beta = 0; p.split_stride = (size_t)I * J;
+  } else {
+    p.ldc = out_ldc; p.beta = out_beta; p.split_stride = 0;
+  }
+  switch (op) {
+    case GemmOp::NN: rc = tc::launch<false, true>(c, ma, mb, p, splits); break;
+    case GemmOp::NT: rc = tc::launch<false, false>(c, ma, mb, p, splits); break;
+    case GemmOp::TN: rc = tc::launch<true, true>(c, ma, mb, p, splits); break;
+  }
+  if (rc || splits == 1) return rc;
+  TraceScope ts(c, "gemm_splitk_reduce");
+  const size_t q = (size_t)I * J / 4;
+  unsigned blocks = (unsigned)std::min<size_t>((q + 255) / 256, (size_t)c->num_sms * 8);
+  tc::splitk_reduce_kernel<<<blocks, 256, 0, c->stream>>>(C, out_ldc, out_beta, c->gemm_ws, splits, I, J);
+  TL_TRY_CUDA(cudaGetLastError());
+  return TL_OK;
 }
 
 }  // namespace tl
