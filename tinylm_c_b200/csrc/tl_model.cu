@@ -270,9 +270,10 @@ TL_API int tl_model_create(const int *cfg8, int micro_batch, void **handle) {
     delete m;
     return rc0;
   }
-  if (m->T > ATT_TMAX || m->hd > ATT_HDMAX || m->hd % 2) {
+  if (m->T > ATT_TMAX || m->T % 64 || m->hd > ATT_HDMAX || m->hd % 4) {
     delete m;
-    return set_error(TL_EINVAL, "attention supports T <= %d and even head_dim <= %d", ATT_TMAX, ATT_HDMAX);
+    return set_error(TL_EINVAL, "attention supports T <= %d (a multiple of 64) and head_dim <= %d (a multiple of 4)",
+                     ATT_TMAX, ATT_HDMAX);
   }
   m->mb = micro_batch > 0 ? micro_batch : 1;
   m->N = m->mb * m->T;

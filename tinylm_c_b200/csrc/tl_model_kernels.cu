@@ -249,213 +249,300 @@ __global__ void loss_final_kernel(const double *__restrict__ acc, double denom, 
 }
 
 // ---------------------------------------------------------------- attention
-// Causal GQA attention, T <= ATT_TMAX, head_dim <= ATT_HDMAX.  Layout as the
-// reference: q/out [B*T][H*hd], k/v [B*T][KV*hd]; query head h reads kv head
-// h / (H/KV).  Softmax of scale*q.k over keys s <= t.
+// Causal GQA attention in 64x64 tiles, fp32 on the CUDA cores with register
+// tiling (FlashAttention-style: online softmax forward, recomputed scores in
+// the backward).  Layout as the reference: q/out [B*T][H*hd], k/v
+// [B*T][KV*hd]; query head h reads kv head h / (H/KV); softmax of scale*q.k
+// over keys s <= t (tinylm.c:698-783).  Requires T % 64 == 0, hd <= 64 and
+// hd % 4 == 0; head dims below 64 are zero-padded in shared memory.
+//
+// 256 threads as a 16x16 grid; thread (ty, tx) owns rows ty*4..ty*4+3 and
+// columns tx*4..tx*4+3 of every 64x64 tile.  A 16-thread row group lives in
+// one half-warp, so row reductions are 4 xor-shuffles.
+constexpr int AT = 64;        // tile edge
+constexpr int ALD = 68;       // padded row stride of shared tiles (16-byte aligned)
+constexpr int ATILE = AT * ALD;
 
-// Forward: one CTA per (b, h), 16 warps, a warp per query row (interleaved
-// rows for causal balance).  K is held transposed in shared memory so lanes
-// (over keys) read it without bank conflicts; V row-major for lanes over d.
-// Also stores the row log-sum-exp for the backward pass.
-__global__ void __launch_bounds__(512)
+// acc[i][j] += sum_k A^T[k][ty*4+i] * B[k][tx*4+j]   (A^T and B in shared memory)
+__device__ __forceinline__ void mm64(float acc[4][4], const float *__restrict__ At, const float *__restrict__ Bm,
+                                     int kd, int ty, int tx) {
+#pragma unroll 8
+  for (int k = 0; k < kd; k++) {
+    const float4 a = *reinterpret_cast<const float4 *>(At + k * ALD + ty * 4);
+    const float4 b = *reinterpret_cast<const float4 *>(Bm + k * ALD + tx * 4);
+    const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+      for (int j = 0; j < 4; j++) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+  }
+}
+// Two products sharing the k loop: acc1 += A1^T B1, acc2 += A2^T B2.
+__device__ __forceinline__ void mm64x2(float c1[4][4], float c2[4][4], const float *__restrict__ A1,
+                                       const float *__restrict__ B1, const float *__restrict__ A2,
+                                       const float *__restrict__ B2, int kd, int ty, int tx) {
+#pragma unroll 4
+  for (int k = 0; k < kd; k++) {
+    const float4 a = *reinterpret_cast<const float4 *>(A1 + k * ALD + ty * 4);
+    const float4 b = *reinterpret_cast<const float4 *>(B1 + k * ALD + tx * 4);
+    const float4 e = *reinterpret_cast<const float4 *>(A2 + k * ALD + ty * 4);
+    const float4 f = *reinterpret_cast<const float4 *>(B2 + k * ALD + tx * 4);
+    const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+    const float ev[4] = {e.x, e.y, e.z, e.w}, fv[4] = {f.x, f.y, f.z, f.w};
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        c1[i][j] = fmaf(av[i], bv[j], c1[i][j]);
+        c2[i][j] = fmaf(ev[i], fv[j], c2[i][j]);
+      }
+  }
+}
+__device__ __forceinline__ void zero44(float a[4][4]) {
+#pragma unroll
+  for (int i = 0; i < 4; i++)
+#pragma unroll
+    for (int j = 0; j < 4; j++) a[i][j] = 0.0f;
+}
+// 64 rows x hd columns of a [rows][ld] global array (row r0, column c0) into
+// shared memory, row-major (dst[r][c]) or transposed (dst[c][r]); columns
+// hd..63 are zero.
+__device__ __forceinline__ void load_tile(float *__restrict__ dst, const float *__restrict__ src, size_t ld,
+                                          int hd, bool transpose) {
+  const int nq = AT * (AT / 4);  // float4 slots of a 64x64 tile
+  for (int idx = threadIdx.x; idx < nq; idx += blockDim.x) {
+    const int r = idx / (AT / 4), c4 = (idx % (AT / 4)) * 4;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (c4 < hd) v = *reinterpret_cast<const float4 *>(src + (size_t)r * ld + c4);
+    if (!transpose) {
+      *reinterpret_cast<float4 *>(dst + r * ALD + c4) = v;
+    } else {
+      dst[(c4 + 0) * ALD + r] = v.x; dst[(c4 + 1) * ALD + r] = v.y;
+      dst[(c4 + 2) * ALD + r] = v.z; dst[(c4 + 3) * ALD + r] = v.w;
+    }
+  }
+}
+__device__ __forceinline__ float hsum16(float v) {
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float hmax16(float v) {
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Forward: CTA per (b, h, 64-row query tile); online softmax over key tiles
+// 0..qt.  Writes out and the row log-sum-exp.
+__global__ void __launch_bounds__(256)
 attn_fwd_kernel(const float *__restrict__ q, const float *__restrict__ k, const float *__restrict__ v,
                 float *__restrict__ out, float *__restrict__ lse, int T, int H, int KV, int hd, float scale) {
   extern __shared__ float sm[];
-  const int TP = T + 1;
-  float *Kt = sm;                     // [hd][T+1]
-  float *Vs = Kt + hd * TP;           // [T][hd]
-  float *qb = Vs + T * hd;            // [16][hd]
-  float *pb = qb + 16 * hd;           // [16][T]
-  const int bh = blockIdx.x, b = bh / H, h = bh % H, kvh = h / (H / KV);
+  float *Qt = sm, *Kt = Qt + ATILE, *Vr = Kt + ATILE, *Pt = Vr + ATILE;
+  const int nqt = T / AT;
+  const int qt = blockIdx.x % nqt, bh = blockIdx.x / nqt, b = bh / H, h = bh % H, kvh = h / (H / KV);
   const int D = H * hd, KD = KV * hd;
-  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int idx = threadIdx.x; idx < T * hd; idx += blockDim.x) {
-    const int s = idx / hd, d = idx % hd;
-    const size_t g = (size_t)(b * T + s) * KD + (size_t)kvh * hd + d;
-    Kt[d * TP + s] = k[g];
-    Vs[s * hd + d] = v[g];
+  const int tid = threadIdx.x, ty = tid / 16, tx = tid % 16;
+  const size_t qrow0 = (size_t)b * T + qt * AT;
+  load_tile(Qt, q + qrow0 * D + (size_t)h * hd, D, hd, true);
+  float m[4], l[4], o[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; i++) { m[i] = -1e30f; l[i] = 0.0f; }
+  zero44(o);
+  for (int kt = 0; kt <= qt; kt++) {
+    const size_t krow0 = (size_t)b * T + kt * AT;
+    __syncthreads();
+    load_tile(Kt, k + krow0 * KD + (size_t)kvh * hd, KD, hd, true);
+    load_tile(Vr, v + krow0 * KD + (size_t)kvh * hd, KD, hd, false);
+    __syncthreads();
+    float s[4][4];
+    zero44(s);
+    mm64(s, Qt, Kt, hd, ty, tx);
+    float p[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const int qi = qt * AT + ty * 4 + i;
+      float mx = m[i];
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const int kj = kt * AT + tx * 4 + j;
+        s[i][j] = (kj <= qi) ? s[i][j] * scale : -1e30f;
+        mx = fmaxf(mx, s[i][j]);
+      }
+      mx = hmax16(mx);
+      const float corr = expf(m[i] - mx);
+      float rs = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const int kj = kt * AT + tx * 4 + j;
+        p[i][j] = (kj <= qi) ? expf(s[i][j] - mx) : 0.0f;
+        rs += p[i][j];
+      }
+      rs = hsum16(rs);
+      l[i] = l[i] * corr + rs;
+#pragma unroll
+      for (int j = 0; j < 4; j++) o[i][j] *= corr;
+      m[i] = mx;
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+      for (int j = 0; j < 4; j++) Pt[(tx * 4 + j) * ALD + ty * 4 + i] = p[i][j];
+    __syncthreads();
+    mm64(o, Pt, Vr, AT, ty, tx);
   }
-  __syncthreads();
-  float *myq = qb + w * hd, *myp = pb + w * T;
-  for (int t = w; t < T; t += 16) {
-    const float *qr = q + (size_t)(b * T + t) * D + (size_t)h * hd;
-    for (int d = lane; d < hd; d += 32) myq[d] = qr[d];
-    __syncwarp();
-    float mx = -1e30f;
-    for (int s = lane; s <= t; s += 32) {
-      float dot = 0.0f;
-      for (int d = 0; d < hd; d++) dot += myq[d] * Kt[d * TP + s];
-      dot *= scale;
-      myp[s] = dot;
-      mx = fmaxf(mx, dot);
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const int r = ty * 4 + i;
+    const float inv = 1.0f / l[i];
+    float *orow = out + (qrow0 + r) * D + (size_t)h * hd;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const int d = tx * 4 + j;
+      if (d < hd) orow[d] = o[i][j] * inv;
     }
-    mx = warp_max_f(mx);
-    float sum = 0.0f;
-    for (int s = lane; s <= t; s += 32) {
-      const float e = expf(myp[s] - mx);
-      myp[s] = e;
-      sum += e;
-    }
-    sum = warp_sum_f(sum);
-    const float inv = 1.0f / sum;
-    if (lane == 0) lse[(size_t)bh * T + t] = mx + logf(sum);
-    __syncwarp();
-    float *orow = out + (size_t)(b * T + t) * D + (size_t)h * hd;
-    for (int d = lane; d < hd; d += 32) {
-      float acc = 0.0f;
-      for (int s = 0; s <= t; s++) acc += (myp[s] * inv) * Vs[s * hd + d];
-      orow[d] = acc;
-    }
-    __syncwarp();
+    if (tx == 0) lse[(size_t)bh * T + qt * AT + r] = m[i] + logf(l[i]);
   }
 }
 
-// Backward, query side: one CTA per (b, h), 8 warps, a warp per query row.
-//   p = exp(scale q.k - lse), dp_s = dO.v_s, Drow = dO.out,
-//   ds = p (dp - Drow) scale, dq = sum_s ds k_s.
-// Writes dq (overwrite) and Drow for the key-side kernel.
+// Per-row D = dO . out (softmax backward identity sum_s p_s dp_s = dO . out).
+__global__ void attn_rowdot_kernel(const float *__restrict__ dout, const float *__restrict__ out,
+                                   float *__restrict__ Drow, int B, int T, int H, int hd) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  const int rows = B * H * T;
+  if (warp >= rows) return;
+  const int bh = warp / T, t = warp % T, b = bh / H, h = bh % H;
+  const size_t o = ((size_t)b * T + t) * H * hd + (size_t)h * hd;
+  float acc = 0.0f;
+  for (int d = lane; d < hd; d += 32) acc += dout[o + d] * out[o + d];
+  acc = warp_sum_f(acc);
+  if (lane == 0) Drow[warp] = acc;
+}
+
+// Backward, query side: CTA per (b, h, query tile).  For every key tile:
+// S and dP = dO V^T in one k loop, P = exp(scale S - lse), dS = P (dP - D)
+// scale, dQ += dS K.  Writes dq (overwrite).
 __global__ void __launch_bounds__(256)
 attn_bwd_dq_kernel(const float *__restrict__ q, const float *__restrict__ k, const float *__restrict__ v,
-                   const float *__restrict__ out, const float *__restrict__ dout, const float *__restrict__ lse,
-                   float *__restrict__ dq, float *__restrict__ Drow, int T, int H, int KV, int hd, float scale) {
+                   const float *__restrict__ dout, const float *__restrict__ lse, const float *__restrict__ Drow,
+                   float *__restrict__ dq, int T, int H, int KV, int hd, float scale) {
   extern __shared__ float sm[];
-  const int TP = T + 1;
-  float *Kt = sm;                 // [hd][T+1]
-  float *Ks = Kt + hd * TP;       // [T][hd]
-  float *Vt = Ks + T * hd;        // [hd][T+1]
-  float *qb = Vt + hd * TP;       // [8][hd]
-  float *ob = qb + 8 * hd;        // [8][hd]
-  float *pb = ob + 8 * hd;        // [8][T]
-  const int bh = blockIdx.x, b = bh / H, h = bh % H, kvh = h / (H / KV);
+  float *Qt = sm, *Ot = Qt + ATILE, *Kt = Ot + ATILE, *Vt = Kt + ATILE, *Kr = Vt + ATILE, *St = Kr + ATILE;
+  const int nqt = T / AT;
+  const int qt = blockIdx.x % nqt, bh = blockIdx.x / nqt, b = bh / H, h = bh % H, kvh = h / (H / KV);
   const int D = H * hd, KD = KV * hd;
-  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int idx = threadIdx.x; idx < T * hd; idx += blockDim.x) {
-    const int s = idx / hd, d = idx % hd;
-    const size_t g = (size_t)(b * T + s) * KD + (size_t)kvh * hd + d;
-    const float kv = k[g];
-    Kt[d * TP + s] = kv;
-    Ks[s * hd + d] = kv;
-    Vt[d * TP + s] = v[g];
+  const int tid = threadIdx.x, ty = tid / 16, tx = tid % 16;
+  const size_t qrow0 = (size_t)b * T + qt * AT;
+  load_tile(Qt, q + qrow0 * D + (size_t)h * hd, D, hd, true);
+  load_tile(Ot, dout + qrow0 * D + (size_t)h * hd, D, hd, true);
+  float Lr[4], Dr[4];
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    Lr[i] = lse[(size_t)bh * T + qt * AT + ty * 4 + i];
+    Dr[i] = Drow[(size_t)bh * T + qt * AT + ty * 4 + i];
   }
-  __syncthreads();
-  float *myq = qb + w * hd, *myo = ob + w * hd, *myp = pb + w * T;
-  for (int t = w; t < T; t += 8) {
-    const size_t ro = (size_t)(b * T + t) * D + (size_t)h * hd;
-    float dd = 0.0f;
-    for (int d = lane; d < hd; d += 32) {
-      myq[d] = q[ro + d];
-      const float g = dout[ro + d];
-      myo[d] = g;
-      dd += g * out[ro + d];
-    }
-    dd = warp_sum_f(dd);
-    if (lane == 0) Drow[(size_t)bh * T + t] = dd;
-    __syncwarp();
-    const float L = lse[(size_t)bh * T + t];
-    for (int s = lane; s <= t; s += 32) {
-      float dot = 0.0f, dp = 0.0f;
-      for (int d = 0; d < hd; d++) {
-        dot += myq[d] * Kt[d * TP + s];
-        dp += myo[d] * Vt[d * TP + s];
+  float g[4][4];
+  zero44(g);
+  for (int kt = 0; kt <= qt; kt++) {
+    const size_t krow0 = (size_t)b * T + kt * AT;
+    __syncthreads();
+    load_tile(Kt, k + krow0 * KD + (size_t)kvh * hd, KD, hd, true);
+    load_tile(Vt, v + krow0 * KD + (size_t)kvh * hd, KD, hd, true);
+    load_tile(Kr, k + krow0 * KD + (size_t)kvh * hd, KD, hd, false);
+    __syncthreads();
+    float s[4][4], dp[4][4];
+    zero44(s);
+    zero44(dp);
+    mm64x2(s, dp, Qt, Kt, Ot, Vt, hd, ty, tx);
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const int qi = qt * AT + ty * 4 + i;
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const int kj = kt * AT + tx * 4 + j;
+        const float pr = (kj <= qi) ? expf(s[i][j] * scale - Lr[i]) : 0.0f;
+        St[(tx * 4 + j) * ALD + ty * 4 + i] = pr * (dp[i][j] - Dr[i]) * scale;
       }
-      const float p = expf(dot * scale - L);
-      myp[s] = p * (dp - dd) * scale;
     }
-    __syncwarp();
-    for (int d = lane; d < hd; d += 32) {
-      float acc = 0.0f;
-      for (int s = 0; s <= t; s++) acc += myp[s] * Ks[s * hd + d];
-      dq[ro + d] = acc;
+    __syncthreads();
+    mm64(g, St, Kr, AT, ty, tx);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    float *row = dq + (qrow0 + ty * 4 + i) * D + (size_t)h * hd;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const int d = tx * 4 + j;
+      if (d < hd) row[d] = g[i][j];
     }
-    __syncwarp();
   }
 }
 
-// Backward, key side: one CTA per (b, kv head), 16 warps, a warp per key.
-// Loops over the H/KV query heads of the group: Q and dO of the head are held
-// transposed in shared memory (lanes over queries, then lanes over d).
-//   dv_s += sum_{t>=s} p_ts dO_t,  dk_s += sum_{t>=s} ds_ts q_t.
-// Writes dk, dv (overwrite).  Keys per warp: T/16 <= 16.
-__global__ void __launch_bounds__(512)
+// Backward, key side: CTA per (b, kv head, key tile); loops over the group's
+// query heads and the query tiles at or after the key tile:
+//   S^T = K Q^T and dP^T = V dO^T in one k loop, P^T, dS^T as above,
+//   dV += P^T dO, dK += dS^T Q.  Writes dk, dv (overwrite).
+__global__ void __launch_bounds__(256)
 attn_bwd_dkdv_kernel(const float *__restrict__ q, const float *__restrict__ k, const float *__restrict__ v,
                      const float *__restrict__ dout, const float *__restrict__ lse, const float *__restrict__ Drow,
                      float *__restrict__ dk, float *__restrict__ dv, int T, int H, int KV, int hd, float scale) {
   extern __shared__ float sm[];
-  const int TP = T + 1;
-  float *Qt = sm;                 // [hd][T+1]
-  float *Ot = Qt + hd * TP;       // [hd][T+1]  (dO transposed)
-  float *Lh = Ot + hd * TP;       // [T]
-  float *Dh = Lh + T;             // [T]
-  float *kb = Dh + T;             // [16][hd]
-  float *vb = kb + 16 * hd;       // [16][hd]
-  float *pb = vb + 16 * hd;       // [16][T]
-  float *sb = pb + 16 * T;        // [16][T]
-  const int bk = blockIdx.x, b = bk / KV, kvh = bk % KV, grp = H / KV;
+  float *Kt = sm, *Vt = Kt + ATILE, *Qt = Vt + ATILE, *Ot = Qt + ATILE, *Qr = Ot + ATILE, *Or = Qr + ATILE;
+  float *Ps = Or + ATILE, *Ss = Ps + ATILE;
+  float *Ls = Ss + ATILE, *Ds = Ls + AT;
+  const int nkt = T / AT;
+  const int kt = blockIdx.x % nkt, bk = blockIdx.x / nkt, b = bk / KV, kvh = bk % KV, grp = H / KV;
   const int D = H * hd, KD = KV * hd;
-  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  constexpr int KPW = ATT_TMAX / 16;  // keys per warp (max)
-  float dka[KPW][2], dva[KPW][2];
-#pragma unroll
-  for (int j = 0; j < KPW; j++) { dka[j][0] = dka[j][1] = dva[j][0] = dva[j][1] = 0.0f; }
-  float *myk = kb + w * hd, *myv = vb + w * hd, *myp = pb + w * T, *mys = sb + w * T;
+  const int tid = threadIdx.x, ty = tid / 16, tx = tid % 16;
+  const size_t krow0 = (size_t)b * T + kt * AT;
+  load_tile(Kt, k + krow0 * KD + (size_t)kvh * hd, KD, hd, true);
+  load_tile(Vt, v + krow0 * KD + (size_t)kvh * hd, KD, hd, true);
+  float gk[4][4], gv[4][4];
+  zero44(gk);
+  zero44(gv);
   for (int hh = 0; hh < grp; hh++) {
-    const int h = kvh * grp + hh;
-    const int bh = b * H + h;
-    __syncthreads();
-    for (int idx = threadIdx.x; idx < T * hd; idx += blockDim.x) {
-      const int t = idx / hd, d = idx % hd;
-      const size_t g = (size_t)(b * T + t) * D + (size_t)h * hd + d;
-      Qt[d * TP + t] = q[g];
-      Ot[d * TP + t] = dout[g];
-    }
-    for (int t = threadIdx.x; t < T; t += blockDim.x) {
-      Lh[t] = lse[(size_t)bh * T + t];
-      Dh[t] = Drow[(size_t)bh * T + t];
-    }
-    __syncthreads();
-#pragma unroll
-    for (int j = 0; j < KPW; j++) {
-      const int s = w + 16 * j;
-      if (s >= T) break;
-      const size_t gk = (size_t)(b * T + s) * KD + (size_t)kvh * hd;
-      for (int d = lane; d < hd; d += 32) { myk[d] = k[gk + d]; myv[d] = v[gk + d]; }
-      __syncwarp();
-      for (int t = s + lane; t < T; t += 32) {
-        float dot = 0.0f, dp = 0.0f;
-        for (int d = 0; d < hd; d++) {
-          dot += Qt[d * TP + t] * myk[d];
-          dp += Ot[d * TP + t] * myv[d];
-        }
-        const float p = expf(dot * scale - Lh[t]);
-        myp[t] = p;
-        mys[t] = p * (dp - Dh[t]) * scale;
+    const int h = kvh * grp + hh, bh = b * H + h;
+    for (int qt = kt; qt < T / AT; qt++) {
+      const size_t qrow0 = (size_t)b * T + qt * AT;
+      __syncthreads();
+      load_tile(Qt, q + qrow0 * D + (size_t)h * hd, D, hd, true);
+      load_tile(Ot, dout + qrow0 * D + (size_t)h * hd, D, hd, true);
+      load_tile(Qr, q + qrow0 * D + (size_t)h * hd, D, hd, false);
+      load_tile(Or, dout + qrow0 * D + (size_t)h * hd, D, hd, false);
+      if (tid < AT) {
+        Ls[tid] = lse[(size_t)bh * T + qt * AT + tid];
+        Ds[tid] = Drow[(size_t)bh * T + qt * AT + tid];
       }
-      __syncwarp();
+      __syncthreads();
+      float st[4][4], dpt[4][4];   // rows = keys (ty), cols = queries (tx)
+      zero44(st);
+      zero44(dpt);
+      mm64x2(st, dpt, Kt, Qt, Vt, Ot, hd, ty, tx);
 #pragma unroll
-      for (int c = 0; c < 2; c++) {
-        const int d = lane + 32 * c;
-        if (d < hd) {
-          float av = 0.0f, ak = 0.0f;
-          for (int t = s; t < T; t++) {
-            av += myp[t] * Ot[d * TP + t];
-            ak += mys[t] * Qt[d * TP + t];
-          }
-          dva[j][c] += av;
-          dka[j][c] += ak;
+      for (int i = 0; i < 4; i++) {
+        const int kj = kt * AT + ty * 4 + i;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          const int qi = qt * AT + tx * 4 + j;
+          const int ql = tx * 4 + j;
+          const float pr = (kj <= qi) ? expf(st[i][j] * scale - Ls[ql]) : 0.0f;
+          Ps[ql * ALD + ty * 4 + i] = pr;
+          Ss[ql * ALD + ty * 4 + i] = pr * (dpt[i][j] - Ds[ql]) * scale;
         }
       }
-      __syncwarp();
+      __syncthreads();
+      mm64(gv, Ps, Or, AT, ty, tx);
+      mm64(gk, Ss, Qr, AT, ty, tx);
     }
   }
 #pragma unroll
-  for (int j = 0; j < KPW; j++) {
-    const int s = w + 16 * j;
-    if (s >= T) break;
-    const size_t gk = (size_t)(b * T + s) * KD + (size_t)kvh * hd;
+  for (int i = 0; i < 4; i++) {
+    const size_t o = (krow0 + ty * 4 + i) * KD + (size_t)kvh * hd;
 #pragma unroll
-    for (int c = 0; c < 2; c++) {
-      const int d = lane + 32 * c;
-      if (d < hd) { dk[gk + d] = dka[j][c]; dv[gk + d] = dva[j][c]; }
+    for (int j = 0; j < 4; j++) {
+      const int d = tx * 4 + j;
+      if (d < hd) { dk[o + d] = gk[i][j]; dv[o + d] = gv[i][j]; }
     }
   }
 }
@@ -470,23 +557,19 @@ static inline unsigned grid_for(size_t n, int threads, int cap_waves_sm, int num
   return (unsigned)(b ? b : 1);
 }
 
-size_t attn_smem_fwd(int T, int hd) { return sizeof(float) * ((size_t)hd * (T + 1) + (size_t)T * hd + 16 * hd + 16 * T); }
-size_t attn_smem_dq(int T, int hd) {
-  return sizeof(float) * (2 * (size_t)hd * (T + 1) + (size_t)T * hd + 16 * hd + 8 * T);
-}
-size_t attn_smem_dkdv(int T, int hd) {
-  return sizeof(float) * (2 * (size_t)hd * (T + 1) + 2 * T + 32 * hd + 32 * T);
-}
+size_t attn_smem_fwd() { return sizeof(float) * 4 * mk::ATILE; }
+size_t attn_smem_dq() { return sizeof(float) * 6 * mk::ATILE; }
+size_t attn_smem_dkdv() { return sizeof(float) * (8 * mk::ATILE + 2 * mk::AT); }
 
 int mk_setup(int device) {
   static bool done[kMaxDevices] = {};
   if (done[device]) return TL_OK;
   TL_TRY_CUDA(cudaFuncSetAttribute(mk::attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   (int)attn_smem_fwd(ATT_TMAX, ATT_HDMAX)));
+                                   (int)attn_smem_fwd()));
   TL_TRY_CUDA(cudaFuncSetAttribute(mk::attn_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   (int)attn_smem_dq(ATT_TMAX, ATT_HDMAX)));
+                                   (int)attn_smem_dq()));
   TL_TRY_CUDA(cudaFuncSetAttribute(mk::attn_bwd_dkdv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   (int)attn_smem_dkdv(ATT_TMAX, ATT_HDMAX)));
+                                   (int)attn_smem_dkdv()));
   done[device] = true;
   return TL_OK;
 }
@@ -581,7 +664,8 @@ int k_attn_fwd(DeviceCtx *c, const float *q, const float *k, const float *v, flo
                int H, int KV, int hd) {
   TraceScope ts(c, "k_attn_fwd");
   const float scale = 1.0f / sqrtf((float)hd);
-  mk::attn_fwd_kernel<<<B * H, 512, attn_smem_fwd(T, hd), c->stream>>>(q, k, v, out, lse, T, H, KV, hd, scale);
+  mk::attn_fwd_kernel<<<B * H * (T / mk::AT), 256, attn_smem_fwd(), c->stream>>>(q, k, v, out, lse, T, H, KV, hd,
+                                                                                  scale);
   MK_LAUNCH_CHECK();
   return TL_OK;
 }
@@ -589,11 +673,14 @@ int k_attn_bwd(DeviceCtx *c, const float *q, const float *k, const float *v, con
                const float *lse, float *Drow, float *dq, float *dk, float *dv, int B, int T, int H, int KV, int hd) {
   TraceScope ts(c, "k_attn_bwd");
   const float scale = 1.0f / sqrtf((float)hd);
-  mk::attn_bwd_dq_kernel<<<B * H, 256, attn_smem_dq(T, hd), c->stream>>>(q, k, v, out, dout, lse, dq, Drow, T, H,
-                                                                         KV, hd, scale);
+  const int rows = B * H * T;
+  mk::attn_rowdot_kernel<<<(rows + 7) / 8, 256, 0, c->stream>>>(dout, out, Drow, B, T, H, hd);
   MK_LAUNCH_CHECK();
-  mk::attn_bwd_dkdv_kernel<<<B * KV, 512, attn_smem_dkdv(T, hd), c->stream>>>(q, k, v, dout, lse, Drow, dk, dv, T,
-                                                                             H, KV, hd, scale);
+  mk::attn_bwd_dq_kernel<<<B * H * (T / mk::AT), 256, attn_smem_dq(), c->stream>>>(q, k, v, dout, lse, Drow, dq, T,
+                                                                                   H, KV, hd, scale);
+  MK_LAUNCH_CHECK();
+  mk::attn_bwd_dkdv_kernel<<<B * KV * (T / mk::AT), 256, attn_smem_dkdv(), c->stream>>>(q, k, v, dout, lse, Drow,
+                                                                                       dk, dv, T, H, KV, hd, scale);
   MK_LAUNCH_CHECK();
   return TL_OK;
 }
