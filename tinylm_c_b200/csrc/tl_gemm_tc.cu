@@ -7,21 +7,23 @@
 // MN-major (mm, mm_atb) or K-major (mm_bt).  tcgen05 reads both majors for tf32,
 // so no operand is transposed in memory.
 //
-// 3xTF32: every fp32 operand x is split into hi = tf32(x) (round to nearest)
-// and lo = x - hi (exact in fp32), and the tile product is accumulated as
-// lo*hi + hi*lo + hi*hi in fp32 in TMEM.  The dropped lo*lo term and the tf32
-// rounding of lo leave a relative error near 2^-21 per product, i.e. fp32-level
+// 3xTF32: every fp32 operand x is split into hi = tf32(x) and lo = x - hi
+// (exact in fp32), and the tile product is accumulated as lo*hi + hi*lo +
+// hi*hi in fp32 in TMEM.  The tensor core reads a tf32 operand by dropping the
+// low 13 mantissa bits of the fp32 word, so the landed raw tile *is* hi and
+// only lo = x - trunc(x) is written.  The dropped lo*lo term and the
+// truncation of lo leave a relative error near 2^-20 per product: fp32-level
 // results from the tf32 tensor pipe.
 //
 // CTA roles (320 threads):
 //   warp 0      TMA producer: raw fp32 tiles of A and B -> shared memory stage
 //   warp 1      TMEM owner and MMA issuer (one elected thread)
-//   warps 2..5  split warpgroup: hi written in place over the raw tile, lo into
-//               its own buffer
+//   warps 2..5  split warpgroup: lo of each landed raw tile into its own
+//               buffer (the raw tile is read as hi)
 //   warps 6..9  accumulator warpgroup: every CHUNK_KB k-blocks the TMEM
 //               accumulator (double buffered) is added into fp32 registers;
 //               finally the epilogue (registers -> global, beta = 0 or 1)
-// Pipeline per stage: full (TMA bytes landed) -> ready (hi/lo written) ->
+// Pipeline per stage: full (TMA bytes landed) -> ready (lo written) ->
 // empty (MMAs that read the stage finished, via tcgen05.commit); per TMEM
 // buffer: accf (chunk finished) -> acce (chunk drained).
 //
@@ -138,11 +140,10 @@ __host__ __device__ constexpr uint32_t make_idesc(bool a_mn, bool b_mn) {
          ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
 }
 
-__device__ __forceinline__ float tf32_hi(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return __uint_as_float(r);
-}
+// The value the tf32 MMA reads from an fp32 word: the low 13 mantissa bits
+// are ignored (measured on B200: 1 + 3*2^-12 multiplies as 1.0), so the raw
+// tile serves as hi and only lo = x - trunc_tf32(x), exact in fp32, is stored.
+__device__ __forceinline__ float tf32_trunc(float x) { return __uint_as_float(__float_as_uint(x) & 0xffffe000u); }
 
 struct Params {
   float *C;
@@ -305,10 +306,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const int off = idx < 1024 ? OFF_AHI + idx * 16 : OFF_BHI + (idx - 1024) * 16;
         float4 *src = reinterpret_cast<float4 *>(st + off);
         float4 *dlo = reinterpret_cast<float4 *>(st + off + (idx < 1024 ? TILE_A : TILE_B));
-        float4 x = *src, hi, lo;
-        hi.x = tf32_hi(x.x); hi.y = tf32_hi(x.y); hi.z = tf32_hi(x.z); hi.w = tf32_hi(x.w);
-        lo.x = x.x - hi.x; lo.y = x.y - hi.y; lo.z = x.z - hi.z; lo.w = x.w - hi.w;
-        *src = hi;
+        const float4 x = *src;
+        float4 lo;
+        lo.x = x.x - tf32_trunc(x.x); lo.y = x.y - tf32_trunc(x.y);
+        lo.z = x.z - tf32_trunc(x.z); lo.w = x.w - tf32_trunc(x.w);
         *dlo = lo;
       }
       fence_proxy_async();
