@@ -155,8 +155,9 @@ int tl_model_destroy(void *handle);
 size_t tl_model_param_count(const int *cfg8);
 /* init_params (tinylm.c:395-419) into a HOST buffer of tl_model_param_count
  * floats, reference generator seeded as TINYLM_SEED does (tinylm.c:4809-4811).
- * Host only (no GPU needed). */
-int tl_model_init_params(const int *cfg8, float *P_host, unsigned long long seed);
+ * rng_out (may be NULL) gets the generator state after the draws, where the
+ * reference's batch sampling continues.  Host only (no GPU needed). */
+int tl_model_init_params(const int *cfg8, float *P_host, unsigned long long seed, unsigned long long *rng_out);
 /* Loss only (mean cross-entropy, as forward() returns). */
 int tl_model_forward(void *handle, const float *P, const int *tok, const int *tgt, int B, float *loss_dev);
 /* G += gradients of the batch; loss_dev (may be NULL) = mean loss. */
@@ -166,6 +167,34 @@ int tl_model_forward_backward(void *handle, const float *P, float *G, const int 
  * 0.95, 0.1, t): one step of train_loop / cmd_bench (tinylm.c:2627-2633). */
 int tl_model_step(void *handle, float *P, float *G, float *M, float *V, const int *tok, const int *tgt,
                   const int *tgt_mtp, int B, float lr, int t, float max_norm, float *loss_dev, float *norm_dev);
+
+/* ------------------------------------- training loop: host-side pieces */
+/* Checkpoints in the reference's formats.  Buffers may be host or device
+ * memory (device data is staged through the host).
+ * TLM4 bundle, model_save_bundle (tinylm.c:1895-1914): hdr11 =
+ * {V,D,L,H,KV,F,T,eot,tmpl,n_mtp,n_exp}, then n fp32 parameters, then the
+ * tokenizer blob. */
+int tl_ckpt_save_bundle(const char *path, const int *hdr11, const float *P, size_t n, const void *tok_blob,
+                        int tok_len);
+/* model_load (tinylm.c:1915-1938) for TLM1-TLM4: header into hdr11 (missing
+ * fields 0); when P is not NULL, n_expected parameters into P.  *n_in_file
+ * (may be NULL) = floats after the header (parameters + tokenizer tail). */
+int tl_ckpt_load_bundle(const char *path, int *hdr11, float *P, size_t n_expected, size_t *n_in_file);
+/* TOPT sidecar, opt_save / opt_load (tinylm.c:2526-2539): "TOPT", iter, M[n],
+ * V[n].  Create the file once, then write / read any range of M and V -- each
+ * ZeRO-1 rank stores and restores its own shard, no gather needed. */
+int tl_ckpt_opt_create(const char *path, int iter, size_t n);
+int tl_ckpt_opt_write(const char *path, size_t n, size_t offset, const float *M, const float *V, size_t count);
+int tl_ckpt_opt_read(const char *path, size_t n, size_t offset, float *M, float *V, size_t count, int *iter_out);
+/* LR at iteration it: linear warm-up, then cosine to 0.1*lr (train_loop,
+ * tinylm.c:2587-2590). */
+float tl_lr_at(int it, float lr, int iters, float warmup);
+/* B windows of a uint16 token stream drawn with the reference's generator
+ * (*rng is advanced): training (val=0, tinylm.c:2623-2626) or validation
+ * batches (val=1, 2596-2597).  Outputs are host int32 arrays: tok/tgt [B*T],
+ * tgt_mtp [n_mtp][B*T] (training only). */
+int tl_sample_windows(unsigned long long *rng, const unsigned short *stream, size_t n, int B, int T, int n_mtp,
+                      int val, int *tok, int *tgt, int *tgt_mtp);
 
 /* ------------------------------------------- data parallel + ZeRO-1 (NCCL) */
 /* No counterpart in the reference (it has no distributed code); this is the

@@ -64,6 +64,8 @@ def port():
         L.tlo_seed.argtypes = [_u64]
         L.tlo_xorshift.restype = _u64
         L.tlo_fill_normal.argtypes = [_fp, _sz, _f]
+        L.tlo_lr_at.argtypes = [_i, _f, _i, _f]
+        L.tlo_lr_at.restype = _f
         _port = L
     return _port
 
@@ -105,6 +107,12 @@ def ref():
         L.tlref_model_step.restype = _f
         L.tlref_model_free.argtypes = [ctypes.c_void_p]
         L.tlref_max_threads.restype = _i
+        _u16p = ctypes.POINTER(ctypes.c_uint16)
+        L.tlref_train.argtypes = [_ip, _i, _i, _i, _f, _u64, _u16p, _sz, _u16p, _sz, ctypes.c_char_p,
+                                  ctypes.c_char_p, ctypes.c_char_p, _i, ctypes.c_char_p, ctypes.c_char_p]
+        L.tlref_train.restype = _i
+        L.tlref_model_load.argtypes = [ctypes.c_char_p, _ip, _fp, _sz]
+        L.tlref_model_load.restype = _sz
         _ref = L
     return _ref
 
@@ -165,3 +173,27 @@ def adamw_inputs(n, seed=0):
     m = (rng.standard_normal(n, dtype=np.float32) * np.float32(1e-4))
     v = np.abs(rng.standard_normal(n, dtype=np.float32) * np.float32(1e-6))
     return p, g, m, v
+
+
+def ref_train(cfg7, n_mtp, B, iters, lr, seed, tr, vl, out, optpath, tok_blob=b"", resume=None):
+    """Run the reference's train_loop (tinylm.c:2562-2654) on uint16 streams tr/vl;
+    returns its stdout lines.  resume = (bundle, opt) continues from files."""
+    import tempfile
+    R = ref()
+    tr = np.ascontiguousarray(tr, dtype=np.uint16)
+    vl = np.ascontiguousarray(vl, dtype=np.uint16)
+    u16 = ctypes.POINTER(ctypes.c_uint16)
+    cap = tempfile.TemporaryFile(mode="w+b")
+    import sys
+    sys.stdout.flush()
+    saved = os.dup(1)
+    os.dup2(cap.fileno(), 1)
+    try:
+        R.tlref_train((_i * 7)(*cfg7), n_mtp, B, iters, lr, seed, tr.ctypes.data_as(u16), tr.size,
+                      vl.ctypes.data_as(u16), vl.size, out.encode(), optpath.encode(), tok_blob, len(tok_blob),
+                      resume[0].encode() if resume else None, resume[1].encode() if resume else None)
+    finally:
+        os.dup2(saved, 1)
+        os.close(saved)
+    cap.seek(0)
+    return cap.read().decode(errors="replace").replace("\r", "\n").splitlines()

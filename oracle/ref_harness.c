@@ -10,7 +10,8 @@
  *   mm 439-478, mm_bt 480-508, mm_atb 510-537, adamw 1159-1170,
  *   global_gradnorm 1171-1176, forward 968-1029, backward 1072-1154,
  *   init_params 395-419, param_count 345-358, preset 109-124, rng 126-134,
- *   set_ftz 4790-4804, step order of cmd_bench 4734-4741.
+ *   set_ftz 4790-4804, step order of cmd_bench 4734-4741, train_loop 2562-2654,
+ *   model_load 1915-1938, opt_load 2533-2539.
  */
 #define main tinylm_main
 #include "tinylm.c"
@@ -149,4 +150,62 @@ TLREF_API void tlref_model_free(void *h)
     for (int k = 0; k < r->c.n_mtp; k++) free(r->tgt_mtp[k]);
     free(r->tgt_mtp);
     free(r);   /* Acts and weight-pointer tables are leaked as the reference does */
+}
+
+/* ---- the reference's whole training loop, for trainer / checkpoint parity --
+ * Runs train_loop (tinylm.c:2562-2654) on a fresh model (init_params seeded
+ * as TINYLM_SEED) or, when resume_bundle is given, on the parameters of that
+ * TLM bundle and the AdamW state of resume_opt (model_load + opt_load, the
+ * resume path of cmd_train 2742-2743; the generator restarts from the seed).
+ * tr/vl are uint16 token streams.  Writes `out` (TLM4) and `optpath` (TOPT)
+ * as train_loop does; its progress lines go to stdout. */
+TLREF_API int tlref_train(const int *cfg7, int n_mtp, int B, int iters, float lr, unsigned long long seed,
+                          const uint16_t *tr, size_t ntr, const uint16_t *vl, size_t nvl,
+                          const char *out, const char *optpath, const uint8_t *tok_blob, int tok_len,
+                          const char *resume_bundle, const char *resume_opt)
+{
+    Cfg c; memset(&c, 0, sizeof(c));
+    int start_iter = 0;
+    float *loaded = NULL;
+    if (resume_bundle) {
+        loaded = model_load(resume_bundle, &c);
+    } else {
+        c.V = cfg7[0]; c.D = cfg7[1]; c.L = cfg7[2]; c.H = cfg7[3]; c.KV = cfg7[4];
+        c.F = cfg7[5]; c.T = cfg7[6] > 0 ? cfg7[6] : 256; c.rope_base = 10000.0f;
+        c.n_mtp = n_mtp;
+        cfg_derive(&c);
+    }
+    g_rng = (uint64_t)seed | 1ULL;
+    free(rope_cos); free(rope_sin); rope_cos = rope_sin = NULL; rope_max = 0;
+    rope_init(&c, c.T);
+    size_t np = param_count(&c);
+    float *P = fz(np), *G = fz(np), *M = fz(np), *Vv = fz(np);
+    Weights w, gr; map_weights(&c, P, &w); map_weights(&c, G, &gr);
+    memset(&w.ng, 0, sizeof(w.ng)); memset(&gr.ng, 0, sizeof(gr.ng));
+    if (loaded) {
+        memcpy(P, loaded, sizeof(float) * np); free(loaded);
+        start_iter = opt_load(resume_opt, M, Vv, np);
+    } else {
+        init_params(&c, &w);
+    }
+    fflush(stdout);
+    train_loop(&c, &w, &gr, P, G, M, Vv, np, tr, ntr, vl, nvl, B, iters, lr, start_iter,
+               out, optpath, tok_blob, tok_len);
+    fflush(stdout);
+    free(P); free(G); free(M); free(Vv);
+    return start_iter;
+}
+/* model_load (tinylm.c:1915-1938) of a bundle: fills cfg11 with the header
+ * fields V,D,L,H,KV,F,T,eot,tmpl,n_mtp,n_exp and returns the parameter count;
+ * copies the parameters to P when P is not NULL. */
+TLREF_API size_t tlref_model_load(const char *path, int *cfg11, float *P, size_t cap)
+{
+    Cfg c; memset(&c, 0, sizeof(c));
+    float *p = model_load(path, &c);
+    size_t np = param_count(&c);
+    int h[11] = {c.V, c.D, c.L, c.H, c.KV, c.F, c.T, c.eot, c.tmpl, c.n_mtp, c.n_exp};
+    memcpy(cfg11, h, sizeof(h));
+    if (P && cap >= np) memcpy(P, p, sizeof(float) * np);
+    free(p);
+    return np;
 }

@@ -156,3 +156,13 @@ TLO_API void tlo_fill_normal(float *dst, size_t n, float scale)
         dst[i] = scale * (sqrtf(-2.0f * logf(u1)) * cosf(6.28318530718f * u2));
     }
 }
+
+/* Learning-rate schedule of train_loop -- tinylm.c:2587-2590: linear warm-up
+ * over `warmup` iterations, then cosine from lr to 0.1*lr. */
+TLO_API float tlo_lr_at(int it, float lr, int iters, float warmup)
+{
+    if (it < warmup) return lr * (it + 1) / warmup;
+    float r = (it - warmup) / (float)(iters > warmup ? iters - warmup : 1);
+    if (r > 1) r = 1;
+    return 0.1f * lr + 0.5f * (1 + cosf(3.14159265f * r)) * (lr - 0.1f * lr);
+}

@@ -1,0 +1,117 @@
+"""The training loop on the GPU (tinylm_c_b200.trainer) against the
+reference's own train_loop (tinylm.c:2562-2654) run live on the same data:
+validation losses, the final TLM4 bundle and TOPT sidecar, and resuming from
+files the reference wrote."""
+import os
+import re
+import shutil
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from tinylm_c_b200 import _lib, model, trainer
+
+pytestmark = [pytest.mark.gpu, pytest.mark.skipif(not oracle.has_ref(), reason="reference leg not built")]
+CFG7 = [512, 64, 4, 4, 2, 176, 256]      # nano preset (tinylm.c:112)
+LR = 6e-4                                 # default_lr_for a D=64 model (tinylm.c:2546)
+VAL_RE = re.compile(r"iter\s+(\d+) .*\| val ([0-9.]+)")
+
+
+def streams():
+    rng = np.random.default_rng(0)
+    return rng.integers(0, 512, 20000).astype(np.uint16), rng.integers(0, 512, 5000).astype(np.uint16)
+
+
+def vals(lines):
+    return [(int(m.group(1)), float(m.group(2))) for m in map(VAL_RE.search, lines) if m]
+
+
+def read_opt(path, n):
+    raw = open(path, "rb").read()
+    it = int(np.frombuffer(raw[4:8], np.int32)[0])
+    body = np.frombuffer(raw[8:], np.float32)
+    return it, body[:n].astype(np.float64), body[n:2 * n].astype(np.float64)
+
+
+def read_bundle(path, n):
+    raw = open(path, "rb").read()
+    return raw[:48], np.frombuffer(raw[48:48 + 4 * n], np.float32).astype(np.float64)
+
+
+def rel(a, b):
+    return np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30)
+
+
+def compare_runs(mine, ref, P0, n):
+    hm, Pm = read_bundle(mine[0], n)
+    hr, Pr = read_bundle(ref[0], n)
+    assert hm == hr, "bundle headers differ"
+    assert rel(Pm - P0, Pr - P0) <= 1e-3, "parameter update differs"
+    itm, Mm, Vm = read_opt(mine[1], n)
+    itr, Mr, Vr = read_opt(ref[1], n)
+    assert itm == itr
+    assert rel(Mm, Mr) <= 1e-4 and rel(Vm, Vr) <= 1e-4
+
+
+def test_fresh_run_matches_reference_train_loop(cuda, tmp_path):
+    tr, vl = streams()
+    oracle.ref().tlref_init(8, 0)
+    ref = (str(tmp_path / "r.bin"), str(tmp_path / "r.opt"))
+    ref_lines = oracle.ref_train(CFG7, 0, 2, 6, LR, 0, tr, vl, ref[0], ref[1])
+    cfg = model.cfg8("nano", 0)
+    t = trainer.Trainer(cfg, 2, device=0)
+    mine = (str(tmp_path / "m.bin"), str(tmp_path / "m.opt"))
+    lines = []
+    t.run(tr, vl, 6, LR, seed=0, out=mine[0], optpath=mine[1], log=lines.append)
+    _lib.check(_lib.lib().tl_device_status())
+    t.close()
+    vr, vm = vals(ref_lines), vals(lines)
+    assert [i for i, _ in vr] == [i for i, _ in vm] == [0, 6]
+    for (_, a), (_, b) in zip(vm, vr):
+        assert abs(a - b) <= 2e-4, (vm, vr)            # the reference prints 4 decimals
+    P0 = model.init_params(cfg, 0).numpy().astype(np.float64)
+    compare_runs(mine, ref, P0, t.n)
+
+
+def test_resume_from_reference_files_matches_reference_resume(cuda, tmp_path):
+    """The reference trains 3 iterations and writes its files; the reference and
+    this trainer each resume from those files to iteration 6."""
+    tr, vl = streams()
+    R = oracle.ref()
+    R.tlref_init(8, 0)
+    a = (str(tmp_path / "a.bin"), str(tmp_path / "a.opt"))
+    oracle.ref_train(CFG7, 0, 2, 3, LR, 0, tr, vl, a[0], a[1])
+    ref = (str(tmp_path / "r.bin"), str(tmp_path / "r.opt"))
+    shutil.copy(a[0], ref[0]); shutil.copy(a[1], ref[1])
+    ref_lines = oracle.ref_train(CFG7, 0, 2, 6, LR, 0, tr, vl, ref[0], ref[1], resume=ref)
+    mine = (str(tmp_path / "m.bin"), str(tmp_path / "m.opt"))
+    shutil.copy(a[0], mine[0]); shutil.copy(a[1], mine[1])
+    cfg = model.cfg8("nano", 0)
+    t = trainer.Trainer(cfg, 2, device=0)
+    lines = []
+    t.run(tr, vl, 6, LR, seed=0, out=mine[0], optpath=mine[1], resume=True, log=lines.append)
+    _lib.check(_lib.lib().tl_device_status())
+    t.close()
+    vr, vm = vals(ref_lines), vals(lines)
+    assert [i for i, _ in vr] == [i for i, _ in vm] == [3, 6]
+    for (_, x), (_, y) in zip(vm, vr):
+        assert abs(x - y) <= 2e-4, (vm, vr)
+    _, P3 = read_bundle(a[0], t.n)
+    compare_runs(mine, ref, P3, t.n)
+
+
+def test_micro_batched_trainer_matches_whole_batch(cuda, tmp_path):
+    """Same run with the batch as one micro-batch or as two: same validation
+    losses and parameters up to rounding."""
+    tr, vl = streams()
+    cfg = model.cfg8("nano", 0)
+    out = []
+    for mb in (4, 2):
+        t = trainer.Trainer(cfg, 4, micro_batch=mb, device=0)
+        h = t.run(tr, vl, 3, LR, seed=1, log=lambda *_: None)
+        out.append(([v for k, _, v in h if k == "val"], t.P[: t.n].cpu().numpy().astype(np.float64)))
+        t.close()
+    assert np.allclose(out[0][0], out[1][0], atol=1e-5)
+    assert np.max(np.abs(out[0][1] - out[1][1])) < 1e-6

@@ -58,7 +58,18 @@ SIGNATURES = {
     "tl_model_nparams": (_c_size, [_c_void_p]),
     "tl_model_destroy": (_c_int, [_c_void_p]),
     "tl_model_param_count": (_c_size, [ctypes.POINTER(_c_int)]),
-    "tl_model_init_params": (_c_int, [ctypes.POINTER(_c_int), _c_void_p, ctypes.c_ulonglong]),
+    "tl_model_init_params": (_c_int, [ctypes.POINTER(_c_int), _c_void_p, ctypes.c_ulonglong,
+                                      ctypes.POINTER(ctypes.c_ulonglong)]),
+    "tl_ckpt_save_bundle": (_c_int, [ctypes.c_char_p, ctypes.POINTER(_c_int), _c_void_p, _c_size, _c_void_p, _c_int]),
+    "tl_ckpt_load_bundle": (_c_int, [ctypes.c_char_p, ctypes.POINTER(_c_int), _c_void_p, _c_size,
+                                     ctypes.POINTER(_c_size)]),
+    "tl_ckpt_opt_create": (_c_int, [ctypes.c_char_p, _c_int, _c_size]),
+    "tl_ckpt_opt_write": (_c_int, [ctypes.c_char_p, _c_size, _c_size, _c_void_p, _c_void_p, _c_size]),
+    "tl_ckpt_opt_read": (_c_int, [ctypes.c_char_p, _c_size, _c_size, _c_void_p, _c_void_p, _c_size,
+                                  ctypes.POINTER(_c_int)]),
+    "tl_lr_at": (_c_float, [_c_int, _c_float, _c_int, _c_float]),
+    "tl_sample_windows": (_c_int, [ctypes.POINTER(ctypes.c_ulonglong), _c_void_p, _c_size, _c_int, _c_int, _c_int,
+                                   _c_int, _c_void_p, _c_void_p, _c_void_p]),
     "tl_model_forward": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_int, _c_void_p]),
     "tl_model_forward_backward": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
                                            _c_int, _c_void_p]),

@@ -318,8 +318,9 @@ TL_API size_t tl_model_param_count(const int *cfg8) {
 
 // init_params (tinylm.c:395-419) into a host buffer of tl_model_param_count
 // floats, with the reference generator seeded as TINYLM_SEED does (seed | 1).
-// Host only: needs no GPU.
-TL_API int tl_model_init_params(const int *cfg8, float *P_host, unsigned long long seed) {
+// rng_out (may be NULL) receives the generator state after the draws, where
+// train_loop's batch sampling continues.  Host only: needs no GPU.
+TL_API int tl_model_init_params(const int *cfg8, float *P_host, unsigned long long seed, unsigned long long *rng_out) {
   if (!cfg8 || !P_host) return set_error(TL_EINVAL, "NULL argument");
   Model mm;
   int rc = cfg_model(cfg8, mm);
@@ -343,6 +344,7 @@ TL_API int tl_model_init_params(const int *cfg8, float *P_host, unsigned long lo
   for (size_t i = 0; i < D; i++) p[m->o_nf + i] = 1.0f;
   for (int k = 0; k < m->n_mtp; k++)
     for (size_t i = 0; i < D * D; i++) p[m->o_mtp[k] + i] = 0.0f;
+  if (rng_out) *rng_out = r.s;  // the generator continues into batch sampling
   return TL_OK;
 }
 

@@ -32,13 +32,15 @@ def param_count(cfg):
     return lib().tl_model_param_count(cfg)
 
 
-def init_params(cfg, seed):
+def init_params(cfg, seed, return_rng=False):
     """init_params (tinylm.c:395-419) on the host, reference generator seeded
-    as TINYLM_SEED=seed does; returns a float32 CPU tensor."""
+    as TINYLM_SEED=seed does; returns a float32 CPU tensor (and, when asked,
+    the generator state the reference's batch sampling continues from)."""
     n = param_count(cfg)
     P = torch.empty(n, dtype=torch.float32)
-    check(lib().tl_model_init_params(cfg, P.data_ptr(), seed))
-    return P
+    st = ctypes.c_ulonglong(0)
+    check(lib().tl_model_init_params(cfg, P.data_ptr(), seed, ctypes.byref(st)))
+    return (P, st.value) if return_rng else P
 
 
 def _iptr(t, name):
