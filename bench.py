@@ -71,6 +71,8 @@ def parse():
     ap.add_argument("--no-adamw-line", action="store_true", help="train: skip the config-2 AdamW sub-measurement")
     ap.add_argument("--shape", default="", help="gemm workload: one M,K,N instead of the sweep")
     ap.add_argument("--op", default="all", choices=["all", "mm", "mm_bt", "mm_atb"], help="gemm workload: primitive")
+    ap.add_argument("--gemm-engine", type=int, default=0, choices=[0, 1, 2, 3],
+                    help="GEMM engine: 0 automatic, 1 CUDA-core, 2 tensor-core one CTA, 3 tensor-core CTA pair")
     return ap.parse_args()
 
 
@@ -393,7 +395,7 @@ def run_train(args, rk):
     # ---- roofline of the dominant kernel (the tensor-core GEMM)
     peaks, peak_kind = measured_peaks()
     gflop_tok = gemm_flops_per_token(tuple(cfg))
-    gemm = kernels.get("gemm_tc", {"ms_per_step": 0.0, "launches": 0})
+    gemm = gemm_kernels(kernels)
     flops_rank = gflop_tok * N
     achieved = flops_rank / (gemm["ms_per_step"] * 1e-3) / 1e12 if gemm["ms_per_step"] else None
     bf16 = peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops"))
@@ -524,6 +526,18 @@ def run_adamw(args, rk, n):
                        "parallelism": "single" if world == 1 else f"zero1_dp{world}",
                        "l2": "inputs 4 GiB >> 126 MB L2 (no flush needed)"},
             "e2e": e2e, "roofline": roofline, "clocks": clocks, "gpu_launches": launches, "kernels": kernels}
+
+
+def gemm_kernels(kernels):
+    """The tensor-core GEMM launches of a traced region, both kernels summed."""
+    out = {"ms_per_step": 0.0, "launches": 0, "names": []}
+    for name in ("gemm_tc", "gemm_tc_pair"):
+        k = kernels.get(name)
+        if k:
+            out["ms_per_step"] += k["ms_per_step"]
+            out["launches"] += k["launches"]
+            out["names"].append(name)
+    return out
 
 
 # ------------------------------------------------------------- gemm (cfg 3)
@@ -669,6 +683,8 @@ def main():
         return 0
 
     rk = Run(rank, world, local)
+    if args.gemm_engine:
+        rk.ops.set_gemm_engine(args.gemm_engine)
     if args.workload == "gemm":
         out = run_gemm(args, rk)
         if rank == 0 and world == 1 and not args.no_cpu_baseline:

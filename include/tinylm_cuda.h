@@ -93,11 +93,13 @@ int tl_matmul_at(float *dW, const float *X, const float *dY, int M, int K, int N
 
 /* GEMM engine selection, for tests and benchmarks: 0 = automatic (tensor-core
  * 3xTF32 where the shape allows, else CUDA-core fp32), 1 = CUDA-core fp32 only,
- * 2 = tensor-core 3xTF32 only (TL_EINVAL where the shape does not allow it).
+ * 2 = tensor-core 3xTF32, one CTA per 128 x 128 tile, 3 = tensor-core 3xTF32,
+ * a CTA pair (two SMs, cta_group::2) per 256 x 256 tile (2 and 3: TL_EINVAL
+ * where the shape does not allow the tensor-core engine).
  * No counterpart in the reference (its only engine switch is USE_BLAS,
  * tinylm.c:29-31). */
 int tl_set_gemm_engine(int engine);
-/* Engine the last GEMM call on this thread ran on (1 or 2), 0 if none. */
+/* Engine the last GEMM call on this thread ran on (1, 2 or 3), 0 if none. */
 int tl_last_gemm_engine(void);
 
 /* -------------------------------------------------------------- optimizer */

@@ -98,11 +98,19 @@ def test_gemm_rejects_host_memory(cuda):
         ops.mm(torch.zeros(4, device=cuda), X.ctypes.data, X.ctypes.data, 2, 2, 2)
 
 
-@pytest.mark.parametrize("M,K,N", [(128, 32, 128), (256, 64, 256), (130, 68, 100), (1000, 36, 72), (257, 1024, 2816)])
-def test_tensor_core_engine_forced(cuda, M, K, N):
-    """The tcgen05 3xTF32 engine alone (engine 2) on aligned shapes, including
-    partial tiles in every dimension."""
-    ops.set_gemm_engine(2)
+TC_ENGINES = {"tc_1cta": 2, "tc_pair": 3}
+
+
+@pytest.mark.parametrize("tc_engine", list(TC_ENGINES))
+@pytest.mark.parametrize("M,K,N", [(128, 32, 128), (256, 64, 256), (130, 68, 100), (1000, 36, 72), (257, 1024, 2816),
+                                   (384, 8, 520), (100, 4096, 260)])
+def test_tensor_core_engine_forced(cuda, tc_engine, M, K, N):
+    """Each tcgen05 3xTF32 kernel alone (engine 2: one CTA per 128 x 128
+    tile; engine 3: a CTA pair per 256 x 256 tile) on aligned shapes,
+    including partial tiles in every dimension, a pair whose second CTA has
+    no rows (M=100) and split-K (K=4096 with few tiles)."""
+    eng = TC_ENGINES[tc_engine]
+    ops.set_gemm_engine(eng)
     try:
         rng = np.random.default_rng(M + K + N)
         X = rng.standard_normal(M * K, dtype=np.float32)
@@ -113,11 +121,11 @@ def test_tensor_core_engine_forced(cuda, M, K, N):
         Y = torch.full((M * N,), float("nan"), device=cuda)
         dX, dW = dev(dX0, cuda), dev(dW0, cuda)
         ops.mm(Y, dev(X, cuda), dev(W, cuda), M, K, N)
-        assert ops.last_gemm_engine() == 2
+        assert ops.last_gemm_engine() == eng
         ops.mm_bt(dX, dev(dY, cuda), dev(W, cuda), M, K, N)
-        assert ops.last_gemm_engine() == 2
+        assert ops.last_gemm_engine() == eng
         ops.mm_atb(dW, dev(X, cuda), dev(dY, cuda), M, K, N)
-        assert ops.last_gemm_engine() == 2
+        assert ops.last_gemm_engine() == eng
         torch.cuda.synchronize()
         device_ok()
     finally:
@@ -131,8 +139,9 @@ def test_tensor_core_engine_forced(cuda, M, K, N):
     assert gemm_rel(dW.cpu().numpy(), dW64) <= GEMM_REL_TOL
 
 
-def test_tensor_core_engine_rejects_unaligned(cuda):
-    ops.set_gemm_engine(2)
+@pytest.mark.parametrize("tc_engine", list(TC_ENGINES))
+def test_tensor_core_engine_rejects_unaligned(cuda, tc_engine):
+    ops.set_gemm_engine(TC_ENGINES[tc_engine])
     try:
         z = torch.zeros(201 * 259, device=cuda)
         with pytest.raises(TLError):
@@ -141,10 +150,20 @@ def test_tensor_core_engine_rejects_unaligned(cuda):
         ops.set_gemm_engine(0)
 
 
+@pytest.mark.parametrize("tc_engine", list(TC_ENGINES))
 @pytest.mark.parametrize("M,K,N", [(16384, 1024, 1024), (16384, 256, 2816), (65536, 512, 256)])
-def test_gemm_sweep_shapes_sampled(cuda, M, K, N):
-    """BASELINE config-3 shapes at full size, checked on sampled rows/columns
-    against float64 (rows of Y and dX, columns of dW, are independent)."""
+def test_gemm_sweep_shapes_sampled(cuda, tc_engine, M, K, N):
+    """BASELINE config-3 shapes at full size on each tensor-core kernel,
+    checked on sampled rows/columns against float64 (rows of Y and dX,
+    columns of dW, are independent)."""
+    ops.set_gemm_engine(TC_ENGINES[tc_engine])
+    try:
+        _sweep_shape_sampled(cuda, M, K, N)
+    finally:
+        ops.set_gemm_engine(0)
+
+
+def _sweep_shape_sampled(cuda, M, K, N):
     rng = np.random.default_rng(3)
     X = torch.randn(M * K, device=cuda, generator=torch.Generator(device=cuda).manual_seed(1))
     W = torch.randn(K * N, device=cuda, generator=torch.Generator(device=cuda).manual_seed(2)) * 0.02

@@ -3,7 +3,7 @@
 
 namespace tl {
 
-static thread_local int g_engine_pref = 0;   // 0 auto, 1 CUDA-core, 2 tensor-core
+static thread_local int g_engine_pref = 0;   // 0 auto, 1 CUDA-core, 2 tensor-core, 3 tensor-core pair
 static thread_local int g_engine_last = 0;
 
 static int gemm_entry(GemmOp op, float *C, const float *A, const float *B, int M, int K, int N,
@@ -41,11 +41,12 @@ int tl::gemm_run(DeviceCtx *c, GemmOp op, float *C, const float *A, const float 
     return TL_OK;
   }
   const bool tc_ok = gemm_tc_supported(op, C, A, B, M, K, N);
-  if (g_engine_pref == 2 && !tc_ok)
+  if (g_engine_pref >= 2 && !tc_ok)
     return set_error(TL_EINVAL, "tensor-core engine forced but shape/alignment unsupported (M=%d K=%d N=%d)", M, K, N);
   if (tc_ok && g_engine_pref != 1) {
-    g_engine_last = 2;
-    return gemm_tc(c, op, C, A, B, M, K, N);
+    const bool pair = g_engine_pref == 3 || (g_engine_pref == 0 && gemm_tc_prefer_pair(I, J, R));
+    g_engine_last = pair ? 3 : 2;
+    return gemm_tc(c, op, C, A, B, M, K, N, pair);
   }
   g_engine_last = 1;
   return gemm_simt(c, op, C, A, B, M, K, N);
@@ -63,7 +64,7 @@ TL_API int tl_matmul_at(float *dW, const float *X, const float *dY, int M, int K
   return gemm_entry(GemmOp::TN, dW, X, dY, M, K, N, "dW,X,dY");
 }
 TL_API int tl_set_gemm_engine(int engine) {
-  if (engine < 0 || engine > 2) return set_error(TL_EINVAL, "engine must be 0, 1 or 2");
+  if (engine < 0 || engine > 3) return set_error(TL_EINVAL, "engine must be 0, 1, 2 or 3");
   g_engine_pref = engine;
   return TL_OK;
 }

@@ -24,6 +24,11 @@ int gemm_simt(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B,
 // Returns TL_EINVAL (without launching) when the shape or alignment is not
 // supported by the tensor-core engine.
 bool gemm_tc_supported(GemmOp op, const float *C, const float *A, const float *B, int M, int K, int N);
-int gemm_tc(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, int M, int K, int N);
+// Automatic choice between the two tensor-core kernels for an I x J output
+// with reduction length R.
+bool gemm_tc_prefer_pair(int I, int J, int R);
+// pair: the CTA-pair kernel (256 x 256 tiles over two SMs) instead of the
+// one-CTA kernel (128 x 128 tiles).
+int gemm_tc(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, int M, int K, int N, bool pair);
 
 }  // namespace tl

@@ -31,6 +31,12 @@
 // in the context's device error word, raises a CTA-wide abort flag and the CTA
 // winds down (the MMA thread still waits, bounded, for its own MMAs; TMEM is
 // always released).
+//
+// Two kernels share these tiles and this protocol: gemm_tc_kernel (one CTA
+// per 128 x 128 output tile, cta_group::1) and gemm_tc_pair_kernel (a cluster
+// of two CTAs per 256 x 256 tile, cta_group::2), which halves the shared-
+// memory bytes the tensor pipe reads per flop -- the limit of the one-CTA
+// kernel -- and is the default wherever both output sides exceed 128.
 #include <cuda.h>
 #include <algorithm>
 #include <cudaTypedefs.h>
@@ -384,6 +390,341 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   }
 }
 
+// ------------------------------------------- CTA-pair (2-SM) tensor-core kernel
+// A cluster of two CTAs on an SM pair computes one 256 x 256 output tile with
+// tcgen05.mma.cta_group::2 (M = 256, N = 256).  Each CTA stages only its own
+// 128 rows of A and its own 128 columns of B, so per SM the tensor pipe reads
+// 8 KB of shared memory per 128-cycle MMA instead of 8 KB per 64 cycles in the
+// one-CTA kernel, and L2 serves half the operand bytes per flop.  Tiles in
+// shared memory have the one-CTA kernel's shapes and layouts.
+//
+// Roles: warp 0 loads this CTA's A and B halves (TMA into its own shared
+// memory, no multicast); warp 1 of the leader CTA (rank 0) issues the MMAs of
+// the pair; warps 2-9 of both CTAs write the lo parts of the landed tiles and
+// drain finished TMEM chunks into fp32 registers.  Warps of either CTA signal
+// the leader's `ready`/`acce` barriers through cluster addresses; the
+// leader's commits arrive on the `empty`/`accf` barriers of both CTAs.
+constexpr int PM = 2 * BM, PN = 2 * BN;                 // 256 x 256 per pair
+constexpr int PAIR_TMEM_COLS = 2 * PN;                  // two 256-column accumulators
+constexpr int PAIR_SIGNALLERS = 2 * 8;                  // split/drain warps in the pair
+constexpr int PAIR_DRAIN_LAG = 2;                       // k-blocks split ahead of a forced drain
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_map(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cl(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{ .reg .pred p; mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Cluster-wide barrier of all threads of both CTAs (the non-aligned form:
+// lanes of a warp may arrive from different branches).
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+// Abort raised in this CTA is also written into the peer's flag, so that the
+// peer stops waiting for signals that will not come.
+__device__ __forceinline__ void pair_abort(volatile int *flag, uint32_t peer_flag, int *err, int code) {
+  *flag = 1;
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(peer_flag), "r"(1) : "memory");
+  atomicExch(err, code);
+}
+__device__ __forceinline__ bool mbar_wait_pair(uint32_t bar, uint32_t parity, volatile int *flag, uint32_t peer_flag,
+                                               int *err, int code) {
+  const long long t0 = clock64();
+  while (!mbar_try_wait_cl(bar, parity)) {
+    if (*flag) return false;
+    if (clock64() - t0 > WAIT_LIMIT_CYCLES) {
+      pair_abort(flag, peer_flag, err, code);
+      return false;
+    }
+  }
+  return true;
+}
+__device__ __forceinline__ void tc_mma_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{ .reg .pred p; setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p; }" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive (once the pair's MMAs issued so far have completed) on the barrier at
+// this shared-memory offset in both CTAs of the pair.
+__device__ __forceinline__ void tc_commit_pair(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::
+                   "r"(bar), "h"((uint16_t)0x3)
+               : "memory");
+}
+
+__host__ __device__ constexpr uint32_t make_idesc_pair(bool a_mn, bool b_mn) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) |
+         ((uint32_t)(PN >> 3) << 17) | ((uint32_t)(PM >> 4) << 24);
+}
+
+template <bool A_MN, bool B_MN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
+gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
+  // bars: full[S] (this CTA's TMA landed), ready[S] (both CTAs' lo parts
+  // written; leader's copy used), empty[S] (pair MMAs done with stage s),
+  // accf[2] (chunk in TMEM buffer b complete), acce[2] (buffer b drained by
+  // both CTAs; leader's copy used)
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * STAGES + 4);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int i0 = blockIdx.x * BM;              // this CTA's 128 output rows
+  const int j0 = blockIdx.y * PN;              // the pair's 256 output columns
+  const int jb = j0 + (int)rank * BN;          // this CTA's 128 columns of B
+  const int nk_all = (p.R + BK - 1) / BK;
+  const int kb0 = blockIdx.z * p.kb_per_split;
+  const int nk = max(0, min(nk_all - kb0, p.kb_per_split));
+  const int nchunks = (nk + CHUNK_KB - 1) / CHUNK_KB;
+  float *const Cout = p.C + (size_t)blockIdx.z * p.split_stride;
+  const uint32_t smem_base = smem_u32(smem);
+  auto bar_full = [&](int s) { return smem_u32(&bars[s]); };
+  auto bar_ready = [&](int s) { return smem_u32(&bars[STAGES + s]); };
+  auto bar_empty = [&](int s) { return smem_u32(&bars[2 * STAGES + s]); };
+  auto bar_accf = [&](int b) { return smem_u32(&bars[3 * STAGES + b]); };
+  auto bar_acce = [&](int b) { return smem_u32(&bars[3 * STAGES + 2 + b]); };
+  const uint32_t peer_flag = cluster_map(smem_u32((const void *)abort_flag), rank ^ 1u);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; s++) {
+      mbar_init(bar_full(s), 1);
+      mbar_init(bar_ready(s), PAIR_SIGNALLERS);
+      mbar_init(bar_empty(s), 1);
+    }
+    for (int b = 0; b < 2; b++) {
+      mbar_init(bar_accf(b), 1);
+      mbar_init(bar_acce(b), PAIR_SIGNALLERS);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(PAIR_TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  // Both CTAs' barriers are initialised and TMEM allocated before any signal
+  // crosses the pair.
+  tc_fence_before();
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int issued = 0;
+      for (int kb = 0; kb < nk; kb++) {
+        const int s = kb % STAGES, u = kb / STAGES;
+        if (u > 0 && !mbar_wait_pair(bar_empty(s), (u - 1) & 1, abort_flag, peer_flag, p.err, 1)) break;
+        issued = kb + 1;
+        const uint32_t st = smem_base + s * STAGE_BYTES;
+        mbar_arrive_expect_tx(bar_full(s), TX_BYTES);
+        const int k0 = (kb0 + kb) * BK;
+        if (A_MN) {
+#pragma unroll
+          for (int b = 0; b < BM / 32; b++) tma_load_2d(st + OFF_AHI + b * 4096, &tmA, bar_full(s), i0 + 32 * b, k0);
+        } else {
+          tma_load_2d(st + OFF_AHI, &tmA, bar_full(s), k0, i0);
+        }
+        if (B_MN) {
+#pragma unroll
+          for (int b = 0; b < BN / 32; b++) tma_load_2d(st + OFF_BHI + b * 4096, &tmB, bar_full(s), jb + 32 * b, k0);
+        } else {
+          tma_load_2d(st + OFF_BHI, &tmB, bar_full(s), k0, jb);
+        }
+      }
+      // No copy may still be landing when the CTA exits.
+      for (int kb = issued > STAGES ? issued - STAGES : 0; kb < issued; kb++) {
+        const long long t0 = clock64();
+        while (!mbar_try_wait(bar_full(kb % STAGES), (kb / STAGES) & 1)) {
+          if (clock64() - t0 > WAIT_LIMIT_CYCLES) { atomicExch(p.err, 6); break; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------- MMA issuer (leader CTA only)
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = make_idesc_pair(A_MN, B_MN);
+      int chunk = 0, kin = 0, last_committed = -1;
+      for (int kb = 0; kb < nk; kb++) {
+        const int s = kb % STAGES, u = kb / STAGES;
+        const int b = chunk & 1;
+        if (kin == 0 && chunk >= 2 &&
+            !mbar_wait_pair(bar_acce(b), ((chunk >> 1) - 1) & 1, abort_flag, peer_flag, p.err, 7))
+          break;
+        if (!mbar_wait_pair(bar_ready(s), u & 1, abort_flag, peer_flag, p.err, 2)) break;
+        tc_fence_after();
+        const uint32_t st = smem_base + s * STAGE_BYTES;
+        const uint32_t d = tmem + b * PN;
+#pragma unroll
+        for (int kk = 0; kk < BK / 8; kk++) {
+          const uint32_t a_off = A_MN ? kk * 1024 : kk * 32;
+          const uint32_t b_off = B_MN ? kk * 1024 : kk * 32;
+          constexpr uint32_t a_lbo = A_MN ? 4096 : 16, b_lbo = B_MN ? 4096 : 16;
+          constexpr uint32_t a_sbo = A_MN ? 512 : 1024, b_sbo = B_MN ? 512 : 1024;
+          constexpr uint32_t a_lay = A_MN ? LAYOUT_SW128_BASE32B : LAYOUT_SW128;
+          constexpr uint32_t b_lay = B_MN ? LAYOUT_SW128_BASE32B : LAYOUT_SW128;
+          const uint64_t a_hi = smem_desc(st + OFF_AHI + a_off, a_lbo, a_sbo, a_lay);
+          const uint64_t a_lo = smem_desc(st + OFF_ALO + a_off, a_lbo, a_sbo, a_lay);
+          const uint64_t b_hi = smem_desc(st + OFF_BHI + b_off, b_lbo, b_sbo, b_lay);
+          const uint64_t b_lo = smem_desc(st + OFF_BLO + b_off, b_lbo, b_sbo, b_lay);
+          tc_mma_pair(d, a_lo, b_hi, idesc, (kin > 0 || kk > 0) ? 1u : 0u);
+          tc_mma_pair(d, a_hi, b_lo, idesc, 1);
+          tc_mma_pair(d, a_hi, b_hi, idesc, 1);
+        }
+        tc_commit_pair(bar_empty(s));
+        if (++kin == CHUNK_KB || kb == nk - 1) {
+          tc_commit_pair(bar_accf(b));
+          last_committed = chunk;
+          chunk++;
+          kin = 0;
+        }
+      }
+      // Leave with the pair's MMAs finished (also on the abort path), so TMEM
+      // is idle before it is released.
+      if (kin > 0 || last_committed < chunk - 1 || last_committed < 0) {
+        tc_commit_pair(bar_accf(chunk & 1));
+        last_committed = chunk;
+      }
+      const int b = last_committed & 1;
+      const long long t0 = clock64();
+      while (!mbar_try_wait(bar_accf(b), (last_committed >> 1) & 1)) {
+        if (clock64() - t0 > WAIT_LIMIT_CYCLES) { pair_abort(abort_flag, peer_flag, p.err, 3); break; }
+      }
+    }
+  } else {
+    // ------------------------------ split + fp32 accumulation (warps 2..9)
+    // Warp w reads TMEM lanes 32*(w%4).. (its sub-partition) and accumulates
+    // columns [128*h, 128*h + 128) of this CTA's 256, h = (w-2)/4.  Chunk c is
+    // drained once all its k-blocks are split and its commit has landed,
+    // polled between k-blocks and forced PAIR_DRAIN_LAG k-blocks later.
+    const int t = threadIdx.x - 64;  // 0..255
+    const int q = warp & 3, h = (warp - 2) >> 2;
+    float acc[BN];
+#pragma unroll
+    for (int e = 0; e < BN; e++) acc[e] = 0.0f;
+    bool ok = true;
+    int kb = 0, c = 0;
+    while (kb < nk || c < nchunks) {
+      bool drain = false;
+      if (c < nchunks) {
+        const int c_end = min((c + 1) * CHUNK_KB, nk);
+        if (kb >= nk || kb >= c_end + PAIR_DRAIN_LAG) {
+          drain = true;
+        } else if (kb >= c_end) {
+          const uint32_t done = lane == 0 ? (mbar_try_wait_cl(bar_accf(c & 1), (c >> 1) & 1) ? 1u : 0u) : 0u;
+          drain = __shfl_sync(0xffffffffu, done, 0) != 0;
+        }
+      }
+      if (drain) {
+        const int b = c & 1;
+        // The whole warp leaves together: tcgen05.ld below is warp-collective.
+        const bool landed = mbar_wait_pair(bar_accf(b), (c >> 1) & 1, abort_flag, peer_flag, p.err, 5);
+        if (!__all_sync(0xffffffffu, landed)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int cc = 0; cc < BN / 32; cc++) {
+          uint32_t v[32];
+          const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + b * PN + h * BN + cc * 32;
+          asm volatile(
+              "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+              "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+              : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+                "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]),
+                "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]),
+                "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]),
+                "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+              : "r"(taddr));
+          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+          for (int e = 0; e < 32; e++) acc[cc * 32 + e] += __uint_as_float(v[e]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote(cluster_map(bar_acce(b), 0));
+        c++;
+      } else {
+        const int s = kb % STAGES, u = kb / STAGES;
+        const bool landed = mbar_wait_pair(bar_full(s), u & 1, abort_flag, peer_flag, p.err, 4);
+        if (!__all_sync(0xffffffffu, landed)) { ok = false; break; }
+        uint8_t *st = smem + s * STAGE_BYTES;
+        // A tile then this CTA's B half: 2 x 1024 float4 of raw data, 8 per thread.
+#pragma unroll 4
+        for (int e = 0; e < 8; e++) {
+          const int idx = e * 256 + t;                  // 0..2047
+          const int off = idx < 1024 ? OFF_AHI + idx * 16 : OFF_BHI + (idx - 1024) * 16;
+          const float4 x = *reinterpret_cast<const float4 *>(st + off);
+          float4 lo;
+          lo.x = x.x - tf32_trunc(x.x); lo.y = x.y - tf32_trunc(x.y);
+          lo.z = x.z - tf32_trunc(x.z); lo.w = x.w - tf32_trunc(x.w);
+          *reinterpret_cast<float4 *>(st + off + (idx < 1024 ? TILE_A : TILE_B)) = lo;
+        }
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote(cluster_map(bar_ready(s), 0));
+        kb++;
+      }
+    }
+    if (ok && !*abort_flag) {
+      const int row = i0 + q * 32 + lane;
+      const int jc = j0 + h * BN;
+      if (row < p.I) {
+        float *dst = Cout + (size_t)row * p.ldc + jc;
+        if (jc + BN <= p.J) {
+#pragma unroll
+          for (int e = 0; e < BN; e += 4) {
+            float4 o = make_float4(acc[e], acc[e + 1], acc[e + 2], acc[e + 3]);
+            float4 *d4 = reinterpret_cast<float4 *>(dst + e);
+            if (p.beta) {
+              const float4 old = *d4;
+              o.x += old.x; o.y += old.y; o.z += old.z; o.w += old.w;
+            }
+            *d4 = o;
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < BN; e++) {
+            if (jc + e < p.J) dst[e] = p.beta ? dst[e] + acc[e] : acc[e];
+          }
+        }
+      }
+    }
+  }
+  // Neither CTA releases TMEM or exits while the pair's MMAs, TMEM reads or
+  // cross-CTA signals may still be in flight.
+  tc_fence_before();
+  cluster_sync_all();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(PAIR_TMEM_COLS) : "memory");
+  }
+}
+
 // ------------------------------------------------------------------- host
 static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
@@ -453,6 +794,23 @@ static int launch(DeviceCtx *c, const CUtensorMap &ma, const CUtensorMap &mb, co
   return TL_OK;
 }
 
+// CTA pairs: grid x runs over 128-row halves (cluster of 2 along x), y over
+// 256-column tiles, z over K splits.
+template <bool A_MN, bool B_MN>
+static int launch_pair(DeviceCtx *c, const CUtensorMap &ma, const CUtensorMap &mb, const Params &p, int splits) {
+  static bool attr_set[kMaxDevices] = {};
+  if (!attr_set[c->device]) {
+    TL_TRY_CUDA(cudaFuncSetAttribute(gemm_tc_pair_kernel<A_MN, B_MN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     SMEM_BYTES));
+    attr_set[c->device] = true;
+  }
+  dim3 grid(2 * ((p.I + PM - 1) / PM), (p.J + PN - 1) / PN, splits);
+  TraceScope ts(c, "gemm_tc_pair");
+  gemm_tc_pair_kernel<A_MN, B_MN><<<grid, NUM_THREADS, SMEM_BYTES, c->stream>>>(ma, mb, p);
+  TL_TRY_CUDA(cudaGetLastError());
+  return TL_OK;
+}
+
 }  // namespace tc
 
 bool gemm_tc_supported(GemmOp op, const float *C, const float *A, const float *B, int M, int K, int N) {
@@ -464,10 +822,16 @@ bool gemm_tc_supported(GemmOp op, const float *C, const float *A, const float *B
   int I, J, R;
   gemm_dims(op, M, K, N, &I, &J, &R);
   if ((I + tc::BM - 1) / tc::BM > 65535) return false;
+  if ((J + tc::PN - 1) / tc::PN > 65535) return false;
   return true;
 }
 
-int gemm_tc(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, int M, int K, int N) {
+bool gemm_tc_prefer_pair(int I, int J, int R) {
+  (void)R;
+  return I > tc::BM && J > tc::BN;
+}
+
+int gemm_tc(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, int M, int K, int N, bool pair) {
   int rc;
   if ((rc = tc::get_encoder())) return rc;
   int I, J, R;
@@ -478,13 +842,15 @@ int gemm_tc(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, i
   // gradients of narrow layers, whose reduction runs over all tokens): each
   // split gets at least one TMEM chunk of k-blocks, partials go to the
   // context's workspace and a fixed-order reduction adds them into C.
-  const int tiles = ((I + tc::BM - 1) / tc::BM) * ((J + tc::BN - 1) / tc::BN);
+  // A pair tile (256 x 256) occupies two SMs.
+  const int tm = pair ? tc::PM : tc::BM, tn = pair ? tc::PN : tc::BN, sms_per_tile = pair ? 2 : 1;
+  const int tiles = ((I + tm - 1) / tm) * ((J + tn - 1) / tn);
   const int nk = (R + tc::BK - 1) / tc::BK;
   int splits = 1;
-  if (tiles < c->num_sms && c->gemm_ws) {
-    splits = c->num_sms / tiles;
+  if (tiles * sms_per_tile < c->num_sms && c->gemm_ws) {
+    splits = c->num_sms / (tiles * sms_per_tile);
     splits = std::min(splits, nk / tc::CHUNK_KB);
-    splits = std::min(splits, 16);
+    splits = std::min(splits, 64);
     const size_t cap = c->gemm_ws_floats / ((size_t)I * J);
     splits = (int)std::min<size_t>((size_t)splits, cap);
     if (splits < 2) splits = 1;
@@ -521,9 +887,15 @@ int gemm_tc(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, i
     p.ldc = out_ldc; p.beta = out_beta; p.split_stride = 0;
   }
   switch (op) {
-    case GemmOp::NN: rc = tc::launch<false, true>(c, ma, mb, p, splits); break;
-    case GemmOp::NT: rc = tc::launch<false, false>(c, ma, mb, p, splits); break;
-    case GemmOp::TN: rc = tc::launch<true, true>(c, ma, mb, p, splits); break;
+    case GemmOp::NN:
+      rc = pair ? tc::launch_pair<false, true>(c, ma, mb, p, splits) : tc::launch<false, true>(c, ma, mb, p, splits);
+      break;
+    case GemmOp::NT:
+      rc = pair ? tc::launch_pair<false, false>(c, ma, mb, p, splits) : tc::launch<false, false>(c, ma, mb, p, splits);
+      break;
+    case GemmOp::TN:
+      rc = pair ? tc::launch_pair<true, true>(c, ma, mb, p, splits) : tc::launch<true, true>(c, ma, mb, p, splits);
+      break;
   }
   if (rc || splits == 1) return rc;
   TraceScope ts(c, "gemm_splitk_reduce");
