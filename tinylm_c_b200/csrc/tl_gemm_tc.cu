@@ -398,16 +398,39 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 // one-CTA kernel, and L2 serves half the operand bytes per flop.  Tiles in
 // shared memory have the one-CTA kernel's shapes and layouts.
 //
+// Shared memory holds two rings: RAW_STAGES slots of raw tiles (what TMA
+// lands; read by the MMA as hi) and LO_STAGES slots of lo tiles (written by
+// the split warps).  The raw ring is the deeper one, so loads run up to
+// RAW_STAGES k-blocks ahead of the tensor pipe and hide DRAM latency.
+//
 // Roles: warp 0 loads this CTA's A and B halves (TMA into its own shared
 // memory, no multicast); warp 1 of the leader CTA (rank 0) issues the MMAs of
 // the pair; warps 2-9 of both CTAs write the lo parts of the landed tiles and
-// drain finished TMEM chunks into fp32 registers.  Warps of either CTA signal
-// the leader's `ready`/`acce` barriers through cluster addresses; the
-// leader's commits arrive on the `empty`/`accf` barriers of both CTAs.
+// drain finished TMEM chunks into fp32 registers.  Every split warp of both
+// CTAs signals the leader's `ready` barrier once per k-block and its `acce`
+// barrier once per chunk, through cluster addresses; the leader's commits
+// arrive on the `rempty`/`lempty`/`accf` barriers of both CTAs.
+//
+// Output tiles are visited in groups of PAIR_GROUP_M pair-rows, so the pairs
+// resident at one time share rows of A and columns of B in L2.
 constexpr int PM = 2 * BM, PN = 2 * BN;                 // 256 x 256 per pair
+#ifndef TL_PAIR_RAW_STAGES
+#define TL_PAIR_RAW_STAGES 4
+#endif
+#ifndef TL_PAIR_LO_STAGES
+#define TL_PAIR_LO_STAGES 3
+#endif
+#ifndef TL_PAIR_GROUP_M
+#define TL_PAIR_GROUP_M 4
+#endif
+constexpr int RAW_STAGES = TL_PAIR_RAW_STAGES, LO_STAGES = TL_PAIR_LO_STAGES;
+constexpr int RAW_BYTES = TILE_A + TILE_B;              // 32 KB: A rows, then this CTA's B half
+constexpr int PAIR_SMEM_BYTES = (RAW_STAGES + LO_STAGES) * RAW_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 constexpr int PAIR_TMEM_COLS = 2 * PN;                  // two 256-column accumulators
 constexpr int PAIR_SIGNALLERS = 2 * 8;                  // split/drain warps in the pair
 constexpr int PAIR_DRAIN_LAG = 2;                       // k-blocks split ahead of a forced drain
+constexpr int PAIR_GROUP_M = TL_PAIR_GROUP_M;           // pair-rows per tile group
+static_assert(PAIR_SMEM_BYTES <= 232448, "pair kernel exceeds the opt-in shared memory per block");
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
@@ -419,8 +442,13 @@ __device__ __forceinline__ uint32_t cluster_map(uint32_t addr, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
   return r;
 }
+// Arrive on a barrier of either CTA of the pair (default .release.cta
+// semantics).  Callers have already ordered their shared-memory writes for the
+// tensor pipe with fence.proxy.async.  A .release.cluster arrive here costs
+// ~1 us per call (measured: the pair kernel ran at 173 TFLOP/s with it and at
+// 246 without).
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 __device__ __forceinline__ bool mbar_try_wait_cl(uint32_t bar, uint32_t parity) {
   uint32_t ok;
@@ -481,37 +509,50 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
 gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
-  // bars: full[S] (this CTA's TMA landed), ready[S] (both CTAs' lo parts
-  // written; leader's copy used), empty[S] (pair MMAs done with stage s),
-  // accf[2] (chunk in TMEM buffer b complete), acce[2] (buffer b drained by
-  // both CTAs; leader's copy used)
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * STAGES + 4);
+  uint8_t *raw_ring = smem, *lo_ring = smem + RAW_STAGES * RAW_BYTES;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(lo_ring + LO_STAGES * RAW_BYTES);
+  // bars: full[R] (this CTA's raw slot landed), rempty[R] (pair MMAs done
+  // with raw slot), ready[L] (both CTAs' lo slot written; leader's copy
+  // used), lempty[L] (pair MMAs done with lo slot), accf[2] (chunk in TMEM
+  // buffer b complete), acce[2] (buffer b drained; leader's copy used)
+  constexpr int NBARS = 2 * RAW_STAGES + 2 * LO_STAGES + 4;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + NBARS);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
-  const int i0 = blockIdx.x * BM;              // this CTA's 128 output rows
-  const int j0 = blockIdx.y * PN;              // the pair's 256 output columns
+  // Grouped tile order over the pairs: pair L (launch order) -> (pm, tn).
+  const int npm = (p.I + PM - 1) / PM, ntn = (p.J + PN - 1) / PN;
+  const int L = blockIdx.x >> 1;
+  const int group = L / (PAIR_GROUP_M * ntn), first_pm = group * PAIR_GROUP_M;
+  const int gsz = min(npm - first_pm, PAIR_GROUP_M);
+  const int in_group = L - group * PAIR_GROUP_M * ntn;
+  const int pm = first_pm + in_group % gsz, tn = in_group / gsz;
+  const int i0 = (2 * pm + (int)rank) * BM;    // this CTA's 128 output rows
+  const int j0 = tn * PN;                      // the pair's 256 output columns
   const int jb = j0 + (int)rank * BN;          // this CTA's 128 columns of B
   const int nk_all = (p.R + BK - 1) / BK;
   const int kb0 = blockIdx.z * p.kb_per_split;
   const int nk = max(0, min(nk_all - kb0, p.kb_per_split));
   const int nchunks = (nk + CHUNK_KB - 1) / CHUNK_KB;
   float *const Cout = p.C + (size_t)blockIdx.z * p.split_stride;
-  const uint32_t smem_base = smem_u32(smem);
+  const uint32_t raw_base = smem_u32(raw_ring), lo_base = smem_u32(lo_ring);
   auto bar_full = [&](int s) { return smem_u32(&bars[s]); };
-  auto bar_ready = [&](int s) { return smem_u32(&bars[STAGES + s]); };
-  auto bar_empty = [&](int s) { return smem_u32(&bars[2 * STAGES + s]); };
-  auto bar_accf = [&](int b) { return smem_u32(&bars[3 * STAGES + b]); };
-  auto bar_acce = [&](int b) { return smem_u32(&bars[3 * STAGES + 2 + b]); };
+  auto bar_rempty = [&](int s) { return smem_u32(&bars[RAW_STAGES + s]); };
+  auto bar_ready = [&](int s) { return smem_u32(&bars[2 * RAW_STAGES + s]); };
+  auto bar_lempty = [&](int s) { return smem_u32(&bars[2 * RAW_STAGES + LO_STAGES + s]); };
+  auto bar_accf = [&](int b) { return smem_u32(&bars[2 * RAW_STAGES + 2 * LO_STAGES + b]); };
+  auto bar_acce = [&](int b) { return smem_u32(&bars[2 * RAW_STAGES + 2 * LO_STAGES + 2 + b]); };
   const uint32_t peer_flag = cluster_map(smem_u32((const void *)abort_flag), rank ^ 1u);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; s++) {
+    for (int s = 0; s < RAW_STAGES; s++) {
       mbar_init(bar_full(s), 1);
+      mbar_init(bar_rempty(s), 1);
+    }
+    for (int s = 0; s < LO_STAGES; s++) {
       mbar_init(bar_ready(s), PAIR_SIGNALLERS);
-      mbar_init(bar_empty(s), 1);
+      mbar_init(bar_lempty(s), 1);
     }
     for (int b = 0; b < 2; b++) {
       mbar_init(bar_accf(b), 1);
@@ -538,29 +579,29 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     if (lane == 0) {
       int issued = 0;
       for (int kb = 0; kb < nk; kb++) {
-        const int s = kb % STAGES, u = kb / STAGES;
-        if (u > 0 && !mbar_wait_pair(bar_empty(s), (u - 1) & 1, abort_flag, peer_flag, p.err, 1)) break;
+        const int s = kb % RAW_STAGES, u = kb / RAW_STAGES;
+        if (u > 0 && !mbar_wait_pair(bar_rempty(s), (u - 1) & 1, abort_flag, peer_flag, p.err, 1)) break;
         issued = kb + 1;
-        const uint32_t st = smem_base + s * STAGE_BYTES;
+        const uint32_t st = raw_base + s * RAW_BYTES;
         mbar_arrive_expect_tx(bar_full(s), TX_BYTES);
         const int k0 = (kb0 + kb) * BK;
         if (A_MN) {
 #pragma unroll
-          for (int b = 0; b < BM / 32; b++) tma_load_2d(st + OFF_AHI + b * 4096, &tmA, bar_full(s), i0 + 32 * b, k0);
+          for (int b = 0; b < BM / 32; b++) tma_load_2d(st + b * 4096, &tmA, bar_full(s), i0 + 32 * b, k0);
         } else {
-          tma_load_2d(st + OFF_AHI, &tmA, bar_full(s), k0, i0);
+          tma_load_2d(st, &tmA, bar_full(s), k0, i0);
         }
         if (B_MN) {
 #pragma unroll
-          for (int b = 0; b < BN / 32; b++) tma_load_2d(st + OFF_BHI + b * 4096, &tmB, bar_full(s), jb + 32 * b, k0);
+          for (int b = 0; b < BN / 32; b++) tma_load_2d(st + TILE_A + b * 4096, &tmB, bar_full(s), jb + 32 * b, k0);
         } else {
-          tma_load_2d(st + OFF_BHI, &tmB, bar_full(s), k0, jb);
+          tma_load_2d(st + TILE_A, &tmB, bar_full(s), k0, jb);
         }
       }
       // No copy may still be landing when the CTA exits.
-      for (int kb = issued > STAGES ? issued - STAGES : 0; kb < issued; kb++) {
+      for (int kb = issued > RAW_STAGES ? issued - RAW_STAGES : 0; kb < issued; kb++) {
         const long long t0 = clock64();
-        while (!mbar_try_wait(bar_full(kb % STAGES), (kb / STAGES) & 1)) {
+        while (!mbar_try_wait(bar_full(kb % RAW_STAGES), (kb / RAW_STAGES) & 1)) {
           if (clock64() - t0 > WAIT_LIMIT_CYCLES) { atomicExch(p.err, 6); break; }
         }
       }
@@ -571,32 +612,33 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
       constexpr uint32_t idesc = make_idesc_pair(A_MN, B_MN);
       int chunk = 0, kin = 0, last_committed = -1;
       for (int kb = 0; kb < nk; kb++) {
-        const int s = kb % STAGES, u = kb / STAGES;
+        const int rs = kb % RAW_STAGES, ls = kb % LO_STAGES;
         const int b = chunk & 1;
         if (kin == 0 && chunk >= 2 &&
             !mbar_wait_pair(bar_acce(b), ((chunk >> 1) - 1) & 1, abort_flag, peer_flag, p.err, 7))
           break;
-        if (!mbar_wait_pair(bar_ready(s), u & 1, abort_flag, peer_flag, p.err, 2)) break;
+        if (!mbar_wait_pair(bar_ready(ls), (kb / LO_STAGES) & 1, abort_flag, peer_flag, p.err, 2)) break;
         tc_fence_after();
-        const uint32_t st = smem_base + s * STAGE_BYTES;
+        const uint32_t hi = raw_base + rs * RAW_BYTES, lo = lo_base + ls * RAW_BYTES;
         const uint32_t d = tmem + b * PN;
 #pragma unroll
         for (int kk = 0; kk < BK / 8; kk++) {
           const uint32_t a_off = A_MN ? kk * 1024 : kk * 32;
-          const uint32_t b_off = B_MN ? kk * 1024 : kk * 32;
+          const uint32_t b_off = (B_MN ? kk * 1024 : kk * 32) + TILE_A;
           constexpr uint32_t a_lbo = A_MN ? 4096 : 16, b_lbo = B_MN ? 4096 : 16;
           constexpr uint32_t a_sbo = A_MN ? 512 : 1024, b_sbo = B_MN ? 512 : 1024;
           constexpr uint32_t a_lay = A_MN ? LAYOUT_SW128_BASE32B : LAYOUT_SW128;
           constexpr uint32_t b_lay = B_MN ? LAYOUT_SW128_BASE32B : LAYOUT_SW128;
-          const uint64_t a_hi = smem_desc(st + OFF_AHI + a_off, a_lbo, a_sbo, a_lay);
-          const uint64_t a_lo = smem_desc(st + OFF_ALO + a_off, a_lbo, a_sbo, a_lay);
-          const uint64_t b_hi = smem_desc(st + OFF_BHI + b_off, b_lbo, b_sbo, b_lay);
-          const uint64_t b_lo = smem_desc(st + OFF_BLO + b_off, b_lbo, b_sbo, b_lay);
+          const uint64_t a_hi = smem_desc(hi + a_off, a_lbo, a_sbo, a_lay);
+          const uint64_t a_lo = smem_desc(lo + a_off, a_lbo, a_sbo, a_lay);
+          const uint64_t b_hi = smem_desc(hi + b_off, b_lbo, b_sbo, b_lay);
+          const uint64_t b_lo = smem_desc(lo + b_off, b_lbo, b_sbo, b_lay);
           tc_mma_pair(d, a_lo, b_hi, idesc, (kin > 0 || kk > 0) ? 1u : 0u);
           tc_mma_pair(d, a_hi, b_lo, idesc, 1);
           tc_mma_pair(d, a_hi, b_hi, idesc, 1);
         }
-        tc_commit_pair(bar_empty(s));
+        tc_commit_pair(bar_lempty(ls));
+        tc_commit_pair(bar_rempty(rs));
         if (++kin == CHUNK_KB || kb == nk - 1) {
           tc_commit_pair(bar_accf(b));
           last_committed = chunk;
@@ -668,24 +710,28 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         if (lane == 0) mbar_arrive_remote(cluster_map(bar_acce(b), 0));
         c++;
       } else {
-        const int s = kb % STAGES, u = kb / STAGES;
-        const bool landed = mbar_wait_pair(bar_full(s), u & 1, abort_flag, peer_flag, p.err, 4);
+        const int rs = kb % RAW_STAGES, ls = kb % LO_STAGES;
+        bool landed = mbar_wait_pair(bar_full(rs), (kb / RAW_STAGES) & 1, abort_flag, peer_flag, p.err, 4);
+        if (landed && kb >= LO_STAGES)
+          landed = mbar_wait_pair(bar_lempty(ls), ((kb / LO_STAGES) - 1) & 1, abort_flag, peer_flag, p.err, 8);
         if (!__all_sync(0xffffffffu, landed)) { ok = false; break; }
-        uint8_t *st = smem + s * STAGE_BYTES;
-        // A tile then this CTA's B half: 2 x 1024 float4 of raw data, 8 per thread.
-#pragma unroll 4
+        const uint8_t *src = raw_ring + rs * RAW_BYTES;
+        uint8_t *dst = lo_ring + ls * RAW_BYTES;
+        // A tile then this CTA's B half: 2048 float4 of raw data, 8 per thread;
+        // lo lands at the same offset of the lo slot (same swizzled layout).
+#pragma unroll
         for (int e = 0; e < 8; e++) {
-          const int idx = e * 256 + t;                  // 0..2047
-          const int off = idx < 1024 ? OFF_AHI + idx * 16 : OFF_BHI + (idx - 1024) * 16;
-          const float4 x = *reinterpret_cast<const float4 *>(st + off);
+          const int off = (e * 256 + t) * 16;
+          const float4 x = *reinterpret_cast<const float4 *>(src + off);
           float4 lo;
           lo.x = x.x - tf32_trunc(x.x); lo.y = x.y - tf32_trunc(x.y);
           lo.z = x.z - tf32_trunc(x.z); lo.w = x.w - tf32_trunc(x.w);
-          *reinterpret_cast<float4 *>(st + off + (idx < 1024 ? TILE_A : TILE_B)) = lo;
+          *reinterpret_cast<float4 *>(dst + off) = lo;
         }
+        // Every writer orders its stores before the tensor pipe's reads.
         fence_proxy_async();
         __syncwarp();
-        if (lane == 0) mbar_arrive_remote(cluster_map(bar_ready(s), 0));
+        if (lane == 0) mbar_arrive_remote(cluster_map(bar_ready(ls), 0));
         kb++;
       }
     }
@@ -794,19 +840,20 @@ static int launch(DeviceCtx *c, const CUtensorMap &ma, const CUtensorMap &mb, co
   return TL_OK;
 }
 
-// CTA pairs: grid x runs over 128-row halves (cluster of 2 along x), y over
-// 256-column tiles, z over K splits.
+// CTA pairs: grid x runs over the pairs' CTAs (cluster of 2 along x; the
+// kernel maps pairs to output tiles in grouped order), z over K splits.
 template <bool A_MN, bool B_MN>
 static int launch_pair(DeviceCtx *c, const CUtensorMap &ma, const CUtensorMap &mb, const Params &p, int splits) {
   static bool attr_set[kMaxDevices] = {};
   if (!attr_set[c->device]) {
     TL_TRY_CUDA(cudaFuncSetAttribute(gemm_tc_pair_kernel<A_MN, B_MN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     SMEM_BYTES));
+                                     PAIR_SMEM_BYTES));
     attr_set[c->device] = true;
   }
-  dim3 grid(2 * ((p.I + PM - 1) / PM), (p.J + PN - 1) / PN, splits);
+  const unsigned pairs = (unsigned)((p.I + PM - 1) / PM) * (unsigned)((p.J + PN - 1) / PN);
+  dim3 grid(2 * pairs, 1, splits);
   TraceScope ts(c, "gemm_tc_pair");
-  gemm_tc_pair_kernel<A_MN, B_MN><<<grid, NUM_THREADS, SMEM_BYTES, c->stream>>>(ma, mb, p);
+  gemm_tc_pair_kernel<A_MN, B_MN><<<grid, NUM_THREADS, PAIR_SMEM_BYTES, c->stream>>>(ma, mb, p);
   TL_TRY_CUDA(cudaGetLastError());
   return TL_OK;
 }
@@ -822,7 +869,7 @@ bool gemm_tc_supported(GemmOp op, const float *C, const float *A, const float *B
   int I, J, R;
   gemm_dims(op, M, K, N, &I, &J, &R);
   if ((I + tc::BM - 1) / tc::BM > 65535) return false;
-  if ((J + tc::PN - 1) / tc::PN > 65535) return false;
+  if (2LL * ((I + tc::PM - 1) / tc::PM) * ((J + tc::PN - 1) / tc::PN) > 0x7fffffffLL) return false;
   return true;
 }
 
