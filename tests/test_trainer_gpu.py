@@ -115,3 +115,59 @@ def test_micro_batched_trainer_matches_whole_batch(cuda, tmp_path):
         t.close()
     assert np.allclose(out[0][0], out[1][0], atol=1e-5)
     assert np.max(np.abs(out[0][1] - out[1][1])) < 1e-6
+
+
+def _torchrun(script_args, port):
+    script = os.path.join(os.path.dirname(__file__), "trainer_multi.py")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    import subprocess
+    import sys
+    r = subprocess.run(["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run",
+                        "--nnodes=1", "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={port}",
+                        script] + script_args, capture_output=True, text=True, env=env)
+    assert r.returncode == 0 and "TRAINER_OK" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
+    return [ln[4:] for ln in r.stdout.splitlines() if ln.startswith("VAL ")]
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_rank_trainer_matches_one_rank(cuda, tmp_path):
+    """Data parallel over 2 GPUs (each rank half of the global batch, ZeRO-1
+    step, shard-wise TOPT writes) against the one-rank trainer on the same
+    global batch: same validation losses, parameters and optimizer state up
+    to the rounding of the cross-rank gradient average.  Then both resume
+    from one-rank files written at iteration 3."""
+    tr, vl = streams()
+    cfg = model.cfg8("nano", 0)
+    one = (str(tmp_path / "w1.bin"), str(tmp_path / "w1.opt"))
+    t = trainer.Trainer(cfg, 4, device=0)
+    lines1 = []
+    t.run(tr, vl, 6, LR, seed=0, out=one[0], optpath=one[1], log=lines1.append)
+    n = t.n
+    t.close()
+    lines2 = _torchrun([str(tmp_path), "fresh"], 29541)
+    v1, v2 = vals(lines1), vals(lines2)
+    assert [i for i, _ in v1] == [i for i, _ in v2] == [0, 6]
+    for (_, a), (_, b) in zip(v1, v2):
+        assert abs(a - b) <= 2e-4, (v1, v2)
+    P0 = model.init_params(cfg, 0).numpy().astype(np.float64)
+    compare_runs((str(tmp_path / "w2.bin"), str(tmp_path / "w2.opt")), one, P0, n)
+
+    # resume: one-rank files at iteration 3, continued by 1 and by 2 ranks
+    a = (str(tmp_path / "a.bin"), str(tmp_path / "a.opt"))
+    t = trainer.Trainer(cfg, 4, device=0)
+    t.run(tr, vl, 3, LR, seed=0, out=a[0], optpath=a[1], log=lambda *_: None)
+    t.close()
+    r1 = (str(tmp_path / "r1.bin"), str(tmp_path / "r1.opt"))
+    for dst in (r1, (str(tmp_path / "w2r.bin"), str(tmp_path / "w2r.opt"))):
+        shutil.copy(a[0], dst[0]); shutil.copy(a[1], dst[1])
+    t = trainer.Trainer(cfg, 4, device=0)
+    lines1 = []
+    t.run(tr, vl, 6, LR, seed=0, out=r1[0], optpath=r1[1], resume=True, log=lines1.append)
+    t.close()
+    lines2 = _torchrun([str(tmp_path), "resume"], 29543)
+    v1, v2 = vals(lines1), vals(lines2)
+    assert [i for i, _ in v1] == [i for i, _ in v2] == [3, 6]
+    for (_, x), (_, y) in zip(v1, v2):
+        assert abs(x - y) <= 2e-4, (v1, v2)
+    _, P3 = read_bundle(a[0], n)
+    compare_runs((str(tmp_path / "w2r.bin"), str(tmp_path / "w2r.opt")), r1, P3, n)
