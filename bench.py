@@ -71,6 +71,8 @@ def parse():
     ap.add_argument("--no-adamw-line", action="store_true", help="train: skip the config-2 AdamW sub-measurement")
     ap.add_argument("--shape", default="", help="gemm workload: one M,K,N instead of the sweep")
     ap.add_argument("--op", default="all", choices=["all", "mm", "mm_bt", "mm_atb"], help="gemm workload: primitive")
+    ap.add_argument("--zero1", default="nccl", choices=["nccl", "p2p"],
+                    help="N>1: ZeRO-1 exchanges by NCCL collectives or by the library's peer-memory kernels")
     ap.add_argument("--gemm-engine", type=int, default=0, choices=[0, 1, 2, 3],
                     help="GEMM engine: 0 automatic, 1 CUDA-core, 2 tensor-core one CTA, 3 tensor-core CTA pair")
     return ap.parse_args()
@@ -332,7 +334,7 @@ def run_train(args, rk):
         G = torch.zeros(n, device=dev)
     else:
         from tinylm_c_b200.zero1 import Zero1
-        z = Zero1(n, rank, world, rk.local)
+        z = Zero1(n, rank, world, rk.local, exchange=args.zero1)
         n_pad, shard = z.n_pad, z.shard
         P = torch.zeros(n_pad, device=dev)
         P[:n] = P0.to(dev)
@@ -431,7 +433,7 @@ def run_train(args, rk):
                "data": "synthetic (uniform random token ids, seeded); weights from the reference's seeded init_params",
                "config": {"workload": cfg_name, "model": preset, "n_params": n, "n_mtp": n_mtp,
                           "global_batch": B_glob, "seq_len": T_CTX, "micro_batch": mb,
-                          "parallelism": "single" if world == 1 else f"dp{world}_zero1",
+                          "parallelism": "single" if world == 1 else f"dp{world}_zero1_{args.zero1}",
                           "gemm_gflop_per_token": round(gflop_tok / 1e9, 4),
                           "l2": "per-step working set >> 126 MB L2 (no flush needed)"},
                "e2e": e2e, "roofline": roofline, "clocks": clocks, "gpu_launches": launches,
@@ -458,7 +460,7 @@ def run_adamw(args, rk, n):
             ops.clip_adamw(p, g, m, v, n, LR, B1, B2, WD, t, MAX_NORM, norm)
     else:
         from tinylm_c_b200.zero1 import Zero1
-        z = Zero1(n, rank, world, rk.local)
+        z = Zero1(n, rank, world, rk.local, exchange=args.zero1)
         shard = z.shard
         p = torch.zeros(z.n_pad, device=dev)
         g = torch.zeros(z.n_pad, device=dev)
@@ -499,11 +501,15 @@ def run_adamw(args, rk, n):
                "path": "pinned host G -> tl_clip_adamw_step / tl_zero1_step -> host norm; P,M,V resident"}
 
     peaks, peak_kind = measured_peaks()
-    adam = kernels.get("adamw_vec", {"ms_per_launch": 0})
+    # The peer-memory step's AdamW kernel also stores the shard into the other
+    # ranks' P (the fused all-gather); its algorithmic bytes here are the
+    # local 28 B/elem, like adamw_vec's.
+    kname = "p2p_adamw" if (world > 1 and args.zero1 == "p2p") else "adamw_vec"
+    adam = kernels.get(kname, {"ms_per_launch": 0})
     a_ms = adam["ms_per_launch"]
     achieved = shard * ADAMW_BYTES / (a_ms * 1e-3) / 1e9 if a_ms else None
     nk = kernels.get("sumsq", {"ms_per_launch": 0})
-    roofline = {"kernel": "adamw_vec", "bound": "hbm", "unit": "GB/s",
+    roofline = {"kernel": kname, "bound": "hbm", "unit": "GB/s",
                 "achieved": round(achieved, 1) if achieved else None, "peak": peaks["hbm_gbs"],
                 "peak_source": f"{peak_kind} HBM copy", "frac": round(achieved / peaks["hbm_gbs"], 4) if achieved else None,
                 "traffic": None, "algorithmic_bytes": shard * ADAMW_BYTES,
@@ -523,7 +529,7 @@ def run_adamw(args, rk, n):
             "data": "synthetic (seeded normals with config-2 distributions)",
             "config": {"workload": "config2_fused_adamw_clip" if world == 1 else "config2_zero1_adamw",
                        "n_params": n, "bytes_per_param": BYTES_PER_PARAM, "t_start": ADAMW_T0,
-                       "parallelism": "single" if world == 1 else f"zero1_dp{world}",
+                       "parallelism": "single" if world == 1 else f"zero1_dp{world}_{args.zero1}",
                        "l2": "inputs 4 GiB >> 126 MB L2 (no flush needed)"},
             "e2e": e2e, "roofline": roofline, "clocks": clocks, "gpu_launches": launches, "kernels": kernels}
 

@@ -223,6 +223,25 @@ int tl_dist_finalize(void);
 int tl_zero1_step(float *P, float *G, float *M_shard, float *V_shard, size_t n,
                   float lr, float b1, float b2, float wd, int t, float max_norm,
                   float *norm_dev);
+/* The same ZeRO-1 step with the exchanges done by this library's kernels over
+ * peer memory (one node, every GPU reachable over NVLink) instead of NCCL
+ * collectives: the averaged gradient of this rank's shard is summed straight
+ * from every rank's G (rank order 0..R-1) fused with the shard's sum of
+ * squares; shard sums are exchanged through peer stores; AdamW on the shard
+ * stores the updated parameters into every rank's P.  Same results as
+ * tl_zero1_step (bit for bit at R = 2, 4, 8).  Before the first step every rank
+ * registers its own P and G (n_pad floats each, 16-byte aligned, cudaMalloc
+ * memory that CUDA IPC can share) -- a collective call; tl_zero1_step_p2p must
+ * then be given exactly those buffers.  Device waits are bounded by
+ * TL_DIST_TIMEOUT_MS: on expiry the step records an error that
+ * tl_device_status() returns as TL_ETIMEOUT and the rest of the step touches
+ * no peer memory.  Up to 8 ranks.  No counterpart in the reference. */
+int tl_zero1_p2p_register(float *P, float *G, size_t n);
+int tl_zero1_step_p2p(float *P, float *G, float *M_shard, float *V_shard, size_t n,
+                      float lr, float b1, float b2, float wd, int t, float max_norm,
+                      float *norm_dev);
+/* Unmap the peers' buffers (after every rank's last step has completed). */
+int tl_zero1_p2p_release(void);
 /* Plain collectives on the library communicator (fp32, in place / out of place). */
 int tl_dist_allreduce_f32(float *buf, size_t count, int average);
 int tl_dist_allreduce_f64(double *buf, size_t count);

@@ -30,18 +30,39 @@ def main():
     p, _, m, v = oracle.adamw_inputs(n, seed=1)
     grads = [oracle.adamw_inputs(n, seed=100 + r)[1] * np.float32(40.0) for r in range(world)]
     gavg = (np.sum(np.stack(grads).astype(np.float64), axis=0) / world).astype(np.float32)
-    z = Zero1(n, rank, world, local)
+    exchange = sys.argv[2] if len(sys.argv) > 2 else "nccl"
+    z = Zero1(n, rank, world, local, exchange=exchange)
     n_pad, shard = zero1_layout(n, world)
     lo = rank * shard
-    P = torch.zeros(n_pad, device=dev); P[:n] = torch.from_numpy(p)
-    G = torch.zeros(n_pad, device=dev); G[:n] = torch.from_numpy(grads[rank])
     mp = np.zeros(n_pad, np.float32); mp[:n] = m
     vp = np.zeros(n_pad, np.float32); vp[:n] = v
-    M = torch.from_numpy(mp[lo:lo + shard].copy()).to(dev)
-    V = torch.from_numpy(vp[lo:lo + shard].copy()).to(dev)
-    norm = torch.zeros(1, device=dev)
-    z.step(P, G, M, V, LR, B1, B2, WD, 2, 1.0, norm)
-    z.sync(60000)
+
+    def run(zz):
+        P = torch.zeros(n_pad, device=dev); P[:n] = torch.from_numpy(p)
+        G = torch.zeros(n_pad, device=dev); G[:n] = torch.from_numpy(grads[rank])
+        M = torch.from_numpy(mp[lo:lo + shard].copy()).to(dev)
+        V = torch.from_numpy(vp[lo:lo + shard].copy()).to(dev)
+        norm = torch.zeros(1, device=dev)
+        zz.step(P, G, M, V, LR, B1, B2, WD, 2, 1.0, norm)
+        zz.sync(60000)
+        return P, G, M, V, norm
+
+    P, G, M, V, norm = run(z)
+    P1, M1, norm1 = P.clone(), M.clone(), norm.clone()
+    if exchange == "p2p":
+        # the collective path on the same inputs: identical bits
+        z.exchange = "nccl"
+        Pn, Gn, Mn, Vn, normn = run(z)
+        z.exchange = "p2p"
+        assert torch.equal(P, Pn) and torch.equal(M, Mn) and torch.equal(V, Vn), "p2p != nccl"
+        assert torch.equal(G[lo:lo + shard], Gn[lo:lo + shard]) and torch.equal(norm, normn)
+        # a second p2p step on the same registered buffers (epoch 2)
+        z.step(P, G, M, V, LR, B1, B2, WD, 3, 1.0, norm)
+        z.sync(60000)
+        assert torch.isfinite(P).all()
+        from tinylm_c_b200 import _lib
+        _lib.check(_lib.lib().tl_device_status())
+    P, M, norm = P1, M1, norm1
     gn = oracle.grad_norm(gavg)
     assert abs(norm.item() - gn) <= 1e-6 * gn, (norm.item(), gn)
     ref = [p.copy(), gavg.copy(), m.copy(), v.copy()]
@@ -57,7 +78,7 @@ def main():
     dist.barrier()
     dist.destroy_process_group()
     if rank == 0:
-        print("ZERO1_OK")
+        print("ZERO1_OK", exchange)
 
 
 if __name__ == "__main__":

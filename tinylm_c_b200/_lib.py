@@ -82,6 +82,11 @@ SIGNATURES = {
     "tl_zero1_step": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_size,
                                _c_float, _c_float, _c_float, _c_float, _c_int, _c_float,
                                _c_void_p]),
+    "tl_zero1_p2p_register": (_c_int, [_c_void_p, _c_void_p, _c_size]),
+    "tl_zero1_step_p2p": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_size,
+                                   _c_float, _c_float, _c_float, _c_float, _c_int, _c_float,
+                                   _c_void_p]),
+    "tl_zero1_p2p_release": (_c_int, []),
     "tl_dist_allreduce_f32": (_c_int, [_c_void_p, _c_size, _c_int]),
     "tl_dist_allreduce_f64": (_c_int, [_c_void_p, _c_size]),
     "tl_dist_sync": (_c_int, [_c_int]),

@@ -23,6 +23,7 @@ int launch_sumsq(DeviceCtx *c, const float *G, size_t n, double *sumsq_out, floa
 int launch_adamw(DeviceCtx *c, float *P, const float *G, float *M, float *V, size_t n, float lr,
                  float b1, float b2, float wd, int t, float gscale, const float *gscale_dev);
 __global__ void clip_scale_kernel(const double *sumsq, float max_norm, float *norm_out, float *gscale_out);
+void p2p_release_device(int device);
 
 struct DistCtx {
   ncclComm_t comm = nullptr;
@@ -71,6 +72,27 @@ static DistCtx *dist() {
   return g_dist[dev].ready ? &g_dist[dev] : nullptr;
 }
 
+// This device's rank and world size (false without a communicator).
+bool dist_rank_world(int *rank, int *world) {
+  DistCtx *d = dist();
+  if (!d) return false;
+  *rank = d->rank;
+  *world = d->world;
+  return true;
+}
+
+// All-gather `bytes` bytes per rank between device buffers on the library
+// stream, then wait for it with the host deadline.
+int dist_allgather_bytes(const void *send_dev, void *recv_dev, size_t bytes) {
+  TL_REQUIRE_CTX(c);
+  DistCtx *d = dist();
+  if (!d) return set_error(TL_ENOINIT, "tl_dist_init() not called for this device");
+  ncclResult_t r = ncclAllGather(send_dev, recv_dev, bytes, ncclInt8, d->comm, c->stream);
+  int rc = nccl_settle(*d, r, "ncclAllGather(bytes)");
+  if (rc) return rc;
+  return tl_dist_sync(0);
+}
+
 }  // namespace tl
 
 using namespace tl;
@@ -115,6 +137,7 @@ TL_API int tl_dist_init(int rank, int world, const void *uid128) {
 TL_API int tl_dist_finalize(void) {
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return TL_OK;
+  p2p_release_device(dev);
   DistCtx &d = g_dist[dev];
   if (d.comm) {
     ncclCommFinalize(d.comm);

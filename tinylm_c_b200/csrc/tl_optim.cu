@@ -6,35 +6,10 @@
 // Both are HBM-bound streams.  Algorithmic bytes: the norm reads G once
 // (4 B/elem); AdamW reads P,G,M,V and writes P,M,V (28 B/elem).
 #include <cmath>
-#include "tl_common.cuh"
+#include "tl_optim.cuh"
 #include "tl_trace.cuh"
 
 namespace tl {
-
-__device__ __forceinline__ float4 ld_stream(const float4 *p) {
-  float4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
-  return v;
-}
-
-__device__ __forceinline__ double warp_sum(double v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
-}
-
-// Block-wide sum in a fixed order (result valid in thread 0).
-__device__ __forceinline__ double block_sum(double v, double *smem) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  v = warp_sum(v);
-  if (lane == 0) smem[warp] = v;
-  __syncthreads();
-  const int nw = blockDim.x >> 5;
-  v = (threadIdx.x < nw) ? smem[threadIdx.x] : 0.0;
-  if (warp == 0) v = warp_sum(v);
-  return v;
-}
 
 // Two-stage deterministic sum of squares.  Stage 1: each of the gridDim.x
 // blocks reduces a fixed strided subset of G into partials[block].  Stage 2:
@@ -109,20 +84,6 @@ __global__ void clip_scale_kernel(const double *__restrict__ sumsq, float max_no
   if (gscale_out) *gscale_out = norm > max_norm ? max_norm / norm : 1.0f;
 }
 
-struct AdamArgs {
-  float lr, b1, b2, omb1, omb2, wd, bc1, bc2, gscale;
-  const float *gscale_ptr;
-};
-
-__device__ __forceinline__ void adam_elem(float &p, float g, float &m, float &v,
-                                          const AdamArgs &a, float gs) {
-  g = g * gs;
-  m = a.b1 * m + a.omb1 * g;
-  v = a.b2 * v + a.omb2 * g * g;
-  const float mh = m / a.bc1, vh = v / a.bc2;
-  p -= a.lr * (mh / (sqrtf(vh) + 1e-8f) + a.wd * p);
-}
-
 // Vector body: one float4 of each of P,G,M,V per thread per step, two steps
 // unrolled so eight 16-byte loads are in flight per thread.
 __global__ void __launch_bounds__(256)
@@ -177,14 +138,7 @@ int launch_sumsq(DeviceCtx *c, const float *G, size_t n, double *sumsq_out, floa
 int launch_adamw(DeviceCtx *c, float *P, const float *G, float *M, float *V, size_t n, float lr,
                  float b1, float b2, float wd, int t, float gscale, const float *gscale_dev) {
   if (n == 0) return TL_OK;
-  AdamArgs a;
-  a.lr = lr; a.b1 = b1; a.b2 = b2; a.wd = wd;
-  a.omb1 = 1.0f - b1; a.omb2 = 1.0f - b2;
-  // Bias corrections in fp32 with powf, as tinylm.c:1161.
-  a.bc1 = 1.0f - powf(b1, (float)t);
-  a.bc2 = 1.0f - powf(b2, (float)t);
-  a.gscale = gscale;
-  a.gscale_ptr = gscale_dev;
+  const AdamArgs a = make_adam_args(lr, b1, b2, wd, t, gscale, gscale_dev);
   const bool aligned = ((reinterpret_cast<uintptr_t>(P) | reinterpret_cast<uintptr_t>(G) |
                          reinterpret_cast<uintptr_t>(M) | reinterpret_cast<uintptr_t>(V)) & 15) == 0;
   size_t done = 0;

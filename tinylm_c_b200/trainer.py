@@ -55,7 +55,7 @@ def load_bundle(path, P=None):
 
 
 class Trainer:
-    def __init__(self, cfg, B, micro_batch=None, device=0, rank=0, world=1):
+    def __init__(self, cfg, B, micro_batch=None, device=0, rank=0, world=1, exchange="nccl"):
         self.cfg = cfg
         self.T = cfg[6] if cfg[6] > 0 else 256
         self.n_mtp = cfg[7]
@@ -72,7 +72,7 @@ class Trainer:
         self.n = self.model.nparams
         if world > 1:
             from .zero1 import Zero1
-            self.z = Zero1(self.n, rank, world, self.device)
+            self.z = Zero1(self.n, rank, world, self.device, exchange=exchange)
             self.n_pad, self.shard = self.z.n_pad, self.z.shard
         else:
             self.z = None
