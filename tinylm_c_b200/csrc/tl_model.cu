@@ -37,7 +37,7 @@ struct Model {
   float *rope_cos, *rope_sin;
   std::vector<float *> a_in, a_norm, rinv1, q, k, v, att, lse, f_in, f_norm, rinv2, g, u;
   float *x_final, *fn, *fn_rinv, *logits;
-  float *act, *dact, *dgb, *du, *dout, *dfnorm, *dfin, *datt, *dq, *dnorm, *dain, *dfn, *dk, *dv, *Drow;
+  float *act, *dact, *dgb, *du, *dout, *dfnorm, *dfin, *datt, *dq, *dnorm, *dain, *dfn, *dk, *dv, *Drow, *dsT;
   float *t1, *hk, *dhk, *dt1;
   float *rms_part;
   double *loss_rows, *loss_acc;
@@ -161,7 +161,7 @@ static int micro_step(DeviceCtx *c, Model &m, const float *P, float *G, const in
     TRY(gemm(c, GemmOp::NT, m.datt, m.dfin, P + m.o_wo[l], N, D, D));
     TRY(gemm(c, GemmOp::TN, G + m.o_wo[l], m.att[l], m.dfin, N, D, D));
     // attention
-    TRY(k_attn_bwd(c, m.q[l], m.k[l], m.v[l], m.att[l], m.datt, m.lse[l], m.Drow, m.dq, m.dk, m.dv, m.mb, m.T, m.H,
+    TRY(k_attn_bwd(c, m.q[l], m.k[l], m.v[l], m.att[l], m.datt, m.lse[l], m.Drow, m.dsT, m.dq, m.dk, m.dv, m.mb, m.T, m.H,
                    m.KV, m.hd));
     TRY(k_rope(c, m.dq, m.rope_cos, m.rope_sin, N, m.H, m.hd, m.T, 1));
     TRY(k_rope(c, m.dk, m.rope_cos, m.rope_sin, N, m.KV, m.hd, m.T, 1));
@@ -233,6 +233,7 @@ static int alloc_model(Model &m) {
   slots.push_back({&m.dk, take(N * KD)});
   slots.push_back({&m.dv, take(N * KD)});
   slots.push_back({&m.Drow, take(att_rows)});
+  slots.push_back({&m.dsT, take(att_rows * m.T)});
   slots.push_back({&m.rms_part, take((size_t)RMS_PART_ROWS * D)});
   const size_t o_loss = take(2 * N + 2);  // doubles: N rows + accumulator
   TL_TRY_CUDA(cudaMalloc(&m.arena, floats * sizeof(float)));

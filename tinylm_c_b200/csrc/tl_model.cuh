@@ -24,7 +24,10 @@ int k_loss_sum(DeviceCtx *c, const double *rows, int N, double *acc);
 int k_loss_final(DeviceCtx *c, const double *acc, double denom, float *out);
 int k_attn_fwd(DeviceCtx *c, const float *q, const float *k, const float *v, float *out, float *lse, int B, int T,
                int H, int KV, int hd);
+// dsT: scratch of B*H*T*T floats (dS^T of the causal tile pairs, written by the
+// key-side kernel and read by the query-side one).
 int k_attn_bwd(DeviceCtx *c, const float *q, const float *k, const float *v, const float *out, const float *dout,
-               const float *lse, float *Drow, float *dq, float *dk, float *dv, int B, int T, int H, int KV, int hd);
+               const float *lse, float *Drow, float *dsT, float *dq, float *dk, float *dv, int B, int T, int H,
+               int KV, int hd);
 
 }  // namespace tl

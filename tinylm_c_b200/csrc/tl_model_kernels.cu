@@ -420,77 +420,22 @@ __global__ void attn_rowdot_kernel(const float *__restrict__ dout, const float *
   if (lane == 0) Drow[warp] = acc;
 }
 
-// Backward, query side: CTA per (b, h, query tile).  For every key tile:
-// S and dP = dO V^T in one k loop, P = exp(scale S - lse), dS = P (dP - D)
-// scale, dQ += dS K.  Writes dq (overwrite).
-__global__ void __launch_bounds__(256)
-attn_bwd_dq_kernel(const float *__restrict__ q, const float *__restrict__ k, const float *__restrict__ v,
-                   const float *__restrict__ dout, const float *__restrict__ lse, const float *__restrict__ Drow,
-                   float *__restrict__ dq, int T, int H, int KV, int hd, float scale) {
-  extern __shared__ float sm[];
-  float *Qt = sm, *Ot = Qt + ATILE, *Kt = Ot + ATILE, *Vt = Kt + ATILE, *Kr = Vt + ATILE, *St = Kr + ATILE;
-  const int nqt = T / AT;
-  const int qt = blockIdx.x % nqt, bh = blockIdx.x / nqt, b = bh / H, h = bh % H, kvh = h / (H / KV);
-  const int D = H * hd, KD = KV * hd;
-  const int tid = threadIdx.x, ty = tid / 16, tx = tid % 16;
-  const size_t qrow0 = (size_t)b * T + qt * AT;
-  load_tile(Qt, q + qrow0 * D + (size_t)h * hd, D, hd, true);
-  load_tile(Ot, dout + qrow0 * D + (size_t)h * hd, D, hd, true);
-  float Lr[4], Dr[4];
-#pragma unroll
-  for (int i = 0; i < 4; i++) {
-    Lr[i] = lse[(size_t)bh * T + qt * AT + ty * 4 + i];
-    Dr[i] = Drow[(size_t)bh * T + qt * AT + ty * 4 + i];
-  }
-  float g[4][4];
-  zero44(g);
-  for (int kt = 0; kt <= qt; kt++) {
-    const size_t krow0 = (size_t)b * T + kt * AT;
-    __syncthreads();
-    load_tile(Kt, k + krow0 * KD + (size_t)kvh * hd, KD, hd, true);
-    load_tile(Vt, v + krow0 * KD + (size_t)kvh * hd, KD, hd, true);
-    load_tile(Kr, k + krow0 * KD + (size_t)kvh * hd, KD, hd, false);
-    __syncthreads();
-    float s[4][4], dp[4][4];
-    zero44(s);
-    zero44(dp);
-    mm64x2(s, dp, Qt, Kt, Ot, Vt, hd, ty, tx);
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-      const int qi = qt * AT + ty * 4 + i;
-#pragma unroll
-      for (int j = 0; j < 4; j++) {
-        const int kj = kt * AT + tx * 4 + j;
-        const float pr = (kj <= qi) ? expf(s[i][j] * scale - Lr[i]) : 0.0f;
-        St[(tx * 4 + j) * ALD + ty * 4 + i] = pr * (dp[i][j] - Dr[i]) * scale;
-      }
-    }
-    __syncthreads();
-    mm64(g, St, Kr, AT, ty, tx);
-  }
-#pragma unroll
-  for (int i = 0; i < 4; i++) {
-    float *row = dq + (qrow0 + ty * 4 + i) * D + (size_t)h * hd;
-#pragma unroll
-    for (int j = 0; j < 4; j++) {
-      const int d = tx * 4 + j;
-      if (d < hd) row[d] = g[i][j];
-    }
-  }
-}
-
 // Backward, key side: CTA per (b, kv head, key tile); loops over the group's
 // query heads and the query tiles at or after the key tile:
 //   S^T = K Q^T and dP^T = V dO^T in one k loop, P^T, dS^T as above,
-//   dV += P^T dO, dK += dS^T Q.  Writes dk, dv (overwrite).
-__global__ void __launch_bounds__(256)
+//   dV += P^T dO, dK += dS^T Q.  Writes dk, dv (overwrite) and dS^T of every
+//   causal tile pair to dsT[b][h][key][q] for the query-side product.
+// P^T and dS^T reuse the shared tiles of Q^T and dO^T (no longer read once
+// S^T and dP^T are in registers): six tiles, two CTAs per SM.
+__global__ void __launch_bounds__(256, 2)
 attn_bwd_dkdv_kernel(const float *__restrict__ q, const float *__restrict__ k, const float *__restrict__ v,
                      const float *__restrict__ dout, const float *__restrict__ lse, const float *__restrict__ Drow,
-                     float *__restrict__ dk, float *__restrict__ dv, int T, int H, int KV, int hd, float scale) {
+                     float *__restrict__ dk, float *__restrict__ dv, float *__restrict__ dsT, int T, int H, int KV,
+                     int hd, float scale) {
   extern __shared__ float sm[];
   float *Kt = sm, *Vt = Kt + ATILE, *Qt = Vt + ATILE, *Ot = Qt + ATILE, *Qr = Ot + ATILE, *Or = Qr + ATILE;
-  float *Ps = Or + ATILE, *Ss = Ps + ATILE;
-  float *Ls = Ss + ATILE, *Ds = Ls + AT;
+  float *Ps = Qt, *Ss = Ot;
+  float *Ls = Or + ATILE, *Ds = Ls + AT;
   const int nkt = T / AT;
   const int kt = blockIdx.x % nkt, bk = blockIdx.x / nkt, b = bk / KV, kvh = bk % KV, grp = H / KV;
   const int D = H * hd, KD = KV * hd;
@@ -527,9 +472,20 @@ attn_bwd_dkdv_kernel(const float *__restrict__ q, const float *__restrict__ k, c
           const int qi = qt * AT + tx * 4 + j;
           const int ql = tx * 4 + j;
           const float pr = (kj <= qi) ? expf(st[i][j] * scale - Ls[ql]) : 0.0f;
-          Ps[ql * ALD + ty * 4 + i] = pr;
-          Ss[ql * ALD + ty * 4 + i] = pr * (dpt[i][j] - Ds[ql]) * scale;
+          st[i][j] = pr;
+          dpt[i][j] = pr * (dpt[i][j] - Ds[ql]) * scale;
         }
+      }
+      __syncthreads();             // every thread is done reading Q^T and dO^T
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          Ps[(tx * 4 + j) * ALD + ty * 4 + i] = st[i][j];
+          Ss[(tx * 4 + j) * ALD + ty * 4 + i] = dpt[i][j];
+        }
+        float *row = dsT + ((size_t)bh * T + kt * AT + ty * 4 + i) * T + qt * AT + tx * 4;
+        *reinterpret_cast<float4 *>(row) = make_float4(dpt[i][0], dpt[i][1], dpt[i][2], dpt[i][3]);
       }
       __syncthreads();
       mm64(gv, Ps, Or, AT, ty, tx);
@@ -547,6 +503,41 @@ attn_bwd_dkdv_kernel(const float *__restrict__ q, const float *__restrict__ k, c
   }
 }
 
+// Backward, query side: CTA per (b, h, query tile); dQ = sum over key tiles
+// 0..qt of dS (read back as dS^T[key][q] from the key-side kernel) times K.
+// Key tiles and the k loop run in the same order as a recomputing kernel
+// would, so dQ is the same to the bit.
+__global__ void __launch_bounds__(256)
+attn_bwd_dq_kernel(const float *__restrict__ k, const float *__restrict__ dsT, float *__restrict__ dq, int T,
+                   int H, int KV, int hd) {
+  extern __shared__ float sm[];
+  float *St = sm, *Kr = St + ATILE;
+  const int nqt = T / AT;
+  const int qt = blockIdx.x % nqt, bh = blockIdx.x / nqt, b = bh / H, h = bh % H, kvh = h / (H / KV);
+  const int D = H * hd, KD = KV * hd;
+  const int tid = threadIdx.x, ty = tid / 16, tx = tid % 16;
+  const size_t qrow0 = (size_t)b * T + qt * AT;
+  float g[4][4];
+  zero44(g);
+  for (int kt = 0; kt <= qt; kt++) {
+    const size_t krow0 = (size_t)b * T + kt * AT;
+    __syncthreads();
+    load_tile(St, dsT + ((size_t)bh * T + kt * AT) * T + qt * AT, T, AT, false);
+    load_tile(Kr, k + krow0 * KD + (size_t)kvh * hd, KD, hd, false);
+    __syncthreads();
+    mm64(g, St, Kr, AT, ty, tx);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    float *row = dq + (qrow0 + ty * 4 + i) * D + (size_t)h * hd;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const int d = tx * 4 + j;
+      if (d < hd) row[d] = g[i][j];
+    }
+  }
+}
+
 }  // namespace mk
 
 // ------------------------------------------------------------ launchers
@@ -558,8 +549,8 @@ static inline unsigned grid_for(size_t n, int threads, int cap_waves_sm, int num
 }
 
 size_t attn_smem_fwd() { return sizeof(float) * 4 * mk::ATILE; }
-size_t attn_smem_dq() { return sizeof(float) * 6 * mk::ATILE; }
-size_t attn_smem_dkdv() { return sizeof(float) * (8 * mk::ATILE + 2 * mk::AT); }
+size_t attn_smem_dq() { return sizeof(float) * 2 * mk::ATILE; }
+size_t attn_smem_dkdv() { return sizeof(float) * (6 * mk::ATILE + 2 * mk::AT); }
 
 int mk_setup(int device) {
   static bool done[kMaxDevices] = {};
@@ -670,17 +661,17 @@ int k_attn_fwd(DeviceCtx *c, const float *q, const float *k, const float *v, flo
   return TL_OK;
 }
 int k_attn_bwd(DeviceCtx *c, const float *q, const float *k, const float *v, const float *out, const float *dout,
-               const float *lse, float *Drow, float *dq, float *dk, float *dv, int B, int T, int H, int KV, int hd) {
+               const float *lse, float *Drow, float *dsT, float *dq, float *dk, float *dv, int B, int T, int H,
+               int KV, int hd) {
   TraceScope ts(c, "k_attn_bwd");
   const float scale = 1.0f / sqrtf((float)hd);
   const int rows = B * H * T;
   mk::attn_rowdot_kernel<<<(rows + 7) / 8, 256, 0, c->stream>>>(dout, out, Drow, B, T, H, hd);
   MK_LAUNCH_CHECK();
-  mk::attn_bwd_dq_kernel<<<B * H * (T / mk::AT), 256, attn_smem_dq(), c->stream>>>(q, k, v, dout, lse, Drow, dq, T,
-                                                                                   H, KV, hd, scale);
+  mk::attn_bwd_dkdv_kernel<<<B * KV * (T / mk::AT), 256, attn_smem_dkdv(), c->stream>>>(
+      q, k, v, dout, lse, Drow, dk, dv, dsT, T, H, KV, hd, scale);
   MK_LAUNCH_CHECK();
-  mk::attn_bwd_dkdv_kernel<<<B * KV * (T / mk::AT), 256, attn_smem_dkdv(), c->stream>>>(q, k, v, dout, lse, Drow,
-                                                                                       dk, dv, T, H, KV, hd, scale);
+  mk::attn_bwd_dq_kernel<<<B * H * (T / mk::AT), 256, attn_smem_dq(), c->stream>>>(k, dsT, dq, T, H, KV, hd);
   MK_LAUNCH_CHECK();
   return TL_OK;
 }
