@@ -33,11 +33,18 @@ static int gemm_entry(GemmOp op, float *C, const float *A, const float *B, int M
 // Engine choice without argument checks, for callers inside the library that
 // have validated their buffers once (the device training step).
 int tl::gemm_run(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, int M, int K, int N) {
+  return gemm_run_add(c, op, C, A, B, M, K, N, op == GemmOp::NN ? nullptr : C);
+}
+
+int tl::gemm_run_add(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, int M, int K, int N,
+                     const float *add) {
   int I, J, R;
   gemm_dims(op, M, K, N, &I, &J, &R);
   if (I == 0 || J == 0) return TL_OK;
   if (R == 0) {
-    if (op == GemmOp::NN) TL_TRY_CUDA(cudaMemsetAsync(C, 0, sizeof(float) * (size_t)I * J, c->stream));
+    const size_t bytes = sizeof(float) * (size_t)I * J;
+    if (!add) TL_TRY_CUDA(cudaMemsetAsync(C, 0, bytes, c->stream));
+    else if (add != C) TL_TRY_CUDA(cudaMemcpyAsync(C, add, bytes, cudaMemcpyDeviceToDevice, c->stream));
     return TL_OK;
   }
   const bool tc_ok = gemm_tc_supported(op, C, A, B, M, K, N);
@@ -46,10 +53,10 @@ int tl::gemm_run(DeviceCtx *c, GemmOp op, float *C, const float *A, const float 
   if (tc_ok && g_engine_pref != 1) {
     const bool pair = g_engine_pref == 3 || (g_engine_pref == 0 && gemm_tc_prefer_pair(I, J, R));
     g_engine_last = pair ? 3 : 2;
-    return gemm_tc(c, op, C, A, B, M, K, N, pair);
+    return gemm_tc(c, op, C, A, B, M, K, N, pair, add);
   }
   g_engine_last = 1;
-  return gemm_simt(c, op, C, A, B, M, K, N);
+  return gemm_simt(c, op, C, A, B, M, K, N, add);
 }
 
 using namespace tl;

@@ -19,8 +19,16 @@ inline void gemm_dims(GemmOp op, int M, int K, int N, int *I, int *J, int *R) {
   }
 }
 
+// The reference semantics: mm overwrites C, mm_bt / mm_atb accumulate into C.
 int gemm_run(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, int M, int K, int N);
-int gemm_simt(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, int M, int K, int N);
+// C = op(A, B) + add, where add is nullptr (overwrite), C itself (accumulate)
+// or another I x J array with C's row stride (a residual).  Each element is
+// the fp32 sum of the rounded product and the addend, exactly what a GEMM
+// followed by an element-wise add produces.
+int gemm_run_add(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, int M, int K, int N,
+                 const float *add);
+int gemm_simt(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, int M, int K, int N,
+              const float *add);
 // Returns TL_EINVAL (without launching) when the shape or alignment is not
 // supported by the tensor-core engine.
 bool gemm_tc_supported(GemmOp op, const float *C, const float *A, const float *B, int M, int K, int N);
@@ -29,6 +37,7 @@ bool gemm_tc_supported(GemmOp op, const float *C, const float *A, const float *B
 bool gemm_tc_prefer_pair(int I, int J, int R);
 // pair: the CTA-pair kernel (256 x 256 tiles over two SMs) instead of the
 // one-CTA kernel (128 x 128 tiles).
-int gemm_tc(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, int M, int K, int N, bool pair);
+int gemm_tc(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, int M, int K, int N, bool pair,
+            const float *add);
 
 }  // namespace tl

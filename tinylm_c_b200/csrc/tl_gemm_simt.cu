@@ -7,9 +7,10 @@
 //
 // One generic form covers all three primitives:
 //   C[i,j] (=|+=) sum_r A(i,r) * B(r,j)
-//   mm     (tinylm.c:439):  I=M J=N R=K, A=X  (r contiguous),  B=W  (j contiguous), beta 0
-//   mm_bt  (tinylm.c:480):  I=M J=K R=N, A=dY (r contiguous),  B=W^T(r contiguous), beta 1
-//   mm_atb (tinylm.c:510):  I=K J=N R=M, A=X^T(i contiguous),  B=dY (j contiguous), beta 1
+//   mm     (tinylm.c:439):  I=M J=N R=K, A=X  (r contiguous),  B=W  (j contiguous)
+//   mm_bt  (tinylm.c:480):  I=M J=K R=N, A=dY (r contiguous),  B=W^T(r contiguous)
+//   mm_atb (tinylm.c:510):  I=K J=N R=M, A=X^T(i contiguous),  B=dY (j contiguous)
+// and C = product + add (add: nullptr, C itself, or a residual).
 #include "tl_common.cuh"
 #include "tl_gemm.cuh"
 #include "tl_trace.cuh"
@@ -23,7 +24,7 @@ constexpr int SB_M = 128, SB_N = 128, SB_K = 16, S_THREADS = 256;
 template <bool A_RC, bool B_RC>
 __global__ void __launch_bounds__(S_THREADS)
 gemm_simt_kernel(float *__restrict__ C, const float *__restrict__ A, const float *__restrict__ B,
-                 int I, int J, int R, int lda, int ldb, int ldc, int beta) {
+                 int I, int J, int R, int lda, int ldb, int ldc, const float *__restrict__ add) {
   __shared__ float As[SB_K][SB_M + 4];
   __shared__ float Bs[SB_K][SB_N + 4];
   const int tid = threadIdx.x;
@@ -76,13 +77,14 @@ gemm_simt_kernel(float *__restrict__ C, const float *__restrict__ A, const float
     for (int y = 0; y < 8; y++) {
       const int gj = j0 + tj + y;
       if (gj >= J) continue;
-      float *dst = C + (size_t)gi * ldc + gj;
-      *dst = beta ? *dst + acc[x][y] : acc[x][y];
+      const size_t o = (size_t)gi * ldc + gj;
+      C[o] = add ? add[o] + acc[x][y] : acc[x][y];
     }
   }
 }
 
-int gemm_simt(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, int M, int K, int N) {
+int gemm_simt(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, int M, int K, int N,
+              const float *add) {
   int I, J, R;
   gemm_dims(op, M, K, N, &I, &J, &R);
   if (I == 0 || J == 0) return TL_OK;
@@ -91,13 +93,13 @@ int gemm_simt(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B,
   TraceScope ts(c, "gemm_simt");
   switch (op) {
     case GemmOp::NN:  // mm: A=X[M,K] lda=K, B=W[K,N] ldb=N (j contiguous), C ldc=N
-      gemm_simt_kernel<true, false><<<grid, S_THREADS, 0, c->stream>>>(C, A, B, I, J, R, K, N, N, 0);
+      gemm_simt_kernel<true, false><<<grid, S_THREADS, 0, c->stream>>>(C, A, B, I, J, R, K, N, N, add);
       break;
     case GemmOp::NT:  // mm_bt: A=dY[M,N] lda=N, B(r=n,j=k)=W[k*N+n] ldb=N, C ldc=K
-      gemm_simt_kernel<true, true><<<grid, S_THREADS, 0, c->stream>>>(C, A, B, I, J, R, N, N, K, 1);
+      gemm_simt_kernel<true, true><<<grid, S_THREADS, 0, c->stream>>>(C, A, B, I, J, R, N, N, K, add);
       break;
     case GemmOp::TN:  // mm_atb: A(i=k,r=m)=X[m*K+k] lda=K, B=dY[M,N] ldb=N, C ldc=N
-      gemm_simt_kernel<false, false><<<grid, S_THREADS, 0, c->stream>>>(C, A, B, I, J, R, K, N, N, 1);
+      gemm_simt_kernel<false, false><<<grid, S_THREADS, 0, c->stream>>>(C, A, B, I, J, R, K, N, N, add);
       break;
   }
   TL_TRY_CUDA(cudaGetLastError());

@@ -22,7 +22,8 @@
 //               buffer (the raw tile is read as hi)
 //   warps 6..9  accumulator warpgroup: every CHUNK_KB k-blocks the TMEM
 //               accumulator (double buffered) is added into fp32 registers;
-//               finally the epilogue (registers -> global, beta = 0 or 1)
+//               finally the epilogue (registers -> global, plus an optional
+//               addend: C itself to accumulate, or a residual)
 // Pipeline per stage: full (TMA bytes landed) -> ready (lo written) ->
 // empty (MMAs that read the stage finished, via tcgen05.commit); per TMEM
 // buffer: accf (chunk finished) -> acce (chunk drained).
@@ -153,7 +154,8 @@ __device__ __forceinline__ float tf32_trunc(float x) { return __uint_as_float(__
 
 struct Params {
   float *C;
-  int I, J, R, ldc, beta;
+  int I, J, R, ldc;
+  const float *add;      // nullptr, C (accumulate) or a residual, row stride ldc
   int kb_per_split;      // k-blocks per CTA along grid z (split-K)
   size_t split_stride;   // floats between the partial outputs of consecutive splits
   int *err;
@@ -362,21 +364,21 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       const int row = i0 + q * 32 + lane;
       if (row < p.I) {
         float *dst = Cout + (size_t)row * p.ldc + j0;
+        const float *addp = p.add ? p.add + (size_t)row * p.ldc + j0 : nullptr;
         if (j0 + BN <= p.J) {
 #pragma unroll
           for (int e = 0; e < BN; e += 4) {
             float4 o = make_float4(acc[e], acc[e + 1], acc[e + 2], acc[e + 3]);
-            float4 *d4 = reinterpret_cast<float4 *>(dst + e);
-            if (p.beta) {
-              const float4 old = *d4;
-              o.x += old.x; o.y += old.y; o.z += old.z; o.w += old.w;
+            if (addp) {
+              const float4 old = *reinterpret_cast<const float4 *>(addp + e);
+              o.x = old.x + o.x; o.y = old.y + o.y; o.z = old.z + o.z; o.w = old.w + o.w;
             }
-            *d4 = o;
+            *reinterpret_cast<float4 *>(dst + e) = o;
           }
         } else {
 #pragma unroll
           for (int e = 0; e < BN; e++) {
-            if (j0 + e < p.J) dst[e] = p.beta ? dst[e] + acc[e] : acc[e];
+            if (j0 + e < p.J) dst[e] = addp ? addp[e] + acc[e] : acc[e];
           }
         }
       }
@@ -740,21 +742,21 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
       const int jc = j0 + h * BN;
       if (row < p.I) {
         float *dst = Cout + (size_t)row * p.ldc + jc;
+        const float *addp = p.add ? p.add + (size_t)row * p.ldc + jc : nullptr;
         if (jc + BN <= p.J) {
 #pragma unroll
           for (int e = 0; e < BN; e += 4) {
             float4 o = make_float4(acc[e], acc[e + 1], acc[e + 2], acc[e + 3]);
-            float4 *d4 = reinterpret_cast<float4 *>(dst + e);
-            if (p.beta) {
-              const float4 old = *d4;
-              o.x += old.x; o.y += old.y; o.z += old.z; o.w += old.w;
+            if (addp) {
+              const float4 old = *reinterpret_cast<const float4 *>(addp + e);
+              o.x = old.x + o.x; o.y = old.y + o.y; o.z = old.z + o.z; o.w = old.w + o.w;
             }
-            *d4 = o;
+            *reinterpret_cast<float4 *>(dst + e) = o;
           }
         } else {
 #pragma unroll
           for (int e = 0; e < BN; e++) {
-            if (jc + e < p.J) dst[e] = p.beta ? dst[e] + acc[e] : acc[e];
+            if (jc + e < p.J) dst[e] = addp ? addp[e] + acc[e] : acc[e];
           }
         }
       }
@@ -803,8 +805,9 @@ static int make_map(CUtensorMap *m, const float *ptr, uint64_t inner, uint64_t o
   return TL_OK;
 }
 
-// C[i, j] = beta*C[i, j] + sum_z ws[z][i][j], partials summed in z order.
-__global__ void splitk_reduce_kernel(float *__restrict__ C, int ldc, int beta, const float *__restrict__ ws,
+// C[i, j] = add[i, j] + sum_z ws[z][i][j], partials summed in z order (add may
+// be nullptr or C itself).
+__global__ void splitk_reduce_kernel(float *C, int ldc, const float *add, const float *__restrict__ ws,
                                      int splits, int I, int J) {
   const size_t total4 = (size_t)I * J / 4;
   const size_t stride = (size_t)I * J;
@@ -816,12 +819,11 @@ __global__ void splitk_reduce_kernel(float *__restrict__ C, int ldc, int beta, c
       const float4 w = reinterpret_cast<const float4 *>(ws + z * stride)[q];
       acc.x += w.x; acc.y += w.y; acc.z += w.z; acc.w += w.w;
     }
-    float4 *dst = reinterpret_cast<float4 *>(C + (size_t)i * ldc + j);
-    if (beta) {
-      const float4 o = *dst;
-      acc.x += o.x; acc.y += o.y; acc.z += o.z; acc.w += o.w;
+    if (add) {
+      const float4 o = *reinterpret_cast<const float4 *>(add + (size_t)i * ldc + j);
+      acc.x = o.x + acc.x; acc.y = o.y + acc.y; acc.z = o.z + acc.z; acc.w = o.w + acc.w;
     }
-    *dst = acc;
+    *reinterpret_cast<float4 *>(C + (size_t)i * ldc + j) = acc;
   }
 }
 
@@ -878,7 +880,8 @@ bool gemm_tc_prefer_pair(int I, int J, int R) {
   return I > tc::BM && J > tc::BN;
 }
 
-int gemm_tc(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, int M, int K, int N, bool pair) {
+int gemm_tc(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, int M, int K, int N, bool pair,
+            const float *add) {
   int rc;
   if ((rc = tc::get_encoder())) return rc;
   int I, J, R;
@@ -909,29 +912,29 @@ int gemm_tc(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, i
     splits = (nk + kb_per - 1) / kb_per;
   }
   p.kb_per_split = kb_per;
-  int out_ldc = 0, out_beta = 0;
+  int out_ldc = 0;
   CUtensorMap ma, mb;
   switch (op) {
     case GemmOp::NN:  // A = X[M,K] K-major; B = W[K,N] MN-major
-      out_ldc = N; out_beta = 0;
+      out_ldc = N;
       if ((rc = tc::make_map(&ma, A, K, M, K, 32, tc::BM, false))) return rc;
       if ((rc = tc::make_map(&mb, B, N, K, N, 32, 32, true))) return rc;
       break;
     case GemmOp::NT:  // A = dY[M,N] K-major; B(r=n, j=k) = W[k*N+n] K-major
-      out_ldc = K; out_beta = 1;
+      out_ldc = K;
       if ((rc = tc::make_map(&ma, A, N, M, N, 32, tc::BM, false))) return rc;
       if ((rc = tc::make_map(&mb, B, N, K, N, 32, tc::BN, false))) return rc;
       break;
     case GemmOp::TN:  // A(i=k, r=m) = X[m*K+k] MN-major; B = dY[M,N] MN-major
-      out_ldc = N; out_beta = 1;
+      out_ldc = N;
       if ((rc = tc::make_map(&ma, A, K, M, K, 32, 32, true))) return rc;
       if ((rc = tc::make_map(&mb, B, N, M, N, 32, 32, true))) return rc;
       break;
   }
   if (splits > 1) {
-    p.C = c->gemm_ws; p.ldc = J; p.beta = 0; p.split_stride = (size_t)I * J;
+    p.C = c->gemm_ws; p.ldc = J; p.add = nullptr; p.split_stride = (size_t)I * J;
   } else {
-    p.ldc = out_ldc; p.beta = out_beta; p.split_stride = 0;
+    p.ldc = out_ldc; p.add = add; p.split_stride = 0;
   }
   switch (op) {
     case GemmOp::NN:
@@ -948,7 +951,7 @@ int gemm_tc(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, i
   TraceScope ts(c, "gemm_splitk_reduce");
   const size_t q = (size_t)I * J / 4;
   unsigned blocks = (unsigned)std::min<size_t>((q + 255) / 256, (size_t)c->num_sms * 8);
-  tc::splitk_reduce_kernel<<<blocks, 256, 0, c->stream>>>(C, out_ldc, out_beta, c->gemm_ws, splits, I, J);
+  tc::splitk_reduce_kernel<<<blocks, 256, 0, c->stream>>>(C, out_ldc, add, c->gemm_ws, splits, I, J);
   TL_TRY_CUDA(cudaGetLastError());
   return TL_OK;
 }

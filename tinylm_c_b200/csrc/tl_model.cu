@@ -35,9 +35,9 @@ struct Model {
   int device;
   void *arena = nullptr;
   float *rope_cos, *rope_sin;
-  std::vector<float *> a_in, a_norm, rinv1, q, k, v, att, lse, f_in, f_norm, rinv2, g, u;
+  std::vector<float *> a_in, a_norm, rinv1, q, k, v, att, lse, f_in, f_norm, rinv2, g, u, act;
   float *x_final, *fn, *fn_rinv, *logits;
-  float *act, *dact, *dgb, *du, *dout, *dfnorm, *dfin, *datt, *dq, *dnorm, *dain, *dfn, *dk, *dv, *Drow, *dsT;
+  float *dact, *dgb, *du, *dout, *dfnorm, *dfin, *datt, *dq, *dnorm, *dain, *dfn, *dk, *dv, *Drow, *dsT;
   float *t1, *hk, *dhk, *dt1;
   float *rms_part;
   double *loss_rows, *loss_acc;
@@ -82,6 +82,12 @@ struct Rng {
 static int gemm(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, int M, int K, int N) {
   return gemm_run(c, op, C, A, B, M, K, N);
 }
+// C = op(A, B) + add (add: nullptr to overwrite, or a residual); replaces the
+// reference's memset-then-accumulate and GEMM-then-add pairs with one pass.
+static int gemm_add(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, int M, int K, int N,
+                    const float *add) {
+  return gemm_run_add(c, op, C, A, B, M, K, N, add);
+}
 
 // One micro-batch: forward + backward, gradients accumulated into G.
 static int micro_step(DeviceCtx *c, Model &m, const float *P, float *G, const int *tok, const int *tgt,
@@ -100,20 +106,17 @@ static int micro_step(DeviceCtx *c, Model &m, const float *P, float *G, const in
     TRY(k_rope(c, m.q[l], m.rope_cos, m.rope_sin, N, m.H, m.hd, m.T, 0));
     TRY(k_rope(c, m.k[l], m.rope_cos, m.rope_sin, N, m.KV, m.hd, m.T, 0));
     TRY(k_attn_fwd(c, m.q[l], m.k[l], m.v[l], m.att[l], m.lse[l], m.mb, m.T, m.H, m.KV, m.hd));
-    TRY(gemm(c, GemmOp::NN, m.f_in[l], m.att[l], P + m.o_wo[l], N, D, D));
-    TRY(k_add(c, m.f_in[l], xin, ND));
+    TRY(gemm_add(c, GemmOp::NN, m.f_in[l], m.att[l], P + m.o_wo[l], N, D, D, xin));   // + residual
     TRY(k_rmsnorm_fwd(c, m.f_in[l], P + m.o_an2[l], m.f_norm[l], m.rinv2[l], N, D));
     float *out = (l + 1 < m.L) ? m.a_in[l + 1] : m.x_final;
     TRY(gemm(c, GemmOp::NN, m.g[l], m.f_norm[l], P + m.o_w1[l], N, D, F));
     TRY(gemm(c, GemmOp::NN, m.u[l], m.f_norm[l], P + m.o_w3[l], N, D, F));
-    TRY(k_swiglu_fwd(c, m.g[l], m.u[l], m.act, NF));
-    TRY(gemm(c, GemmOp::NN, out, m.act, P + m.o_w2[l], N, F, D));
-    TRY(k_add(c, out, m.f_in[l], ND));
+    TRY(k_swiglu_fwd(c, m.g[l], m.u[l], m.act[l], NF));
+    TRY(gemm_add(c, GemmOp::NN, out, m.act[l], P + m.o_w2[l], N, F, D, m.f_in[l]));   // + residual
   }
   TRY(k_rmsnorm_fwd(c, m.x_final, P + m.o_nf, m.fn, m.fn_rinv, N, D));
-  // tied head: logits = fn @ emb^T  (memset + mm_bt, 1015-1016)
-  TL_TRY_CUDA(cudaMemsetAsync(m.logits, 0, sizeof(float) * (size_t)N * V, c->stream));
-  TRY(gemm(c, GemmOp::NT, m.logits, m.fn, emb, N, V, D));
+  // tied head: logits = fn @ emb^T  (memset + mm_bt, 1015-1016, as one overwrite)
+  TRY(gemm_add(c, GemmOp::NT, m.logits, m.fn, emb, N, V, D, nullptr));
   // softmax + CE, logits gradient written in place (1019-1028, 1076-1082)
   TRY(k_softmax_ce(c, m.logits, tgt, N, V, scale, m.loss_rows));
   TRY(k_loss_sum(c, m.loss_rows, N, m.loss_acc));
@@ -129,8 +132,7 @@ static int micro_step(DeviceCtx *c, Model &m, const float *P, float *G, const in
     const float *Wk = P + m.o_mtp[kh];
     TRY(gemm(c, GemmOp::NN, m.t1, m.fn, Wk, N, D, D));
     TRY(k_mtp_hk(c, m.fn, m.t1, m.hk, ND));
-    TL_TRY_CUDA(cudaMemsetAsync(m.logits, 0, sizeof(float) * (size_t)N * V, c->stream));
-    TRY(gemm(c, GemmOp::NT, m.logits, m.hk, emb, N, V, D));
+    TRY(gemm_add(c, GemmOp::NT, m.logits, m.hk, emb, N, V, D, nullptr));
     TRY(k_softmax_ce(c, m.logits, tgt_mtp[kh], N, V, wk * scale, nullptr));
     TRY(gemm(c, GemmOp::TN, gemb, m.logits, m.hk, N, V, D));       // dEmb += dl^T @ hk
     TRY(gemm(c, GemmOp::NN, m.dhk, m.logits, emb, N, V, D));       // dhk = dl @ emb
@@ -138,44 +140,37 @@ static int micro_step(DeviceCtx *c, Model &m, const float *P, float *G, const in
     TRY(gemm(c, GemmOp::TN, G + m.o_mtp[kh], m.fn, m.dt1, N, D, D));
     TRY(gemm(c, GemmOp::NT, m.dfn, m.dt1, Wk, N, D, D));
   }
-  TL_TRY_CUDA(cudaMemsetAsync(m.dout, 0, sizeof(float) * ND, c->stream));
-  TRY(k_rmsnorm_bwd(c, m.x_final, P + m.o_nf, m.fn_rinv, m.dfn, m.dout, G + m.o_nf, m.rms_part, RMS_PART_ROWS, N, D));
+  TRY(k_rmsnorm_bwd(c, m.x_final, P + m.o_nf, m.fn_rinv, m.dfn, nullptr, m.dout, G + m.o_nf, m.rms_part,
+                    RMS_PART_ROWS, N, D));
   for (int l = m.L - 1; l >= 0; l--) {
     // FFN
-    TRY(k_swiglu_fwd(c, m.g[l], m.u[l], m.act, NF));
-    TRY(gemm(c, GemmOp::TN, G + m.o_w2[l], m.act, m.dout, N, F, D));
-    TL_TRY_CUDA(cudaMemsetAsync(m.dact, 0, sizeof(float) * NF, c->stream));
-    TRY(gemm(c, GemmOp::NT, m.dact, m.dout, P + m.o_w2[l], N, F, D));
+    TRY(gemm(c, GemmOp::TN, G + m.o_w2[l], m.act[l], m.dout, N, F, D));
+    TRY(gemm_add(c, GemmOp::NT, m.dact, m.dout, P + m.o_w2[l], N, F, D, nullptr));
     TRY(k_swiglu_bwd(c, m.g[l], m.u[l], m.dact, m.dgb, m.du, NF));
-    TL_TRY_CUDA(cudaMemsetAsync(m.dfnorm, 0, sizeof(float) * ND, c->stream));
-    TRY(gemm(c, GemmOp::NT, m.dfnorm, m.dgb, P + m.o_w1[l], N, D, F));
+    TRY(gemm_add(c, GemmOp::NT, m.dfnorm, m.dgb, P + m.o_w1[l], N, D, F, nullptr));
     TRY(gemm(c, GemmOp::NT, m.dfnorm, m.du, P + m.o_w3[l], N, D, F));
     TRY(gemm(c, GemmOp::TN, G + m.o_w1[l], m.f_norm[l], m.dgb, N, D, F));
     TRY(gemm(c, GemmOp::TN, G + m.o_w3[l], m.f_norm[l], m.du, N, D, F));
     // dfin = dout + rmsnorm2 backward
-    TL_TRY_CUDA(cudaMemcpyAsync(m.dfin, m.dout, sizeof(float) * ND, cudaMemcpyDeviceToDevice, c->stream));
-    TRY(k_rmsnorm_bwd(c, m.f_in[l], P + m.o_an2[l], m.rinv2[l], m.dfnorm, m.dfin, G + m.o_an2[l], m.rms_part,
-                      RMS_PART_ROWS, N, D));
+    TRY(k_rmsnorm_bwd(c, m.f_in[l], P + m.o_an2[l], m.rinv2[l], m.dfnorm, m.dout, m.dfin, G + m.o_an2[l],
+                      m.rms_part, RMS_PART_ROWS, N, D));
     // attention output projection
-    TL_TRY_CUDA(cudaMemsetAsync(m.datt, 0, sizeof(float) * ND, c->stream));
-    TRY(gemm(c, GemmOp::NT, m.datt, m.dfin, P + m.o_wo[l], N, D, D));
+    TRY(gemm_add(c, GemmOp::NT, m.datt, m.dfin, P + m.o_wo[l], N, D, D, nullptr));
     TRY(gemm(c, GemmOp::TN, G + m.o_wo[l], m.att[l], m.dfin, N, D, D));
     // attention
     TRY(k_attn_bwd(c, m.q[l], m.k[l], m.v[l], m.att[l], m.datt, m.lse[l], m.Drow, m.dsT, m.dq, m.dk, m.dv, m.mb, m.T, m.H,
                    m.KV, m.hd));
     TRY(k_rope(c, m.dq, m.rope_cos, m.rope_sin, N, m.H, m.hd, m.T, 1));
     TRY(k_rope(c, m.dk, m.rope_cos, m.rope_sin, N, m.KV, m.hd, m.T, 1));
-    TL_TRY_CUDA(cudaMemsetAsync(m.dnorm, 0, sizeof(float) * ND, c->stream));
-    TRY(gemm(c, GemmOp::NT, m.dnorm, m.dq, P + m.o_wq[l], N, D, D));
+    TRY(gemm_add(c, GemmOp::NT, m.dnorm, m.dq, P + m.o_wq[l], N, D, D, nullptr));
     TRY(gemm(c, GemmOp::NT, m.dnorm, m.dk, P + m.o_wk[l], N, D, KD));
     TRY(gemm(c, GemmOp::NT, m.dnorm, m.dv, P + m.o_wv[l], N, D, KD));
     TRY(gemm(c, GemmOp::TN, G + m.o_wq[l], m.a_norm[l], m.dq, N, D, D));
     TRY(gemm(c, GemmOp::TN, G + m.o_wk[l], m.a_norm[l], m.dk, N, D, KD));
     TRY(gemm(c, GemmOp::TN, G + m.o_wv[l], m.a_norm[l], m.dv, N, D, KD));
     // dain = dfin + rmsnorm1 backward; becomes the next layer's dout
-    TL_TRY_CUDA(cudaMemcpyAsync(m.dain, m.dfin, sizeof(float) * ND, cudaMemcpyDeviceToDevice, c->stream));
-    TRY(k_rmsnorm_bwd(c, m.a_in[l], P + m.o_an1[l], m.rinv1[l], m.dnorm, m.dain, G + m.o_an1[l], m.rms_part,
-                      RMS_PART_ROWS, N, D));
+    TRY(k_rmsnorm_bwd(c, m.a_in[l], P + m.o_an1[l], m.rinv1[l], m.dnorm, m.dfin, m.dain, G + m.o_an1[l],
+                      m.rms_part, RMS_PART_ROWS, N, D));
     std::swap(m.dout, m.dain);
   }
   TRY(k_embed_bwd(c, gemb, tok, m.dout, N, D, V));
@@ -206,7 +201,7 @@ static int alloc_model(Model &m) {
   std::vector<std::pair<float **, size_t>> slots;
   m.a_in.resize(L); m.a_norm.resize(L); m.rinv1.resize(L); m.q.resize(L); m.k.resize(L); m.v.resize(L);
   m.att.resize(L); m.lse.resize(L); m.f_in.resize(L); m.f_norm.resize(L); m.rinv2.resize(L); m.g.resize(L);
-  m.u.resize(L);
+  m.u.resize(L); m.act.resize(L);
   slots.push_back({&m.rope_cos, take((size_t)m.T * m.half)});
   slots.push_back({&m.rope_sin, take((size_t)m.T * m.half)});
   for (size_t l = 0; l < L; l++) {
@@ -223,13 +218,14 @@ static int alloc_model(Model &m) {
     slots.push_back({&m.rinv2[l], take(N)});
     slots.push_back({&m.g[l], take(N * F)});
     slots.push_back({&m.u[l], take(N * F)});
+    slots.push_back({&m.act[l], take(N * F)});   // kept for the backward (no recompute)
   }
   for (float **p : {&m.x_final, &m.fn, &m.dout, &m.dfnorm, &m.dfin, &m.datt, &m.dq, &m.dnorm, &m.dain, &m.dfn,
                     &m.t1, &m.hk, &m.dhk, &m.dt1})
     slots.push_back({p, take(N * D)});
   slots.push_back({&m.fn_rinv, take(N)});
   slots.push_back({&m.logits, take(N * V)});
-  for (float **p : {&m.act, &m.dact, &m.dgb, &m.du}) slots.push_back({p, take(N * F)});
+  for (float **p : {&m.dact, &m.dgb, &m.du}) slots.push_back({p, take(N * F)});
   slots.push_back({&m.dk, take(N * KD)});
   slots.push_back({&m.dv, take(N * KD)});
   slots.push_back({&m.Drow, take(att_rows)});

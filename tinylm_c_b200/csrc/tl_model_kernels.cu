@@ -78,9 +78,11 @@ __global__ void rmsnorm_fwd_kernel(const float *__restrict__ x, const float *__r
 // dx += s*g*dy - (s^3/D * sum(x*g*dy)) * x ; per-block partial of dg = sum_rows x*s*dy.
 // (tinylm.c:568-588; the per-thread buffers + critical section become a fixed-
 // order two-stage reduction.)  Block b handles rows b*8+w, stepping gridDim*8.
+// dx = dres + (RMSNorm backward of dy); dres may be dx itself (accumulate) or
+// nullptr (dx overwritten).
 __global__ void rmsnorm_bwd_kernel(const float *__restrict__ x, const float *__restrict__ g,
                                    const float *__restrict__ rinv, const float *__restrict__ dy,
-                                   float *__restrict__ dx, float *__restrict__ dg_part, int rows, int D) {
+                                   const float *dres, float *dx, float *__restrict__ dg_part, int rows, int D) {
   extern __shared__ float sm[];  // [8][D]
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int i = threadIdx.x; i < 8 * D; i += blockDim.x) sm[i] = 0.0f;
@@ -89,13 +91,15 @@ __global__ void rmsnorm_bwd_kernel(const float *__restrict__ x, const float *__r
   for (int r = blockIdx.x * 8 + w; r < rows; r += gridDim.x * 8) {
     const float *xr = x + (size_t)r * D, *dyr = dy + (size_t)r * D;
     float *dxr = dx + (size_t)r * D;
+    const float *drr = dres ? dres + (size_t)r * D : nullptr;
     const float s = rinv[r];
     float c = 0.0f;
     for (int i = lane; i < D; i += 32) c += xr[i] * g[i] * dyr[i];
     c = warp_sum_f(c);
     const float coef = s * s * s / D * c;
     for (int i = lane; i < D; i += 32) {
-      dxr[i] += s * g[i] * dyr[i] - coef * xr[i];
+      const float t = s * g[i] * dyr[i] - coef * xr[i];
+      dxr[i] = drr ? drr[i] + t : t;
       my[i] += (xr[i] * s) * dyr[i];
     }
   }
@@ -108,13 +112,25 @@ __global__ void rmsnorm_bwd_kernel(const float *__restrict__ x, const float *__r
   }
 }
 
-// dg[i] += sum over blocks of dg_part[b][i], in block order.
-__global__ void colsum_add_kernel(const float *__restrict__ part, int nparts, int D, float *__restrict__ dg) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= D) return;
+// dg[i] += sum over blocks of dg_part[b][i].  Block per 32 columns, lane =
+// column (coalesced rows); warp w sums parts w, w+8, ... and the eight warp
+// sums are added in warp order: a fixed order, so the result is deterministic.
+__global__ void __launch_bounds__(256)
+colsum_add_kernel(const float *__restrict__ part, int nparts, int D, float *__restrict__ dg) {
+  __shared__ float ws[8][32];
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int i = blockIdx.x * 32 + lane;
   float acc = 0.0f;
-  for (int b = 0; b < nparts; b++) acc += part[(size_t)b * D + i];
-  dg[i] += acc;
+  if (i < D)
+    for (int b = w; b < nparts; b += 8) acc += part[(size_t)b * D + i];
+  ws[w][lane] = acc;
+  __syncthreads();
+  if (w == 0 && i < D) {
+    float t = ws[0][lane];
+#pragma unroll
+    for (int k = 1; k < 8; k++) t += ws[k][lane];
+    dg[i] += t;
+  }
 }
 
 // ------------------------------------------------------------------- RoPE
@@ -138,28 +154,60 @@ __global__ void rope_kernel(float *__restrict__ buf, const float *__restrict__ c
 }
 
 // --------------------------------------------------------------- elementwise
+// The element-wise kernels below run a float4 body over the first n & ~3
+// elements (all buffers are 256-byte aligned arena slices) and a scalar tail.
 __global__ void add_inplace_kernel(float *__restrict__ y, const float *__restrict__ x, size_t n) {
-  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
-    y[i] += x[i];
+  const size_t n4 = n / 4, stride = (size_t)gridDim.x * blockDim.x;
+  float4 *y4 = reinterpret_cast<float4 *>(y);
+  const float4 *x4 = reinterpret_cast<const float4 *>(x);
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
+    float4 a = y4[i];
+    const float4 b = __ldcs(x4 + i);
+    a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
+    y4[i] = a;
+  }
+  for (size_t i = n4 * 4 + (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) y[i] += x[i];
 }
 // act = silu(g) * u   (tinylm.c:1005-1006)
 __global__ void swiglu_fwd_kernel(const float *__restrict__ g, const float *__restrict__ u,
                                   float *__restrict__ act, size_t n) {
-  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+  const size_t n4 = n / 4, stride = (size_t)gridDim.x * blockDim.x;
+  const float4 *g4 = reinterpret_cast<const float4 *>(g), *u4 = reinterpret_cast<const float4 *>(u);
+  float4 *a4 = reinterpret_cast<float4 *>(act);
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
+    const float4 z = __ldcs(g4 + i), v = __ldcs(u4 + i);
+    a4[i] = make_float4(siluf(z.x) * v.x, siluf(z.y) * v.y, siluf(z.z) * v.z, siluf(z.w) * v.w);
+  }
+  for (size_t i = n4 * 4 + (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
     act[i] = siluf(g[i]) * u[i];
 }
 // dg = dact*u*dsilu(g), du = dact*silu(g)   (tinylm.c:1106-1112)
+__device__ __forceinline__ void swiglu_bwd_elem(float z, float uu, float da, float &dg, float &du) {
+  const float sig = 1.0f / (1.0f + expf(-z));
+  const float silu = z * sig;
+  const float dsilu = sig + z * sig * (1.0f - sig);
+  dg = da * uu * dsilu;
+  du = da * silu;
+}
 __global__ void swiglu_bwd_kernel(const float *__restrict__ g, const float *__restrict__ u,
                                   const float *__restrict__ dact, float *__restrict__ dg,
                                   float *__restrict__ du, size_t n) {
-  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
-    const float z = g[i];
-    const float sig = 1.0f / (1.0f + expf(-z));
-    const float silu = z * sig;
-    const float dsilu = sig + z * sig * (1.0f - sig);
-    dg[i] = dact[i] * u[i] * dsilu;
-    du[i] = dact[i] * silu;
+  const size_t n4 = n / 4, stride = (size_t)gridDim.x * blockDim.x;
+  const float4 *g4 = reinterpret_cast<const float4 *>(g), *u4 = reinterpret_cast<const float4 *>(u);
+  const float4 *d4 = reinterpret_cast<const float4 *>(dact);
+  float4 *dg4 = reinterpret_cast<float4 *>(dg), *du4 = reinterpret_cast<float4 *>(du);
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
+    const float4 z = __ldcs(g4 + i), v = __ldcs(u4 + i), a = __ldcs(d4 + i);
+    float4 og, ou;
+    swiglu_bwd_elem(z.x, v.x, a.x, og.x, ou.x);
+    swiglu_bwd_elem(z.y, v.y, a.y, og.y, ou.y);
+    swiglu_bwd_elem(z.z, v.z, a.z, og.z, ou.z);
+    swiglu_bwd_elem(z.w, v.w, a.w, og.w, ou.w);
+    dg4[i] = og;
+    du4[i] = ou;
   }
+  for (size_t i = n4 * 4 + (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+    swiglu_bwd_elem(g[i], u[i], dact[i], dg[i], du[i]);
 }
 // hk = fn + silu(t1)   (tinylm.c:1046-1047)
 __global__ void mtp_hk_kernel(const float *__restrict__ fn, const float *__restrict__ t1,
@@ -585,14 +633,14 @@ int k_rmsnorm_fwd(DeviceCtx *c, const float *x, const float *g, float *out, floa
   MK_LAUNCH_CHECK();
   return TL_OK;
 }
-int k_rmsnorm_bwd(DeviceCtx *c, const float *x, const float *g, const float *rinv, const float *dy, float *dx,
-                  float *dg, float *part, int part_rows, int rows, int D) {
+int k_rmsnorm_bwd(DeviceCtx *c, const float *x, const float *g, const float *rinv, const float *dy,
+                  const float *dres, float *dx, float *dg, float *part, int part_rows, int rows, int D) {
   TraceScope ts(c, "k_rmsnorm_bwd");
   int nb = (rows + 7) / 8;
   if (nb > part_rows) nb = part_rows;
-  mk::rmsnorm_bwd_kernel<<<nb, 256, sizeof(float) * 8 * D, c->stream>>>(x, g, rinv, dy, dx, part, rows, D);
+  mk::rmsnorm_bwd_kernel<<<nb, 256, sizeof(float) * 8 * D, c->stream>>>(x, g, rinv, dy, dres, dx, part, rows, D);
   MK_LAUNCH_CHECK();
-  mk::colsum_add_kernel<<<(D + 255) / 256, 256, 0, c->stream>>>(part, nb, D, dg);
+  mk::colsum_add_kernel<<<(D + 31) / 32, 256, 0, c->stream>>>(part, nb, D, dg);
   MK_LAUNCH_CHECK();
   return TL_OK;
 }
