@@ -888,22 +888,32 @@ int gemm_tc(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, i
   gemm_dims(op, M, K, N, &I, &J, &R);
   tc::Params p;
   p.C = C; p.I = I; p.J = J; p.R = R; p.err = c->err_flag;
-  // Split-K when the output has too few tiles to fill the GPU (e.g. weight
-  // gradients of narrow layers, whose reduction runs over all tokens): each
-  // split gets at least one TMEM chunk of k-blocks, partials go to the
-  // context's workspace and a fixed-order reduction adds them into C.
-  // A pair tile (256 x 256) occupies two SMs.
+  // Split-K.  A launch takes ceil(CTAs / SMs) waves of (k-blocks per split)
+  // k-block times; splitting the reduction over s CTAs multiplies the CTAs by
+  // s and divides the k-blocks by s, so the split count is chosen to minimise
+  // waves * k-blocks plus the cost of the fixed-order reduction of the s
+  // partials (s + 1 passes over the output at ~6 TB/s, ~1 us per k-block
+  // time).  This fills the GPU for outputs with few tiles (weight gradients,
+  // whose reduction runs over all tokens) and evens out the last wave.  Each
+  // split gets whole TMEM chunks of k-blocks; partials go to the context's
+  // workspace.  A pair tile (256 x 256) occupies two SMs.
   const int tm = pair ? tc::PM : tc::BM, tn = pair ? tc::PN : tc::BN, sms_per_tile = pair ? 2 : 1;
-  const int tiles = ((I + tm - 1) / tm) * ((J + tn - 1) / tn);
+  const long long tiles = (long long)((I + tm - 1) / tm) * ((J + tn - 1) / tn);
   const int nk = (R + tc::BK - 1) / tc::BK;
   int splits = 1;
-  if (tiles * sms_per_tile < c->num_sms && c->gemm_ws) {
-    splits = c->num_sms / (tiles * sms_per_tile);
-    splits = std::min(splits, nk / tc::CHUNK_KB);
-    splits = std::min(splits, 64);
+  if (c->gemm_ws) {
     const size_t cap = c->gemm_ws_floats / ((size_t)I * J);
-    splits = (int)std::min<size_t>((size_t)splits, cap);
-    if (splits < 2) splits = 1;
+    const int smax = (int)std::min<size_t>(std::min(64, nk / tc::CHUNK_KB), cap);
+    const double out_units = (double)I * J * 4.0 / 6.0e6;  // one output pass, in k-block times
+    double best = 0.0;
+    for (int s = 1; s <= std::max(1, smax); s++) {
+      const long long ctas = tiles * sms_per_tile * s;
+      const long long waves = (ctas + c->num_sms - 1) / c->num_sms;
+      int kb = (nk + s - 1) / s;
+      if (s > 1) kb = (kb + tc::CHUNK_KB - 1) / tc::CHUNK_KB * tc::CHUNK_KB;
+      const double cost = (double)waves * kb + (s > 1 ? (s + 1) * out_units : 0.0);
+      if (s == 1 || cost < best * 0.97) { best = cost; splits = s; }
+    }
   }
   int kb_per = nk;
   if (splits > 1) {
