@@ -229,7 +229,9 @@ int tl_zero1_step(float *P, float *G, float *M_shard, float *V_shard, size_t n,
  * from every rank's G (rank order 0..R-1) fused with the shard's sum of
  * squares; shard sums are exchanged through peer stores; AdamW on the shard
  * stores the updated parameters into every rank's P.  Same results as
- * tl_zero1_step (bit for bit at R = 2, 4, 8).  Before the first step every rank
+ * tl_zero1_step (bit for bit at R = 2; at larger R the gradient sums may
+ * differ in the last bit, rank order here against NCCL's algorithm order).
+ * Before the first step every rank
  * registers its own P and G (n_pad floats each, 16-byte aligned, cudaMalloc
  * memory that CUDA IPC can share) -- a collective call; tl_zero1_step_p2p must
  * then be given exactly those buffers.  Device waits are bounded by
