@@ -73,6 +73,8 @@ def parse():
     ap.add_argument("--op", default="all", choices=["all", "mm", "mm_bt", "mm_atb"], help="gemm workload: primitive")
     ap.add_argument("--zero1", default="nccl", choices=["nccl", "p2p"],
                     help="N>1: ZeRO-1 exchanges by NCCL collectives or by the library's peer-memory kernels")
+    ap.add_argument("--no-overlap", action="store_true",
+                    help="N>1, nccl exchange: reduce-scatter after the backward instead of per-shard reductions during it")
     ap.add_argument("--gemm-engine", type=int, default=0, choices=[0, 1, 2, 3],
                     help="GEMM engine: 0 automatic, 1 CUDA-core, 2 tensor-core one CTA, 3 tensor-core CTA pair")
     return ap.parse_args()
@@ -354,6 +356,9 @@ def run_train(args, rk):
     if world == 1:
         def step(t):
             m.step(P, G, M, V, tok, tgt, mtp, B, LR, t, MAX_NORM, loss, norm)
+    elif args.zero1 == "nccl" and not args.no_overlap:
+        def step(t):   # tl_model_step_zero1: shard reductions overlap the backward pass
+            m.step_zero1(z, P, G, M, V, tok, tgt, mtp, B, LR, t, MAX_NORM, loss, norm)
     else:
         def step(t):
             G.zero_()
@@ -392,7 +397,7 @@ def run_train(args, rk):
         e2e = {"value": round(B_glob * T_CTX / (ms * 1e-3), 1), "unit": "tokens/s",
                "h2d_bytes_per_step": sum(h.numel() * 4 for h in hs) * world, "d2h_bytes_per_step": 4,
                "steps": steps, "ms_per_step": round(ms, 3),
-               "path": "pinned host tokens -> tl_model_step (N=1) / tl_model_forward_backward + tl_zero1_step -> host loss"}
+               "path": "pinned host tokens -> tl_model_step (N=1) / tl_model_step_zero1 (N>1) -> host loss"}
 
     # ---- roofline of the dominant kernel (the tensor-core GEMM)
     peaks, peak_kind = measured_peaks()
@@ -433,7 +438,8 @@ def run_train(args, rk):
                "data": "synthetic (uniform random token ids, seeded); weights from the reference's seeded init_params",
                "config": {"workload": cfg_name, "model": preset, "n_params": n, "n_mtp": n_mtp,
                           "global_batch": B_glob, "seq_len": T_CTX, "micro_batch": mb,
-                          "parallelism": "single" if world == 1 else f"dp{world}_zero1_{args.zero1}",
+                          "parallelism": "single" if world == 1 else
+                          f"dp{world}_zero1_{args.zero1}" + ("" if args.zero1 != "nccl" or args.no_overlap else "_overlap"),
                           "gemm_gflop_per_token": round(gflop_tok / 1e9, 4),
                           "l2": "per-step working set >> 126 MB L2 (no flush needed)"},
                "e2e": e2e, "roofline": roofline, "clocks": clocks, "gpu_launches": launches,

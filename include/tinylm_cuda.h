@@ -169,6 +169,18 @@ int tl_model_forward_backward(void *handle, const float *P, float *G, const int 
  * 0.95, 0.1, t): one step of train_loop / cmd_bench (tinylm.c:2627-2633). */
 int tl_model_step(void *handle, float *P, float *G, float *M, float *V, const int *tok, const int *tgt,
                   const int *tgt_mtp, int B, float lr, int t, float max_norm, float *loss_dev, float *norm_dev);
+/* The data-parallel step (after tl_dist_init): this rank's batch of B
+ * sequences through forward/backward, the ZeRO-1 update of tl_zero1_step on
+ * the padded buffers (P, G: n_pad floats; M_shard, V_shard: this rank's shard;
+ * n_pad = tl_zero1_padded(nparams, world)), with the gradient reduction
+ * overlapped with the backward pass: each rank's shard of G is reduced
+ * (average) onto its owner as soon as the backward has finished every
+ * gradient inside it.  Same result as tl_model_forward_backward +
+ * tl_zero1_step (bit for bit at 2 ranks).  loss_dev is this rank's own
+ * mean loss. */
+int tl_model_step_zero1(void *handle, float *P, float *G, float *M_shard, float *V_shard, const int *tok,
+                        const int *tgt, const int *tgt_mtp, int B, float lr, int t, float max_norm,
+                        float *loss_dev, float *norm_dev);
 
 /* ------------------------------------- training loop: host-side pieces */
 /* Checkpoints in the reference's formats.  Buffers may be host or device

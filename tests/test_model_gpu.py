@@ -118,6 +118,31 @@ def test_micro_batching_changes_only_rounding(cuda):
     assert rel.item() < 1e-5
 
 
+def test_step_is_deterministic(cuda):
+    """The same forward/backward twice (repeated tokens in the batch, two
+    micro-batches, MTP head): identical loss and gradient bits -- no kernel of
+    the step sums in a timing-dependent order (the embedding scatter adds rows
+    in token order)."""
+    c = model.cfg8("nano", 1)
+    P = model.init_params(c, 11).to(cuda)
+    n = P.numel()
+    g = torch.Generator(device=cuda).manual_seed(5)
+    tok = torch.randint(0, 40, (4 * 256,), generator=g, device=cuda, dtype=torch.int32)   # many repeats
+    tgt = torch.randint(0, 512, (4 * 256,), generator=g, device=cuda, dtype=torch.int32)
+    mtp = torch.randint(0, 512, (1, 4 * 256), generator=g, device=cuda, dtype=torch.int32)
+    m = model.Model(c, 2, 0)
+    out = []
+    for _ in range(2):
+        G = torch.zeros(n, device=cuda)
+        loss = torch.zeros(1, device=cuda)
+        m.forward_backward(P, G, tok, tgt, mtp, 4, loss)
+        torch.cuda.synchronize()
+        out.append((loss.clone(), G))
+    _lib.check(_lib.lib().tl_device_status())
+    m.close()
+    assert torch.equal(out[0][0], out[1][0]) and torch.equal(out[0][1], out[1][1])
+
+
 def test_scaled_config_one_step(cuda):
     """BASELINE config 5 shape (188.8 M parameters) runs one step at batch 1:
     initial loss near ln(8192) + var(logits)/2 (logit std ~ 0.02*sqrt(1024)),

@@ -171,3 +171,11 @@ def test_two_rank_trainer_matches_one_rank(cuda, tmp_path):
         assert abs(x - y) <= 2e-4, (v1, v2)
     _, P3 = read_bundle(a[0], n)
     compare_runs((str(tmp_path / "w2r.bin"), str(tmp_path / "w2r.opt")), r1, P3, n)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_rank_overlapped_reduction_is_bit_identical(cuda, tmp_path):
+    """tl_model_step_zero1 (shard reductions issued during the backward pass,
+    two micro-batches per rank) against forward_backward + tl_zero1_step: at
+    two ranks every sum has two terms, so the results are the same bits."""
+    _torchrun([str(tmp_path), "overlap"], 29545)

@@ -75,6 +75,9 @@ SIGNATURES = {
                                            _c_int, _c_void_p]),
     "tl_model_step": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
                                _c_void_p, _c_int, _c_float, _c_int, _c_float, _c_void_p, _c_void_p]),
+    "tl_model_step_zero1": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
+                                     _c_void_p, _c_void_p, _c_int, _c_float, _c_int, _c_float, _c_void_p,
+                                     _c_void_p]),
     "tl_zero1_padded": (_c_size, [_c_size, _c_int]),
     "tl_dist_unique_id": (_c_int, [_c_void_p]),
     "tl_dist_init": (_c_int, [_c_int, _c_int, _c_void_p]),

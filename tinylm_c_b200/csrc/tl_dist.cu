@@ -16,6 +16,7 @@
 #include <cstring>
 #include <thread>
 #include "tl_common.cuh"
+#include "tl_dist.cuh"
 
 namespace tl {
 int launch_sumsq(DeviceCtx *c, const float *G, size_t n, double *sumsq_out, float *norm_out,
@@ -29,6 +30,8 @@ struct DistCtx {
   ncclComm_t comm = nullptr;
   int rank = 0, world = 1, device = -1;
   bool ready = false;
+  cudaStream_t side = nullptr;            // overlapped shard reductions
+  cudaEvent_t ev[kMaxShards + 1] = {};
 };
 static DistCtx g_dist[kMaxDevices];
 
@@ -139,6 +142,12 @@ TL_API int tl_dist_finalize(void) {
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return TL_OK;
   p2p_release_device(dev);
   DistCtx &d = g_dist[dev];
+  if (d.side) {
+    cudaStreamSynchronize(d.side);
+    for (auto &e : d.ev) if (e) { cudaEventDestroy(e); e = nullptr; }
+    cudaStreamDestroy(d.side);
+    d.side = nullptr;
+  }
   if (d.comm) {
     ncclCommFinalize(d.comm);
     ncclResult_t st = ncclInProgress;
@@ -194,10 +203,30 @@ TL_API int tl_dist_sync(int timeout_ms_arg) {
   }
 }
 
-TL_API int tl_zero1_step(float *P, float *G, float *M_shard, float *V_shard, size_t n, float lr,
-                         float b1, float b2, float wd, int t, float max_norm, float *norm_dev) {
-  TL_REQUIRE_CTX(c);
-  DistCtx *d = dist();
+namespace tl {
+
+// Steps 2-5 of the ZeRO-1 step, once this rank's shard of G holds the
+// averaged gradient: shard sum of squares -> all-reduce -> clip scale ->
+// AdamW on the shard -> all-gather of P.
+static int zero1_tail(DeviceCtx *c, DistCtx *d, float *P, float *G, float *M_shard, float *V_shard, size_t shard,
+                      float lr, float b1, float b2, float wd, int t, float max_norm, float *norm_dev) {
+  int rc;
+  float *Gs = G + (size_t)d->rank * shard;
+  float *Ps = P + (size_t)d->rank * shard;
+  if ((rc = launch_sumsq(c, Gs, shard, c->sumsq, nullptr, nullptr, max_norm))) return rc;
+  ncclResult_t r = ncclAllReduce(c->sumsq, c->sumsq, 1, ncclDouble, ncclSum, d->comm, c->stream);
+  if ((rc = nccl_settle(*d, r, "ncclAllReduce(sumsq)"))) return rc;
+  float *gscale = c->scalars + 1;
+  clip_scale_kernel<<<1, 1, 0, c->stream>>>(c->sumsq, max_norm, norm_dev, gscale);
+  TL_TRY_CUDA(cudaGetLastError());
+  if ((rc = launch_adamw(c, Ps, Gs, M_shard, V_shard, shard, lr, b1, b2, wd, t, 1.0f, gscale))) return rc;
+  r = ncclAllGather(Ps, P, shard, ncclFloat, d->comm, c->stream);
+  return nccl_settle(*d, r, "ncclAllGather(P)");
+}
+
+static int zero1_args(DeviceCtx *c, DistCtx *d, float *P, float *G, float *M_shard, float *V_shard, int t,
+                      float max_norm) {
+  (void)c;
   if (!d) return set_error(TL_ENOINIT, "tl_dist_init() not called for this device");
   if (t < 1) return set_error(TL_EINVAL, "step t must be >= 1 (got %d)", t);
   if (!(max_norm > 0.0f)) return set_error(TL_EINVAL, "max_norm must be > 0");
@@ -205,23 +234,85 @@ TL_API int tl_zero1_step(float *P, float *G, float *M_shard, float *V_shard, siz
   if ((rc = check_device_ptr(P, "P")) || (rc = check_device_ptr(G, "G")) ||
       (rc = check_device_ptr(M_shard, "M_shard")) || (rc = check_device_ptr(V_shard, "V_shard")))
     return rc;
+  return TL_OK;
+}
+
+// ------------------------------------------------ reduction overlapped with backward
+// The shards double as buckets: shard j is reduced (average) onto its owner
+// rank j with one ncclReduce as soon as the backward pass has finished every
+// gradient inside it.  The backward fills the flat G from the end (MTP heads,
+// final norm, last layer ...) towards the embedding at offset 0, so the high
+// shards go out while the early layers are still being differentiated.  The
+// reductions run on a side stream ordered by events; every rank issues them
+// in the same order (shard R-1 down to 0), so the communicator sees one
+// sequence.  At the end the library stream waits for the side stream.
+int overlap_begin(DeviceCtx *c, float *G, size_t n, OverlapState *o) {
+  DistCtx *d = dist();
+  if (!d) return set_error(TL_ENOINIT, "tl_dist_init() not called for this device");
+  if (!d->side) {
+    TL_TRY_CUDA(cudaStreamCreateWithFlags(&d->side, cudaStreamNonBlocking));
+    for (int i = 0; i < kMaxShards + 1; i++) TL_TRY_CUDA(cudaEventCreateWithFlags(&d->ev[i], cudaEventDisableTiming));
+  }
+  if (d->world > kMaxShards) return set_error(TL_EINVAL, "overlapped reduction supports up to %d ranks", kMaxShards);
+  o->G = G;
+  o->n_pad = tl_zero1_padded(n, d->world);
+  o->shard = o->n_pad / d->world;
+  o->next = d->world - 1;   // highest shard not issued yet
+  o->events = 0;
+  return TL_OK;
+}
+
+// G[done_from, n_pad) is final: reduce every remaining shard inside it.
+int overlap_ready(DeviceCtx *c, OverlapState *o, size_t done_from) {
+  DistCtx *d = dist();
+  if (!d) return set_error(TL_ENOINIT, "tl_dist_init() not called for this device");
+  if (o->next < 0 || (size_t)o->next * o->shard < done_from) return TL_OK;
+  cudaEvent_t ev = d->ev[o->events++];
+  TL_TRY_CUDA(cudaEventRecord(ev, c->stream));
+  TL_TRY_CUDA(cudaStreamWaitEvent(d->side, ev, 0));
+  while (o->next >= 0 && (size_t)o->next * o->shard >= done_from) {
+    float *Gj = o->G + (size_t)o->next * o->shard;
+    ncclResult_t r = ncclReduce(Gj, Gj, o->shard, ncclFloat, ncclAvg, o->next, d->comm, d->side);
+    int rc = nccl_settle(*d, r, "ncclReduce(G shard)");
+    if (rc) return rc;
+    o->next--;
+  }
+  return TL_OK;
+}
+
+// Reduce what is left and join the side stream into the library stream.
+int overlap_finish(DeviceCtx *c, OverlapState *o) {
+  int rc = overlap_ready(c, o, 0);
+  if (rc) return rc;
+  DistCtx *d = dist();
+  cudaEvent_t ev = d->ev[kMaxShards];
+  TL_TRY_CUDA(cudaEventRecord(ev, d->side));
+  TL_TRY_CUDA(cudaStreamWaitEvent(c->stream, ev, 0));
+  return TL_OK;
+}
+
+int zero1_finish_after_overlap(DeviceCtx *c, float *P, float *G, float *M_shard, float *V_shard, size_t n,
+                               float lr, float b1, float b2, float wd, int t, float max_norm, float *norm_dev) {
+  DistCtx *d = dist();
+  int rc = zero1_args(c, d, P, G, M_shard, V_shard, t, max_norm);
+  if (rc) return rc;
+  const size_t shard = tl_zero1_padded(n, d->world) / d->world;
+  return zero1_tail(c, d, P, G, M_shard, V_shard, shard, lr, b1, b2, wd, t, max_norm, norm_dev);
+}
+
+}  // namespace tl
+
+TL_API int tl_zero1_step(float *P, float *G, float *M_shard, float *V_shard, size_t n, float lr,
+                         float b1, float b2, float wd, int t, float max_norm, float *norm_dev) {
+  TL_REQUIRE_CTX(c);
+  DistCtx *d = dist();
+  int rc = zero1_args(c, d, P, G, M_shard, V_shard, t, max_norm);
+  if (rc) return rc;
   const size_t n_pad = tl_zero1_padded(n, d->world);
   const size_t shard = n_pad / d->world;
   float *Gs = G + (size_t)d->rank * shard;
-  float *Ps = P + (size_t)d->rank * shard;
   // 1. gradient average, this rank's shard lands in place
   ncclResult_t r = ncclReduceScatter(G, Gs, shard, ncclFloat, ncclAvg, d->comm, c->stream);
   if ((rc = nccl_settle(*d, r, "ncclReduceScatter(G)"))) return rc;
-  // 2. shard sum of squares -> 3. global sum -> clip scale
-  if ((rc = launch_sumsq(c, Gs, shard, c->sumsq, nullptr, nullptr, max_norm))) return rc;
-  r = ncclAllReduce(c->sumsq, c->sumsq, 1, ncclDouble, ncclSum, d->comm, c->stream);
-  if ((rc = nccl_settle(*d, r, "ncclAllReduce(sumsq)"))) return rc;
-  float *gscale = c->scalars + 1;
-  clip_scale_kernel<<<1, 1, 0, c->stream>>>(c->sumsq, max_norm, norm_dev, gscale);
-  TL_TRY_CUDA(cudaGetLastError());
-  // 4. AdamW on the owned shard
-  if ((rc = launch_adamw(c, Ps, Gs, M_shard, V_shard, shard, lr, b1, b2, wd, t, 1.0f, gscale))) return rc;
-  // 5. every rank receives the updated parameters
-  r = ncclAllGather(Ps, P, shard, ncclFloat, d->comm, c->stream);
-  return nccl_settle(*d, r, "ncclAllGather(P)");
+  return zero1_tail(c, d, P, G, M_shard, V_shard, shard, lr, b1, b2, wd, t, max_norm, norm_dev);
 }

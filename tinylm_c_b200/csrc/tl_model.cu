@@ -17,6 +17,7 @@
 #include <vector>
 #include "tl_gemm.cuh"
 #include "tl_model.cuh"
+#include "tl_dist.cuh"
 #include "tl_trace.cuh"
 
 namespace tl {
@@ -90,8 +91,10 @@ static int gemm_add(DeviceCtx *c, GemmOp op, float *C, const float *A, const flo
 }
 
 // One micro-batch: forward + backward, gradients accumulated into G.
+// ov (data-parallel step only, last micro-batch): told after each layer which
+// tail of G is final, so shard reductions start during the backward pass.
 static int micro_step(DeviceCtx *c, Model &m, const float *P, float *G, const int *tok, const int *tgt,
-                      const int *const *tgt_mtp, float scale, bool backward) {
+                      const int *const *tgt_mtp, float scale, bool backward, OverlapState *ov = nullptr) {
   const int N = m.N, D = m.D, F = m.F, KD = m.KD, V = m.V;
   const size_t ND = (size_t)N * D, NF = (size_t)N * F;
   const float *emb = P + m.o_emb;
@@ -142,6 +145,7 @@ static int micro_step(DeviceCtx *c, Model &m, const float *P, float *G, const in
   }
   TRY(k_rmsnorm_bwd(c, m.x_final, P + m.o_nf, m.fn_rinv, m.dfn, nullptr, m.dout, G + m.o_nf, m.rms_part,
                     RMS_PART_ROWS, N, D));
+  if (ov) TRY(overlap_ready(c, ov, m.o_nf));            // final norm and MTP heads are done
   for (int l = m.L - 1; l >= 0; l--) {
     // FFN
     TRY(gemm(c, GemmOp::TN, G + m.o_w2[l], m.act[l], m.dout, N, F, D));
@@ -172,13 +176,14 @@ static int micro_step(DeviceCtx *c, Model &m, const float *P, float *G, const in
     TRY(k_rmsnorm_bwd(c, m.a_in[l], P + m.o_an1[l], m.rinv1[l], m.dnorm, m.dfin, m.dain, G + m.o_an1[l],
                       m.rms_part, RMS_PART_ROWS, N, D));
     std::swap(m.dout, m.dain);
+    if (ov) TRY(overlap_ready(c, ov, m.o_an1[l]));       // layers l..L-1 are done
   }
   TRY(k_embed_bwd(c, gemb, tok, m.dout, N, D, V));
   return TL_OK;
 }
 
 static int run_batch(DeviceCtx *c, Model &m, const float *P, float *G, const int *tok, const int *tgt,
-                     const int *tgt_mtp, int B, float *loss_dev, bool backward) {
+                     const int *tgt_mtp, int B, float *loss_dev, bool backward, OverlapState *ov = nullptr) {
   if (B < 1 || B % m.mb) return set_error(TL_EINVAL, "batch %d must be a positive multiple of the micro-batch %d", B, m.mb);
   const size_t Ntot = (size_t)B * m.T;
   const float scale = 1.0f / (float)Ntot;
@@ -187,7 +192,8 @@ static int run_batch(DeviceCtx *c, Model &m, const float *P, float *G, const int
   for (int i = 0; i < B / m.mb; i++) {
     const size_t off = (size_t)i * m.N;
     for (int kh = 0; kh < m.n_mtp; kh++) mt[kh] = tgt_mtp + (size_t)kh * Ntot + off;
-    TRY(micro_step(c, m, P, G, tok + off, tgt + off, mt.data(), scale, backward));
+    TRY(micro_step(c, m, P, G, tok + off, tgt + off, mt.data(), scale, backward,
+                   i == B / m.mb - 1 ? ov : nullptr));
   }
   if (loss_dev) TRY(k_loss_final(c, m.loss_acc, (double)Ntot, loss_dev));
   return TL_OK;
@@ -381,4 +387,28 @@ TL_API int tl_model_step(void *h, float *P, float *G, float *M, float *V, const 
   float *gscale = c->scalars + 1;                                              // 2630-2631
   if ((rc = launch_sumsq(c, G, m->np, c->sumsq, norm_dev, gscale, max_norm))) return rc;
   return launch_adamw(c, P, G, M, V, m->np, lr, 0.9f, 0.95f, 0.1f, t, 1.0f, gscale);  // 2633
+}
+
+
+TL_API int tl_model_step_zero1(void *h, float *P, float *G, float *M_shard, float *V_shard, const int *tok,
+                               const int *tgt, const int *tgt_mtp, int B, float lr, int t, float max_norm,
+                               float *loss_dev, float *norm_dev) {
+  Model *m = static_cast<Model *>(h);
+  if (!m) return set_error(TL_EINVAL, "NULL model");
+  TL_REQUIRE_CTX(c);
+  if (c->device != m->device) return set_error(TL_EINVAL, "model belongs to device %d", m->device);
+  if (t < 1) return set_error(TL_EINVAL, "step t must be >= 1 (got %d)", t);
+  int rc;
+  if ((rc = check_device_ptr(P, "P")) || (rc = check_device_ptr(G, "G")) || (rc = check_device_ptr(tok, "tok")) ||
+      (rc = check_device_ptr(tgt, "tgt")) || (rc = check_device_ptr(M_shard, "M_shard")) ||
+      (rc = check_device_ptr(V_shard, "V_shard")))
+    return rc;
+  if (m->n_mtp > 0 && (rc = check_device_ptr(tgt_mtp, "tgt_mtp"))) return rc;
+  OverlapState ov;
+  if ((rc = overlap_begin(c, G, m->np, &ov))) return rc;
+  TL_TRY_CUDA(cudaMemsetAsync(G, 0, sizeof(float) * ov.n_pad, c->stream));
+  if ((rc = run_batch(c, *m, P, G, tok, tgt, tgt_mtp, B, loss_dev, true, &ov))) return rc;
+  if ((rc = overlap_finish(c, &ov))) return rc;
+  return zero1_finish_after_overlap(c, P, G, M_shard, V_shard, m->np, lr, 0.9f, 0.95f, 0.1f, t, max_norm,
+                                    norm_dev);
 }

@@ -48,15 +48,56 @@ __global__ void embed_fwd_kernel(const float *__restrict__ emb, const int *__res
 }
 
 // dEmb[tok[n], :] += dout[n, :]   (tinylm.c:1148-1153)
-__global__ void embed_bwd_kernel(float *__restrict__ gemb, const int *__restrict__ tok,
-                                 const float *__restrict__ dout, int N, int D, int V) {
-  const int n = blockIdx.x;
-  if (n >= N) return;
-  const int t = tok[n];
-  if (t < 0 || t >= V) return;
-  float *dst = gemb + (size_t)t * D;
-  const float *src = dout + (size_t)n * D;
-  for (int d = threadIdx.x; d < D; d += blockDim.x) atomicAdd(dst + d, src[d]);
+// gemb[v] += dout[n] for every n with tok[n] == v, in increasing n, starting
+// from the gradient already in gemb: the reference's single-threaded scatter
+// order (tinylm.c:1148-1153), so the result is deterministic and the same
+// bits as that loop (no atomics).  One warp per vocabulary row scans the
+// batch's tokens 32 at a time (ballot) and adds the matching rows; columns go
+// in chunks of 32*EMB_CHUNK so the sums stay in registers.  Rows of tokens
+// outside [0, V) are never added (embed_fwd reports them).
+constexpr int EMB_CHUNK = 8;
+__global__ void __launch_bounds__(256)
+embed_bwd_kernel(float *__restrict__ gemb, const int *__restrict__ tok, const float *__restrict__ dout, int N,
+                 int D, int V) {
+  const int lane = threadIdx.x & 31;
+  const int nwarps = (gridDim.x * blockDim.x) >> 5;
+  for (int v = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; v < V; v += nwarps) {
+    float *row = gemb + (size_t)v * D;
+    for (int c0 = 0; c0 < D; c0 += 32 * EMB_CHUNK) {
+      float acc[EMB_CHUNK];
+      bool any = false;
+      for (int base = 0; base < N; base += 32) {
+        const int n = base + lane;
+        const int t = n < N ? __ldg(tok + n) : -1;
+        unsigned mask = __ballot_sync(0xffffffffu, t == v);
+        if (mask && !any) {
+#pragma unroll
+          for (int e = 0; e < EMB_CHUNK; e++) {
+            const int d = c0 + e * 32 + lane;
+            acc[e] = d < D ? row[d] : 0.0f;
+          }
+          any = true;
+        }
+        while (mask) {
+          const int j = __ffs(mask) - 1;
+          mask &= mask - 1;
+          const float *src = dout + (size_t)(base + j) * D;
+#pragma unroll
+          for (int e = 0; e < EMB_CHUNK; e++) {
+            const int d = c0 + e * 32 + lane;
+            if (d < D) acc[e] += src[d];
+          }
+        }
+      }
+      if (any) {
+#pragma unroll
+        for (int e = 0; e < EMB_CHUNK; e++) {
+          const int d = c0 + e * 32 + lane;
+          if (d < D) row[d] = acc[e];
+        }
+      }
+    }
+  }
 }
 
 // ---------------------------------------------------------------- RMSNorm
@@ -623,7 +664,7 @@ int k_embed_fwd(DeviceCtx *c, const float *emb, const int *tok, float *out, int 
 }
 int k_embed_bwd(DeviceCtx *c, float *gemb, const int *tok, const float *dout, int N, int D, int V) {
   TraceScope ts(c, "k_embed_bwd");
-  mk::embed_bwd_kernel<<<N, 128, 0, c->stream>>>(gemb, tok, dout, N, D, V);
+  mk::embed_bwd_kernel<<<(unsigned)((V + 7) / 8), 256, 0, c->stream>>>(gemb, tok, dout, N, D, V);
   MK_LAUNCH_CHECK();
   return TL_OK;
 }

@@ -86,6 +86,17 @@ class Model:
             None if loss_out is None else ops._ptr(loss_out, "loss_out", 1),
             None if norm_out is None else ops._ptr(norm_out, "norm_out", 1)))
 
+    def step_zero1(self, z, P, G, M_shard, V_shard, tok, tgt, tgt_mtp, B, lr, t, max_norm=1.0, loss_out=None,
+                   norm_out=None):
+        """Data-parallel step over the Zero1 communicator z (NCCL exchange),
+        the gradient reduction overlapped with the backward pass."""
+        ops._prep(P)
+        check(lib().tl_model_step_zero1(
+            self.h, ops._ptr(P, "P", z.n_pad), ops._ptr(G, "G", z.n_pad), ops._ptr(M_shard, "M_shard", z.shard),
+            ops._ptr(V_shard, "V_shard", z.shard), _iptr(tok, "tok"), _iptr(tgt, "tgt"), _iptr(tgt_mtp, "tgt_mtp"),
+            B, lr, int(t), max_norm, None if loss_out is None else ops._ptr(loss_out, "loss_out", 1),
+            None if norm_out is None else ops._ptr(norm_out, "norm_out", 1)))
+
     def close(self):
         if self.h:
             lib().tl_model_destroy(self.h)

@@ -55,11 +55,13 @@ def load_bundle(path, P=None):
 
 
 class Trainer:
-    def __init__(self, cfg, B, micro_batch=None, device=0, rank=0, world=1, exchange="nccl"):
+    def __init__(self, cfg, B, micro_batch=None, device=0, rank=0, world=1, exchange="nccl", overlap=True):
         self.cfg = cfg
         self.T = cfg[6] if cfg[6] > 0 else 256
         self.n_mtp = cfg[7]
         self.B, self.rank, self.world = B, rank, world
+        # NCCL exchange: reduce gradient shards during the backward pass
+        self.overlap = overlap and exchange == "nccl"
         if B % world:
             raise ValueError(f"batch {B} not divisible by {world} ranks")
         self.Bl = B // world
@@ -164,6 +166,9 @@ class Trainer:
         if self.world == 1:
             self.model.step(self.P, self.G, self.M, self.V, self.d_tok, self.d_tgt, self.d_mtp, self.Bl, lr, t,
                             1.0, self.loss, self.norm)
+        elif self.overlap:
+            self.model.step_zero1(self.z, self.P, self.G, self.M, self.V, self.d_tok, self.d_tgt, self.d_mtp,
+                                  self.Bl, lr, t, 1.0, self.loss, self.norm)
         else:
             self.G.zero_()
             self.model.forward_backward(self.P, self.G, self.d_tok, self.d_tgt, self.d_mtp, self.Bl, self.loss)
