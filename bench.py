@@ -73,6 +73,8 @@ def parse():
     ap.add_argument("--op", default="all", choices=["all", "mm", "mm_bt", "mm_atb"], help="gemm workload: primitive")
     ap.add_argument("--zero1", default="nccl", choices=["nccl", "p2p"],
                     help="N>1: ZeRO-1 exchanges by NCCL collectives or by the library's peer-memory kernels")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="train workloads at N=1: launch the step eagerly instead of replaying a CUDA graph")
     ap.add_argument("--no-overlap", action="store_true",
                     help="N>1, nccl exchange: reduce-scatter after the backward instead of per-shard reductions during it")
     ap.add_argument("--gemm-engine", type=int, default=0, choices=[0, 1, 2, 3],
@@ -353,9 +355,13 @@ def run_train(args, rk):
     loss = torch.zeros(1, device=dev)
     norm = torch.zeros(1, device=dev)
 
+    use_graph = world == 1 and not args.no_graph
     if world == 1:
-        def step(t):
+        def eager_step(t):
             m.step(P, G, M, V, tok, tgt, mtp, B, LR, t, MAX_NORM, loss, norm)
+
+        def step(t):   # N=1: the whole step replayed as one CUDA graph (tl_model_graph_step)
+            m.step(P, G, M, V, tok, tgt, mtp, B, LR, t, MAX_NORM, loss, norm, graph=use_graph)
     elif args.zero1 == "nccl" and not args.no_overlap:
         def step(t):   # tl_model_step_zero1: shard reductions overlap the backward pass
             m.step_zero1(z, P, G, M, V, tok, tgt, mtp, B, LR, t, MAX_NORM, loss, norm)
@@ -374,6 +380,15 @@ def run_train(args, rk):
     rk.status()
     value = B_glob * T_CTX / (ms_step * 1e-3)
     loss_val = loss.item()
+    eager_ms = None
+    if use_graph:
+        # A graph replay is one traced launch; the per-kernel breakdown (and the
+        # GEMM roofline) comes from the same step run eagerly with every launch
+        # traced.
+        n_tr = max(1, min(args.steps, 2))
+        eager_ms, kernels, _ = rk.timed(eager_step, n_tr, t0 + args.steps)
+        rk.status()
+        t0 += n_tr
 
     # ---- end to end: tokens from pinned host memory, loss read back, every step
     e2e = None
@@ -412,12 +427,14 @@ def run_train(args, rk):
                 "peak_source": f"{peak_kind} bf16 sustained {bf16} TFLOP/s / 6 (tf32 = bf16/2; 3 tf32 MMAs per fp32 product)",
                 "frac": round(achieved / peak, 4) if achieved else None,
                 "traffic": None, "algorithmic_flops_per_step": flops_rank,
-                "gemm_share_of_step": round(gemm["ms_per_step"] / ms_step, 4) if ms_step else None}
+                "gemm_share_of_step": round(gemm["ms_per_step"] / (eager_ms or ms_step), 4) if ms_step else None}
     tr = committed_traffic(f"{args.workload}:gemm_tc")
     if tr:
         roofline["traffic"] = tr.get("bytes_per_step")
         roofline["traffic_source"] = tr.get("source")
     launches = sum(k["launches"] for k in kernels.values())
+    if use_graph:   # the eager pass ran n_tr steps; the timed region replayed the same kernels args.steps times
+        launches = launches * args.steps // n_tr
 
     adam_line = None
     if kernels.get("adamw_vec", {}).get("ms_per_launch"):
@@ -441,9 +458,12 @@ def run_train(args, rk):
                           "parallelism": "single" if world == 1 else
                           f"dp{world}_zero1_{args.zero1}" + ("" if args.zero1 != "nccl" or args.no_overlap else "_overlap"),
                           "gemm_gflop_per_token": round(gflop_tok / 1e9, 4),
+                          "launch": "cuda_graph" if use_graph else "eager",
                           "l2": "per-step working set >> 126 MB L2 (no flush needed)"},
                "e2e": e2e, "roofline": roofline, "clocks": clocks, "gpu_launches": launches,
                "loss": round(loss_val, 5), "kernels": kernels}
+        if eager_ms is not None:
+            out["eager_ms_per_step"] = round(eager_ms, 3)
         if adam_line:
             out["fused_adamw"] = adam_line
     return out

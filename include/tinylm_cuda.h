@@ -169,6 +169,14 @@ int tl_model_forward_backward(void *handle, const float *P, float *G, const int 
  * 0.95, 0.1, t): one step of train_loop / cmd_bench (tinylm.c:2627-2633). */
 int tl_model_step(void *handle, float *P, float *G, float *M, float *V, const int *tok, const int *tgt,
                   const int *tgt_mtp, int B, float lr, int t, float max_norm, float *loss_dev, float *norm_dev);
+/* tl_model_step as one CUDA graph: captured on the first call (and again when
+ * a buffer, B or max_norm changes) and replayed with a single launch; lr and
+ * the bias corrections of step t are copied to the device before each replay.
+ * Same results as tl_model_step, bit for bit.  The buffers must stay where
+ * they were at capture. */
+int tl_model_graph_step(void *handle, float *P, float *G, float *M, float *V, const int *tok, const int *tgt,
+                        const int *tgt_mtp, int B, float lr, int t, float max_norm, float *loss_dev,
+                        float *norm_dev);
 /* The data-parallel step (after tl_dist_init): this rank's batch of B
  * sequences through forward/backward, the ZeRO-1 update of tl_zero1_step on
  * the padded buffers (P, G: n_pad floats; M_shard, V_shard: this rank's shard;

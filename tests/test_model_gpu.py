@@ -143,6 +143,38 @@ def test_step_is_deterministic(cuda):
     assert torch.equal(out[0][0], out[1][0]) and torch.equal(out[0][1], out[1][1])
 
 
+def test_graph_step_matches_eager_step(cuda):
+    """tl_model_graph_step (one CUDA graph per step, lr and bias corrections
+    read from the device) against tl_model_step: identical bits over steps with
+    different t and lr, and a new capture when an output buffer moves."""
+    c = model.cfg8("m1", 2)
+    P0 = model.init_params(c, 3).to(cuda)
+    n = P0.numel()
+    g = torch.Generator(device=cuda).manual_seed(9)
+    B = 4
+    tok = torch.randint(0, 2048, (B * 256,), generator=g, device=cuda, dtype=torch.int32)
+    tgt = torch.randint(0, 2048, (B * 256,), generator=g, device=cuda, dtype=torch.int32)
+    mtp = torch.randint(0, 2048, (2, B * 256), generator=g, device=cuda, dtype=torch.int32)
+    m = model.Model(c, 2, 0)
+    res = []
+    for graph in (False, True):
+        P, G = P0.clone(), torch.zeros(n, device=cuda)
+        M, V = torch.zeros(n, device=cuda), torch.zeros(n, device=cuda)
+        loss, norm = torch.zeros(1, device=cuda), torch.zeros(1, device=cuda)
+        losses = []
+        for t, lr in ((1, 3e-4), (2, 2e-4), (3, 1e-4)):
+            m.step(P, G, M, V, tok, tgt, mtp, B, lr, t, 1.0, loss, norm, graph=graph)
+            losses.append(loss.clone())
+        loss2 = torch.zeros(1, device=cuda)          # moved output: captured again
+        m.step(P, G, M, V, tok, tgt, mtp, B, 5e-5, 4, 1.0, loss2, norm, graph=graph)
+        torch.cuda.synchronize()
+        res.append((P, M, V, norm.clone(), torch.cat(losses + [loss2])))
+    _lib.check(_lib.lib().tl_device_status())
+    m.close()
+    for a, b in zip(*res):
+        assert torch.equal(a, b)
+
+
 def test_scaled_config_one_step(cuda):
     """BASELINE config 5 shape (188.8 M parameters) runs one step at batch 1:
     initial loss near ln(8192) + var(logits)/2 (logit std ~ 0.02*sqrt(1024)),

@@ -22,7 +22,8 @@ namespace tl {
 int launch_sumsq(DeviceCtx *c, const float *G, size_t n, double *sumsq_out, float *norm_out,
                  float *gscale_out, float max_norm);
 int launch_adamw(DeviceCtx *c, float *P, const float *G, float *M, float *V, size_t n, float lr,
-                 float b1, float b2, float wd, int t, float gscale, const float *gscale_dev);
+                 float b1, float b2, float wd, int t, float gscale, const float *gscale_dev,
+                 const float *hyper = nullptr);
 __global__ void clip_scale_kernel(const double *sumsq, float max_norm, float *norm_out, float *gscale_out);
 void p2p_release_device(int device);
 

@@ -35,6 +35,8 @@ bool gemm_tc_supported(GemmOp op, const float *C, const float *A, const float *B
 // Automatic choice between the two tensor-core kernels for an I x J output
 // with reduction length R.
 bool gemm_tc_prefer_pair(int I, int J, int R);
+// Host-side set-up of every tensor-core kernel (before a CUDA graph capture).
+int gemm_tc_prepare(DeviceCtx *c);
 // pair: the CTA-pair kernel (256 x 256 tiles over two SMs) instead of the
 // one-CTA kernel (128 x 128 tiles).
 int gemm_tc(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, int M, int K, int N, bool pair,

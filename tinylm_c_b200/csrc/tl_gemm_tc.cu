@@ -875,6 +875,23 @@ bool gemm_tc_supported(GemmOp op, const float *C, const float *A, const float *B
   return true;
 }
 
+// Everything the launches set up lazily on the host (driver entry point,
+// shared-memory attributes), done ahead of a CUDA graph capture.
+int gemm_tc_prepare(DeviceCtx *c) {
+  (void)c;
+  int rc = tc::get_encoder();
+  if (rc) return rc;
+#define TL_PREP(K, BYTES) TL_TRY_CUDA(cudaFuncSetAttribute(K, cudaFuncAttributeMaxDynamicSharedMemorySize, BYTES))
+  TL_PREP((tc::gemm_tc_kernel<false, true>), tc::SMEM_BYTES);
+  TL_PREP((tc::gemm_tc_kernel<false, false>), tc::SMEM_BYTES);
+  TL_PREP((tc::gemm_tc_kernel<true, true>), tc::SMEM_BYTES);
+  TL_PREP((tc::gemm_tc_pair_kernel<false, true>), tc::PAIR_SMEM_BYTES);
+  TL_PREP((tc::gemm_tc_pair_kernel<false, false>), tc::PAIR_SMEM_BYTES);
+  TL_PREP((tc::gemm_tc_pair_kernel<true, true>), tc::PAIR_SMEM_BYTES);
+#undef TL_PREP
+  return TL_OK;
+}
+
 bool gemm_tc_prefer_pair(int I, int J, int R) {
   (void)R;
   return I > tc::BM && J > tc::BN;

@@ -24,7 +24,8 @@ namespace tl {
 int launch_sumsq(DeviceCtx *c, const float *G, size_t n, double *sumsq_out, float *norm_out,
                  float *gscale_out, float max_norm);
 int launch_adamw(DeviceCtx *c, float *P, const float *G, float *M, float *V, size_t n, float lr,
-                 float b1, float b2, float wd, int t, float gscale, const float *gscale_dev);
+                 float b1, float b2, float wd, int t, float gscale, const float *gscale_dev,
+                 const float *hyper = nullptr);
 
 constexpr int RMS_PART_ROWS = 1184;
 
@@ -42,6 +43,13 @@ struct Model {
   float *t1, *hk, *dhk, *dt1;
   float *rms_part;
   double *loss_rows, *loss_acc;
+  // CUDA graph of one whole training step (tl_model_graph_step): the buffers
+  // it was captured with, and the per-step scalars it reads on the device
+  // (lr, AdamW bias corrections 1-b1^t, 1-b2^t).
+  cudaGraphExec_t gexec = nullptr;
+  cudaStream_t gstream = nullptr;
+  float *hyper = nullptr;
+  std::vector<uintptr_t> gkey;
 };
 
 // Offsets of every tensor in the flat buffer -- map_weights, tinylm.c:361-393
@@ -297,6 +305,9 @@ TL_API size_t tl_model_nparams(void *h) { return h ? static_cast<Model *>(h)->np
 TL_API int tl_model_destroy(void *h) {
   Model *m = static_cast<Model *>(h);
   if (!m) return TL_OK;
+  if (m->gexec) cudaGraphExecDestroy(m->gexec);
+  if (m->gstream) cudaStreamDestroy(m->gstream);
+  if (m->hyper) cudaFree(m->hyper);
   if (m->arena) cudaFree(m->arena);
   delete m;
   return TL_OK;
@@ -389,6 +400,64 @@ TL_API int tl_model_step(void *h, float *P, float *G, float *M, float *V, const 
   return launch_adamw(c, P, G, M, V, m->np, lr, 0.9f, 0.95f, 0.1f, t, 1.0f, gscale);  // 2633
 }
 
+
+// One training step as a CUDA graph: captured on the first call (and again
+// whenever a buffer, the batch or max_norm changes), then replayed with one
+// launch.  The step's learning rate and bias corrections (1 - b^t in fp32
+// with powf, as the eager step computes them) are copied to the device before
+// each replay, where the captured AdamW kernel reads them; everything else is
+// identical to tl_model_step, to the bit.
+TL_API int tl_model_graph_step(void *h, float *P, float *G, float *M, float *V, const int *tok, const int *tgt,
+                               const int *tgt_mtp, int B, float lr, int t, float max_norm, float *loss_dev,
+                               float *norm_dev) {
+  Model *m = static_cast<Model *>(h);
+  if (!m) return set_error(TL_EINVAL, "NULL model");
+  TL_REQUIRE_CTX(c);
+  if (c->device != m->device) return set_error(TL_EINVAL, "model belongs to device %d", m->device);
+  if (t < 1) return set_error(TL_EINVAL, "step t must be >= 1 (got %d)", t);
+  if (B < 1 || B % m->mb) return set_error(TL_EINVAL, "batch %d must be a positive multiple of the micro-batch %d", B, m->mb);
+  int rc;
+  if ((rc = check_device_ptr(P, "P")) || (rc = check_device_ptr(G, "G")) || (rc = check_device_ptr(M, "M")) ||
+      (rc = check_device_ptr(V, "V")) || (rc = check_device_ptr(tok, "tok")) || (rc = check_device_ptr(tgt, "tgt")))
+    return rc;
+  if (m->n_mtp > 0 && (rc = check_device_ptr(tgt_mtp, "tgt_mtp"))) return rc;
+  if (!m->hyper) TL_TRY_CUDA(cudaMalloc(&m->hyper, 4 * sizeof(float)));
+  if (!m->gstream) TL_TRY_CUDA(cudaStreamCreateWithFlags(&m->gstream, cudaStreamNonBlocking));
+  uint32_t mn_bits;
+  memcpy(&mn_bits, &max_norm, 4);
+  const std::vector<uintptr_t> key = {(uintptr_t)P, (uintptr_t)G, (uintptr_t)M, (uintptr_t)V, (uintptr_t)tok,
+                                      (uintptr_t)tgt, (uintptr_t)tgt_mtp, (uintptr_t)B, (uintptr_t)mn_bits,
+                                      (uintptr_t)loss_dev, (uintptr_t)norm_dev};
+  if (!m->gexec || key != m->gkey) {
+    if (m->gexec) { cudaGraphExecDestroy(m->gexec); m->gexec = nullptr; }
+    if ((rc = gemm_tc_prepare(c))) return rc;
+    TL_TRY_CUDA(cudaStreamSynchronize(c->stream));
+    const cudaStream_t lib_stream = c->stream;
+    TL_TRY_CUDA(cudaStreamBeginCapture(m->gstream, cudaStreamCaptureModeRelaxed));
+    c->stream = m->gstream;
+    trace_suspend(true);
+    float *gscale = c->scalars + 1;
+    rc = cuda_check(cudaMemsetAsync(G, 0, sizeof(float) * m->np, c->stream), "cudaMemsetAsync(G)");
+    if (!rc) rc = run_batch(c, *m, P, G, tok, tgt, tgt_mtp, B, loss_dev, true);
+    if (!rc) rc = launch_sumsq(c, G, m->np, c->sumsq, norm_dev, gscale, max_norm);
+    if (!rc) rc = launch_adamw(c, P, G, M, V, m->np, lr, 0.9f, 0.95f, 0.1f, t, 1.0f, gscale, m->hyper);
+    trace_suspend(false);
+    c->stream = lib_stream;
+    cudaGraph_t graph = nullptr;
+    const cudaError_t ec = cudaStreamEndCapture(m->gstream, &graph);
+    if (rc) { if (graph) cudaGraphDestroy(graph); return rc; }
+    if (ec != cudaSuccess) return cuda_check(ec, "cudaStreamEndCapture");
+    const cudaError_t ei = cudaGraphInstantiate(&m->gexec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (ei != cudaSuccess) { m->gexec = nullptr; return cuda_check(ei, "cudaGraphInstantiate"); }
+    m->gkey = key;
+  }
+  const float hy[4] = {lr, 1.0f - powf(0.9f, (float)t), 1.0f - powf(0.95f, (float)t), 0.0f};
+  TL_TRY_CUDA(cudaMemcpyAsync(m->hyper, hy, sizeof hy, cudaMemcpyHostToDevice, c->stream));
+  TraceScope ts(c, "graph_step");
+  TL_TRY_CUDA(cudaGraphLaunch(m->gexec, c->stream));
+  return TL_OK;
+}
 
 TL_API int tl_model_step_zero1(void *h, float *P, float *G, float *M_shard, float *V_shard, const int *tok,
                                const int *tgt, const int *tgt_mtp, int B, float lr, int t, float max_norm,

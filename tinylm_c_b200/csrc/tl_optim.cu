@@ -88,7 +88,8 @@ __global__ void clip_scale_kernel(const double *__restrict__ sumsq, float max_no
 // unrolled so eight 16-byte loads are in flight per thread.
 __global__ void __launch_bounds__(256)
 adamw_vec_kernel(float4 *__restrict__ P, const float4 *__restrict__ G, float4 *__restrict__ M,
-                 float4 *__restrict__ V, size_t n4, AdamArgs a) {
+                 float4 *__restrict__ V, size_t n4, AdamArgs a0) {
+  const AdamArgs a = adam_live(a0);
   const float gs = a.gscale_ptr ? __ldg(a.gscale_ptr) : a.gscale;
   const size_t stride = (size_t)gridDim.x * blockDim.x;
   size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -116,7 +117,8 @@ adamw_vec_kernel(float4 *__restrict__ P, const float4 *__restrict__ G, float4 *_
 // Scalar path: unaligned buffers and the tail of the vector body.
 __global__ void adamw_scalar_kernel(float *__restrict__ P, const float *__restrict__ G,
                                     float *__restrict__ M, float *__restrict__ V, size_t n,
-                                    AdamArgs a) {
+                                    AdamArgs a0) {
+  const AdamArgs a = adam_live(a0);
   const float gs = a.gscale_ptr ? __ldg(a.gscale_ptr) : a.gscale;
   const size_t stride = (size_t)gridDim.x * blockDim.x;
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
@@ -136,9 +138,11 @@ int launch_sumsq(DeviceCtx *c, const float *G, size_t n, double *sumsq_out, floa
 }
 
 int launch_adamw(DeviceCtx *c, float *P, const float *G, float *M, float *V, size_t n, float lr,
-                 float b1, float b2, float wd, int t, float gscale, const float *gscale_dev) {
+                 float b1, float b2, float wd, int t, float gscale, const float *gscale_dev,
+                 const float *hyper = nullptr) {
   if (n == 0) return TL_OK;
-  const AdamArgs a = make_adam_args(lr, b1, b2, wd, t, gscale, gscale_dev);
+  AdamArgs a = make_adam_args(lr, b1, b2, wd, t, gscale, gscale_dev);
+  a.hyper = hyper;
   const bool aligned = ((reinterpret_cast<uintptr_t>(P) | reinterpret_cast<uintptr_t>(G) |
                          reinterpret_cast<uintptr_t>(M) | reinterpret_cast<uintptr_t>(V)) & 15) == 0;
   size_t done = 0;

@@ -34,7 +34,22 @@ __device__ __forceinline__ double block_sum(double v, double *smem) {
 struct AdamArgs {
   float lr, b1, b2, omb1, omb2, wd, bc1, bc2, gscale;
   const float *gscale_ptr;
+  // When set, lr, bc1, bc2 are read from device memory (hyper[0..2]) instead
+  // of the values above: a captured CUDA graph replays with the step's own
+  // learning rate and bias corrections, written there before each launch.
+  const float *hyper;
 };
+
+// The arguments in effect inside a kernel (device scalars applied).
+__device__ __forceinline__ AdamArgs adam_live(const AdamArgs &a) {
+  AdamArgs e = a;
+  if (a.hyper) {
+    e.lr = __ldg(a.hyper);
+    e.bc1 = __ldg(a.hyper + 1);
+    e.bc2 = __ldg(a.hyper + 2);
+  }
+  return e;
+}
 
 __device__ __forceinline__ void adam_elem(float &p, float g, float &m, float &v,
                                           const AdamArgs &a, float gs) {
@@ -55,6 +70,7 @@ inline AdamArgs make_adam_args(float lr, float b1, float b2, float wd, int t, fl
   a.bc2 = 1.0f - powf(b2, (float)t);
   a.gscale = gscale;
   a.gscale_ptr = gscale_dev;
+  a.hyper = nullptr;
   return a;
 }
 

@@ -40,10 +40,13 @@ static cudaEvent_t get_event() {
   return e;
 }
 
-bool trace_on() { return g_on; }
+static thread_local bool g_suspended = false;   // while a CUDA graph is being captured
+
+bool trace_on() { return g_on && !g_suspended; }
+void trace_suspend(bool on) { g_suspended = on; }
 
 TraceScope::TraceScope(DeviceCtx *c, const char *name) : c_(c), name_(name) {
-  if (!g_on || !c) return;
+  if (!g_on || g_suspended || !c) return;
   a_ = get_event();
   cudaEventRecord(a_, c->stream);
 }

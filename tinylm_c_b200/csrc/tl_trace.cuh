@@ -4,6 +4,8 @@
 
 namespace tl {
 bool trace_on();
+// No kernel is timed while suspended (launches recorded into a CUDA graph).
+void trace_suspend(bool on);
 class TraceScope {
  public:
   TraceScope(DeviceCtx *c, const char *name);

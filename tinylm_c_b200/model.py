@@ -77,10 +77,14 @@ class Model:
             _iptr(tgt, "tgt"), _iptr(tgt_mtp, "tgt_mtp"), B,
             None if loss_out is None else ops._ptr(loss_out, "loss_out", 1)))
 
-    def step(self, P, G, M, V, tok, tgt, tgt_mtp, B, lr, t, max_norm=1.0, loss_out=None, norm_out=None):
+    def step(self, P, G, M, V, tok, tgt, tgt_mtp, B, lr, t, max_norm=1.0, loss_out=None, norm_out=None,
+             graph=False):
+        """One training step; graph=True replays it as a CUDA graph
+        (tl_model_graph_step; buffers must not move between calls)."""
         ops._prep(P)
         n = self.nparams
-        check(lib().tl_model_step(
+        fn = lib().tl_model_graph_step if graph else lib().tl_model_step
+        check(fn(
             self.h, ops._ptr(P, "P", n), ops._ptr(G, "G", n), ops._ptr(M, "M", n), ops._ptr(V, "V", n),
             _iptr(tok, "tok"), _iptr(tgt, "tgt"), _iptr(tgt_mtp, "tgt_mtp"), B, lr, int(t), max_norm,
             None if loss_out is None else ops._ptr(loss_out, "loss_out", 1),
