@@ -428,6 +428,10 @@ constexpr int PM = 2 * BM, PN = 2 * BN;                 // 256 x 256 per pair
 constexpr int RAW_STAGES = TL_PAIR_RAW_STAGES, LO_STAGES = TL_PAIR_LO_STAGES;
 constexpr int RAW_BYTES = TILE_A + TILE_B;              // 32 KB: A rows, then this CTA's B half
 constexpr int PAIR_SMEM_BYTES = (RAW_STAGES + LO_STAGES) * RAW_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+#ifndef TL_PAIR_CHUNK_KB
+#define TL_PAIR_CHUNK_KB 8
+#endif
+constexpr int PAIR_CHUNK_KB = TL_PAIR_CHUNK_KB;         // k-blocks per TMEM chunk before promotion
 constexpr int PAIR_TMEM_COLS = 2 * PN;                  // two 256-column accumulators
 constexpr int PAIR_SIGNALLERS = 2 * 8;                  // split/drain warps in the pair
 constexpr int PAIR_DRAIN_LAG = 2;                       // k-blocks split ahead of a forced drain
@@ -536,7 +540,7 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
   const int nk_all = (p.R + BK - 1) / BK;
   const int kb0 = blockIdx.z * p.kb_per_split;
   const int nk = max(0, min(nk_all - kb0, p.kb_per_split));
-  const int nchunks = (nk + CHUNK_KB - 1) / CHUNK_KB;
+  const int nchunks = (nk + PAIR_CHUNK_KB - 1) / PAIR_CHUNK_KB;
   float *const Cout = p.C + (size_t)blockIdx.z * p.split_stride;
   const uint32_t raw_base = smem_u32(raw_ring), lo_base = smem_u32(lo_ring);
   auto bar_full = [&](int s) { return smem_u32(&bars[s]); };
@@ -641,7 +645,7 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         }
         tc_commit_pair(bar_lempty(ls));
         tc_commit_pair(bar_rempty(rs));
-        if (++kin == CHUNK_KB || kb == nk - 1) {
+        if (++kin == PAIR_CHUNK_KB || kb == nk - 1) {
           tc_commit_pair(bar_accf(b));
           last_committed = chunk;
           chunk++;
@@ -676,7 +680,7 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     while (kb < nk || c < nchunks) {
       bool drain = false;
       if (c < nchunks) {
-        const int c_end = min((c + 1) * CHUNK_KB, nk);
+        const int c_end = min((c + 1) * PAIR_CHUNK_KB, nk);
         if (kb >= nk || kb >= c_end + PAIR_DRAIN_LAG) {
           drain = true;
         } else if (kb >= c_end) {
