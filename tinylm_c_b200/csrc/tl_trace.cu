@@ -4,8 +4,11 @@
 // when tracing is on, every kernel the library launches is bracketed by two
 // events on the stream it is launched on; tl_trace_get folds the finished pairs
 // into a per-name total and count.  Off by default; when off it costs one
-// branch per launch.
+// branch per launch.  With TL_NVTX=1 every launch is also an NVTX range of the
+// same name.
+#include <cstdlib>
 #include <cstring>
+#include <nvtx3/nvToolsExt.h>
 #include <string>
 #include <unordered_map>
 #include <vector>
@@ -42,16 +45,30 @@ static cudaEvent_t get_event() {
 
 static thread_local bool g_suspended = false;   // while a CUDA graph is being captured
 
+// NVTX ranges named after each launch, for profiler timelines (TL_NVTX=1).
+static bool nvtx_on() {
+  static const bool on = [] {
+    const char *e = getenv("TL_NVTX");
+    return e && *e && *e != '0';
+  }();
+  return on;
+}
+
 bool trace_on() { return g_on && !g_suspended; }
 void trace_suspend(bool on) { g_suspended = on; }
 
 TraceScope::TraceScope(DeviceCtx *c, const char *name) : c_(c), name_(name) {
+  if (nvtx_on()) {
+    nvtxRangePushA(name);
+    nvtx_ = true;
+  }
   if (!g_on || g_suspended || !c) return;
   a_ = get_event();
   cudaEventRecord(a_, c->stream);
 }
 
 TraceScope::~TraceScope() {
+  if (nvtx_) nvtxRangePop();
   if (!a_) return;
   cudaEvent_t b = get_event();
   cudaEventRecord(b, c_->stream);

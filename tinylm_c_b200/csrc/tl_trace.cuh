@@ -17,5 +17,6 @@ class TraceScope {
   DeviceCtx *c_ = nullptr;
   const char *name_ = nullptr;
   cudaEvent_t a_ = nullptr;
+  bool nvtx_ = false;
 };
 }  // namespace tl
