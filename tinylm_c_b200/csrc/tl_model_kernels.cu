@@ -242,6 +242,37 @@ __global__ void rope_kernel(float *__restrict__ buf, const float *__restrict__ c
   }
 }
 
+// The same, four rotation pairs (i..i+3 with i+half..i+half+3) per thread,
+// for half % 4 == 0.
+__global__ void rope4_kernel(float *__restrict__ buf, const float *__restrict__ cosT, const float *__restrict__ sinT,
+                             int rows, int nh, int hd, int T, int back) {
+  const int half = hd / 2, q4 = half / 4;
+  const size_t total = (size_t)rows * nh * q4;
+  for (size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += (size_t)gridDim.x * blockDim.x) {
+    const int i = (int)(idx % q4) * 4;
+    const size_t rh = idx / q4;
+    const int t = (int)((rh / nh) % T);
+    float *v = buf + rh * hd;
+    const float4 c = *reinterpret_cast<const float4 *>(cosT + (size_t)t * half + i);
+    const float4 sn = *reinterpret_cast<const float4 *>(sinT + (size_t)t * half + i);
+    const float4 a = *reinterpret_cast<const float4 *>(v + i), b = *reinterpret_cast<const float4 *>(v + i + half);
+    float4 oa, ob;
+    if (!back) {
+      oa.x = a.x * c.x - b.x * sn.x; ob.x = b.x * c.x + a.x * sn.x;
+      oa.y = a.y * c.y - b.y * sn.y; ob.y = b.y * c.y + a.y * sn.y;
+      oa.z = a.z * c.z - b.z * sn.z; ob.z = b.z * c.z + a.z * sn.z;
+      oa.w = a.w * c.w - b.w * sn.w; ob.w = b.w * c.w + a.w * sn.w;
+    } else {
+      oa.x = a.x * c.x + b.x * sn.x; ob.x = -a.x * sn.x + b.x * c.x;
+      oa.y = a.y * c.y + b.y * sn.y; ob.y = -a.y * sn.y + b.y * c.y;
+      oa.z = a.z * c.z + b.z * sn.z; ob.z = -a.z * sn.z + b.z * c.z;
+      oa.w = a.w * c.w + b.w * sn.w; ob.w = -a.w * sn.w + b.w * c.w;
+    }
+    *reinterpret_cast<float4 *>(v + i) = oa;
+    *reinterpret_cast<float4 *>(v + i + half) = ob;
+  }
+}
+
 // --------------------------------------------------------------- elementwise
 // The element-wise kernels below run a float4 body over the first n & ~3
 // elements (all buffers are 256-byte aligned arena slices) and a scalar tail.
@@ -552,7 +583,12 @@ __global__ void attn_rowdot_kernel(const float *__restrict__ dout, const float *
   const int bh = warp / T, t = warp % T, b = bh / H, h = bh % H;
   const size_t o = ((size_t)b * T + t) * H * hd + (size_t)h * hd;
   float acc = 0.0f;
-  for (int d = lane; d < hd; d += 32) acc += dout[o + d] * out[o + d];
+  // float2 per lane (hd % 4 == 0 and rows start at multiples of hd floats)
+  for (int d = 2 * lane; d < hd; d += 64) {
+    const float2 a = *reinterpret_cast<const float2 *>(dout + o + d);
+    const float2 b = *reinterpret_cast<const float2 *>(out + o + d);
+    acc += a.x * b.x + a.y * b.y;
+  }
   acc = warp_sum_f(acc);
   if (lane == 0) Drow[warp] = acc;
 }
@@ -741,7 +777,15 @@ int k_rmsnorm_bwd(DeviceCtx *c, const float *x, const float *g, const float *rin
 }
 int k_rope(DeviceCtx *c, float *buf, const float *cosT, const float *sinT, int rows, int nh, int hd, int T, int back) {
   TraceScope ts(c, "k_rope");
-  const size_t n = (size_t)rows * nh * (hd / 2);
+  const int half = hd / 2;
+  if (half % 4 == 0 && ((reinterpret_cast<uintptr_t>(buf) | reinterpret_cast<uintptr_t>(cosT) |
+                         reinterpret_cast<uintptr_t>(sinT)) & 15) == 0) {
+    const size_t n4 = (size_t)rows * nh * (half / 4);
+    mk::rope4_kernel<<<grid_for(n4, 256, 16, c->num_sms), 256, 0, c->stream>>>(buf, cosT, sinT, rows, nh, hd, T, back);
+    MK_LAUNCH_CHECK();
+    return TL_OK;
+  }
+  const size_t n = (size_t)rows * nh * half;
   mk::rope_kernel<<<grid_for(n, 256, 16, c->num_sms), 256, 0, c->stream>>>(buf, cosT, sinT, rows, nh, hd, T, back);
   MK_LAUNCH_CHECK();
   return TL_OK;
