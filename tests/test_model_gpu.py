@@ -49,7 +49,7 @@ def test_ten_steps_match_reference(cuda, golden, name, preset, micro):
 
 
 @pytest.mark.skipif(not oracle.has_ref(), reason="reference leg not built")
-@pytest.mark.parametrize("preset,n_mtp,B", [("nano", 0, 2), ("m1", 2, 2)])
+@pytest.mark.parametrize("preset,n_mtp,B", [("nano", 0, 2), ("m1", 2, 2), ("m16", 0, 2)])
 def test_gradient_matches_reference_leg(cuda, preset, n_mtp, B):
     """One forward/backward from the reference's own parameters and tokens:
     every parameter tensor's gradient within 1e-4 relative (L2)."""
@@ -94,6 +94,36 @@ def test_gradient_matches_reference_leg(cuda, preset, n_mtp, B):
         assert rel <= 1e-4, (name, rel)
         off += sz
     assert off == n
+
+
+def test_tensor_core_attention_matches_cuda_cores(cuda):
+    """Head dim 64, T=256 (m16): the tcgen05 attention forward against the
+    CUDA-core one inside a whole forward/backward -- same loss to 1e-6 and
+    gradients to 1e-5 relative."""
+    c = model.cfg8("m16", 0)
+    P = model.init_params(c, 5).to(cuda)
+    n = P.numel()
+    g = torch.Generator(device=cuda).manual_seed(8)
+    B = 4
+    tok = torch.randint(0, 2048, (B * 256,), generator=g, device=cuda, dtype=torch.int32)
+    tgt = torch.randint(0, 2048, (B * 256,), generator=g, device=cuda, dtype=torch.int32)
+    m = model.Model(c, B, 0)
+    out = []
+    try:
+        for eng in (1, 2):
+            ops.set_attn_engine(eng)
+            G = torch.zeros(n, device=cuda)
+            loss = torch.zeros(1, device=cuda)
+            m.forward_backward(P, G, tok, tgt, None, B, loss)
+            torch.cuda.synchronize()
+            _lib.check(_lib.lib().tl_device_status())
+            out.append((loss.item(), G.clone()))
+    finally:
+        ops.set_attn_engine(0)
+        m.close()
+    assert out[0][0] == pytest.approx(out[1][0], abs=1e-6)
+    rel = ((out[0][1] - out[1][1]).norm() / out[0][1].norm()).item()
+    assert rel < 1e-5, rel
 
 
 def test_micro_batching_changes_only_rounding(cuda):

@@ -75,6 +75,7 @@ SIGNATURES = {
                                            _c_int, _c_void_p]),
     "tl_model_step": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
                                _c_void_p, _c_int, _c_float, _c_int, _c_float, _c_void_p, _c_void_p]),
+    "tl_set_attn_engine": (_c_int, [_c_int]),
     "tl_model_graph_step": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
                                      _c_void_p, _c_int, _c_float, _c_int, _c_float, _c_void_p, _c_void_p]),
     "tl_model_step_zero1": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,

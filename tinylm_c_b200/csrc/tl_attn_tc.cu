@@ -1,0 +1,406 @@
+// tl_attn_tc.cu -- causal GQA attention forward on the tensor cores (sm_100a).
+//
+// The reference's attention (tinylm.c:698-783) for T = 256 and head_dim 64:
+// one CTA pair (cluster of 2, tcgen05 cta_group::2) per (sequence, query
+// head).  CTA r holds query rows 128r..128r+127 and key rows 128r..128r+127.
+//
+//   S = Q K^T      M = 256 queries, N = 256 keys, K = 64: 2 k-blocks x 4 x 3
+//                  tf32 MMAs (3xTF32: lo*hi + hi*lo + hi*hi) into TMEM
+//                  columns 0..255; Q and K staged by TMA (K-major, 128-byte
+//                  swizzle), their lo parts written by the split warps.
+//   softmax        exact, two passes over S in TMEM: row max over the keys
+//                  <= the query (the two column halves exchange partial maxima
+//                  through shared memory), then p = exp(scale*s - max) and the
+//                  row sum.  P goes to shared memory in 32-key blocks (raw and
+//                  lo, the A operand of the next product).
+//   O = P V        M = 256, N = 64, K = 256 keys in 8 blocks through a 2-slot
+//                  ring (P block + V block, V as the MN-major B operand: each
+//                  CTA holds 32 of the 64 value columns), accumulated in TMEM
+//                  columns 256..319.
+//   epilogue       out = O / rowsum, lse = max + log(rowsum) (what the backward
+//                  kernels read).
+//
+// Roles (320 threads): warp 0 TMA producer; warp 1 TMEM owner and, in the
+// leader CTA, MMA issuer; warps 2-9 split Q/K, then run the softmax (warp w:
+// TMEM lanes 32*(w%4).., h = (w-2)/4: row maximum over keys [128h, 128h+128),
+// then P for the key blocks kb with kb % 2 == h and the lo parts of V for the
+// others), then the epilogue for value columns [32h, 32h + 32).  Every wait is bounded; on
+// expiry the pair records an error code (tl_device_status) and winds down.
+// No TMA multicast: the leader's commits use tcgen05.commit multicast, which
+// moves no data.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include "tl_common.cuh"
+#include "tl_tc_ptx.cuh"
+#include "tl_trace.cuh"
+
+namespace tl {
+namespace atc {
+using namespace tc;
+
+constexpr int T = 256, HD = 64, QR = 128;       // sequence, head dim, query rows per CTA
+constexpr int KBLK = 32;                        // floats per 128-byte swizzle row
+constexpr int NKB = T / KBLK;                   // 8 key blocks
+constexpr int TILE = QR * KBLK * 4;             // 16 KB: 128 rows x 32 floats
+constexpr int OFF_QR = 0, OFF_QL = 2 * TILE, OFF_KR = 4 * TILE, OFF_KL = 6 * TILE;
+constexpr int STAGE0 = 8 * TILE;                // Q, K (raw, lo; 2 k-blocks each): 128 KB
+constexpr int VT = 32 * 32 * 4;                 // V box: 32 keys x 32 value columns, 4 KB
+constexpr int OFF_PR = 0, OFF_PL = TILE, OFF_VR = 2 * TILE, OFF_VL = 2 * TILE + VT;
+constexpr int STAGE_BYTES = 2 * TILE + 2 * VT;  // 40 KB
+constexpr int NSTAGE = 2;
+constexpr int NBARS = 16;
+constexpr int SMEM_BYTES = STAGE0 + NSTAGE * STAGE_BYTES + 1024 /*align*/ + NBARS * 8 + 64 + 4 * QR * 4;
+constexpr int NUM_THREADS = 320;
+constexpr int TMEM_COLS = 512;                  // S: columns 0..255, O: 256..319
+constexpr int O_COL = 256;
+constexpr int SIGNALLERS = 16;                  // split/softmax warps of the pair
+static_assert(SMEM_BYTES <= 232448, "attention kernel exceeds the opt-in shared memory");
+
+__host__ __device__ constexpr uint32_t idesc_m256(int n, bool a_mn, bool b_mn) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) |
+         ((uint32_t)(n >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
+}
+
+struct Args {
+  float *out, *lse;
+  int H, KV, D;
+  float scale;
+  int *err;
+};
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
+        "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+        "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
+attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                   const __grid_constant__ CUtensorMap tmV, Args a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + STAGE0 + NSTAGE * STAGE_BYTES);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + NBARS);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+  float *red = reinterpret_cast<float *>(tmem_slot + 16);   // [2 max/sum][2 halves][128 rows]
+  const uint32_t base = smem_u32(smem);
+  auto stage = [&](int s) { return base + STAGE0 + s * STAGE_BYTES; };
+  // bars: 0 qk_full, 1 qk_ready, 2 s_full, 3-4 st_full, 5-6 st_ready, 7-8 st_empty, 9 o_full, 10 xch
+  auto bar = [&](int i) { return smem_u32(&bars[i]); };
+  constexpr int QK_FULL = 0, QK_READY = 1, S_FULL = 2, ST_FULL = 3, ST_READY = 5, ST_EMPTY = 7, O_FULL = 9,
+                XCH = 10;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int bh = blockIdx.x >> 1, b = bh / a.H, h = bh % a.H, kvh = h / (a.H / a.KV);
+  const uint32_t peer_flag = cluster_map(smem_u32((const void *)abort_flag), rank ^ 1u);
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar(QK_FULL), 1);
+    mbar_init(bar(QK_READY), SIGNALLERS);
+    mbar_init(bar(S_FULL), 1);
+    for (int s = 0; s < NSTAGE; s++) {
+      mbar_init(bar(ST_FULL + s), 1);
+      mbar_init(bar(ST_READY + s), SIGNALLERS);
+      mbar_init(bar(ST_EMPTY + s), 1);
+    }
+    mbar_init(bar(O_FULL), 1);
+    mbar_init(bar(XCH), 8);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const int row0 = b * T + QR * (int)rank;
+      mbar_arrive_expect_tx(bar(QK_FULL), 4 * TILE);
+      for (int kb = 0; kb < 2; kb++) {
+        tma_load_2d(base + OFF_QR + kb * TILE, &tmQ, bar(QK_FULL), h * HD + KBLK * kb, row0);
+        tma_load_2d(base + OFF_KR + kb * TILE, &tmK, bar(QK_FULL), kvh * HD + KBLK * kb, row0);
+      }
+      int issued = 0;
+      for (int kb = 0; kb < NKB; kb++) {
+        const int s = kb & 1, u = kb >> 1;
+        if (u > 0 && !mbar_wait_pair(bar(ST_EMPTY + s), (u - 1) & 1, abort_flag, peer_flag, a.err, 31)) break;
+        issued = kb + 1;
+        mbar_arrive_expect_tx(bar(ST_FULL + s), VT);
+        tma_load_2d(stage(s) + OFF_VR, &tmV, bar(ST_FULL + s), kvh * HD + 32 * (int)rank, b * T + KBLK * kb);
+      }
+      // No copy may still be landing when the CTA exits.
+      const long long t0 = clock64();
+      while (!mbar_try_wait(bar(QK_FULL), 0)) {
+        if (clock64() - t0 > WAIT_LIMIT_CYCLES) { atomicExch(a.err, 36); break; }
+      }
+      for (int kb = issued > NSTAGE ? issued - NSTAGE : 0; kb < issued; kb++) {
+        const long long t1 = clock64();
+        while (!mbar_try_wait(bar(ST_FULL + (kb & 1)), (kb >> 1) & 1)) {
+          if (clock64() - t1 > WAIT_LIMIT_CYCLES) { atomicExch(a.err, 36); break; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------- MMA issuer (leader CTA only)
+    if (lane == 0 && rank == 0) {
+      bool issued_any = false;
+      if (mbar_wait_pair(bar(QK_READY), 0, abort_flag, peer_flag, a.err, 32)) {
+        tc_fence_after();
+        constexpr uint32_t idesc_s = idesc_m256(256, false, false);
+#pragma unroll
+        for (int kb = 0; kb < 2; kb++) {
+#pragma unroll
+          for (int kk = 0; kk < KBLK / 8; kk++) {
+            const uint32_t off = kb * TILE + kk * 32;
+            const uint64_t q_hi = smem_desc(base + OFF_QR + off, 16, 1024, LAYOUT_SW128);
+            const uint64_t q_lo = smem_desc(base + OFF_QL + off, 16, 1024, LAYOUT_SW128);
+            const uint64_t k_hi = smem_desc(base + OFF_KR + off, 16, 1024, LAYOUT_SW128);
+            const uint64_t k_lo = smem_desc(base + OFF_KL + off, 16, 1024, LAYOUT_SW128);
+            tc_mma_pair(tmem, q_lo, k_hi, idesc_s, (kb > 0 || kk > 0) ? 1u : 0u);
+            tc_mma_pair(tmem, q_hi, k_lo, idesc_s, 1);
+            tc_mma_pair(tmem, q_hi, k_hi, idesc_s, 1);
+          }
+        }
+        issued_any = true;
+        tc_commit_pair(bar(S_FULL));
+        constexpr uint32_t idesc_o = idesc_m256(HD, false, true);
+        for (int kb = 0; kb < NKB; kb++) {
+          const int s = kb & 1;
+          if (!mbar_wait_pair(bar(ST_READY + s), (kb >> 1) & 1, abort_flag, peer_flag, a.err, 33)) break;
+          tc_fence_after();
+          const uint32_t st = stage(s);
+#pragma unroll
+          for (int kk = 0; kk < KBLK / 8; kk++) {
+            const uint64_t p_hi = smem_desc(st + OFF_PR + kk * 32, 16, 1024, LAYOUT_SW128);
+            const uint64_t p_lo = smem_desc(st + OFF_PL + kk * 32, 16, 1024, LAYOUT_SW128);
+            const uint64_t v_hi = smem_desc(st + OFF_VR + kk * 1024, 4096, 512, LAYOUT_SW128_BASE32B);
+            const uint64_t v_lo = smem_desc(st + OFF_VL + kk * 1024, 4096, 512, LAYOUT_SW128_BASE32B);
+            tc_mma_pair(tmem + O_COL, p_lo, v_hi, idesc_o, (kb > 0 || kk > 0) ? 1u : 0u);
+            tc_mma_pair(tmem + O_COL, p_hi, v_lo, idesc_o, 1);
+            tc_mma_pair(tmem + O_COL, p_hi, v_hi, idesc_o, 1);
+          }
+          tc_commit_pair(bar(ST_EMPTY + s));
+        }
+      }
+      // O complete (or, on the abort path, every issued MMA finished) before
+      // TMEM can be released.
+      tc_commit_pair(bar(O_FULL));
+      (void)issued_any;
+      const long long t0 = clock64();
+      while (!mbar_try_wait(bar(O_FULL), 0)) {
+        if (clock64() - t0 > WAIT_LIMIT_CYCLES) { pair_abort(abort_flag, peer_flag, a.err, 34); break; }
+      }
+    }
+  } else {
+    // --------------------------- split, softmax and epilogue (warps 2..9)
+    const int t = threadIdx.x - 64;             // 0..255
+    const int q4 = warp & 3, hh = (warp - 2) >> 2;
+    const int r = q4 * 32 + lane;                // this thread's query row in the CTA
+    const int qpos = QR * (int)rank + r;         // its position in the sequence
+    const int tl = q4 * 32 + lane;               // 0..127 within the half
+    const uint32_t lane_addr = (uint32_t)(q4 * 32) << 16;
+    bool ok = true;
+    // Q, K lo parts
+    {
+      const bool landed = mbar_wait_pair(bar(QK_FULL), 0, abort_flag, peer_flag, a.err, 35);
+      ok = __all_sync(0xffffffffu, landed);
+      if (ok) {
+#pragma unroll 4
+        for (int e = 0; e < 16; e++) {
+          const int idx = e * 256 + t;          // 0..4095: Q then K, 2048 float4 each
+          const int src = (idx < 2048 ? OFF_QR : OFF_KR) + (idx & 2047) * 16;
+          const int dst = (idx < 2048 ? OFF_QL : OFF_KL) + (idx & 2047) * 16;
+          const float4 x = *reinterpret_cast<const float4 *>(smem + src);
+          float4 lo;
+          lo.x = x.x - tf32_trunc(x.x); lo.y = x.y - tf32_trunc(x.y);
+          lo.z = x.z - tf32_trunc(x.z); lo.w = x.w - tf32_trunc(x.w);
+          *reinterpret_cast<float4 *>(smem + dst) = lo;
+        }
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote(cluster_map(bar(QK_READY), 0));
+      }
+    }
+    float m = -1e30f, lsum = 0.0f;
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait_pair(bar(S_FULL), 0, abort_flag, peer_flag, a.err, 37));
+    if (ok) {
+      // pass 1: partial row max over this half's keys <= qpos
+      tc_fence_after();
+      float mx = -1e30f;
+#pragma unroll 1
+      for (int c = 0; c < 4; c++) {
+        uint32_t v[32];
+        const int j0 = hh * 128 + c * 32;
+        tmem_ld32(tmem + lane_addr + j0, v);
+#pragma unroll
+        for (int e = 0; e < 32; e++)
+          if (j0 + e <= qpos) mx = fmaxf(mx, __uint_as_float(v[e]) * a.scale);
+      }
+      red[hh * QR + r] = mx;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(XCH));
+      ok = __all_sync(0xffffffffu, mbar_wait_pair(bar(XCH), 0, abort_flag, peer_flag, a.err, 38));
+      if (ok) m = fmaxf(red[r], red[QR + r]);
+    }
+    // pass 2: key blocks in order; half h writes P for the blocks kb with
+    // kb % 2 == h and the lo parts of V for the others, so both halves
+    // produce P blocks at the same time.
+#pragma unroll 1
+    for (int kb = 0; kb < NKB && ok; kb++) {
+      const int s = kb & 1;
+      const uint32_t st = stage(s);
+      if ((kb & 1) == hh) {
+        bool w = true;
+        if (kb >= 2) w = mbar_wait_pair(bar(ST_EMPTY + s), ((kb >> 1) - 1) & 1, abort_flag, peer_flag, a.err, 39);
+        if (!(ok = __all_sync(0xffffffffu, w))) break;
+        tc_fence_after();
+        uint32_t v[32];
+        tmem_ld32(tmem + lane_addr + kb * 32, v);
+        float pr[32];
+#pragma unroll
+        for (int e = 0; e < 32; e++) {
+          const int key = kb * 32 + e;
+          pr[e] = key <= qpos ? expf(__uint_as_float(v[e]) * a.scale - m) : 0.0f;
+          lsum += pr[e];
+        }
+        // row r of the 128 x 32 K-major tile: logical chunk c at c ^ (r % 8)
+#pragma unroll
+        for (int c = 0; c < 8; c++) {
+          const uint32_t off = (uint32_t)r * 128 + (uint32_t)((c ^ (r & 7)) * 16);
+          const float4 x = make_float4(pr[4 * c], pr[4 * c + 1], pr[4 * c + 2], pr[4 * c + 3]);
+          float4 lo;
+          lo.x = x.x - tf32_trunc(x.x); lo.y = x.y - tf32_trunc(x.y);
+          lo.z = x.z - tf32_trunc(x.z); lo.w = x.w - tf32_trunc(x.w);
+          *reinterpret_cast<float4 *>(smem + (st - base) + OFF_PR + off) = x;
+          *reinterpret_cast<float4 *>(smem + (st - base) + OFF_PL + off) = lo;
+        }
+      } else {
+        const bool w = mbar_wait_pair(bar(ST_FULL + s), (kb >> 1) & 1, abort_flag, peer_flag, a.err, 40);
+        if (!(ok = __all_sync(0xffffffffu, w))) break;
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+          const int off = (e * 128 + tl) * 16;
+          const float4 x = *reinterpret_cast<const float4 *>(smem + (st - base) + OFF_VR + off);
+          float4 lo;
+          lo.x = x.x - tf32_trunc(x.x); lo.y = x.y - tf32_trunc(x.y);
+          lo.z = x.z - tf32_trunc(x.z); lo.w = x.w - tf32_trunc(x.w);
+          *reinterpret_cast<float4 *>(smem + (st - base) + OFF_VL + off) = lo;
+        }
+      }
+      tc_fence_before();
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(cluster_map(bar(ST_READY + s), 0));
+    }
+    if (ok) {
+      // row sum: both halves, added in half order
+      red[2 * QR + hh * QR + r] = lsum;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(XCH));
+      ok = __all_sync(0xffffffffu, mbar_wait_pair(bar(XCH), 1, abort_flag, peer_flag, a.err, 41));
+    }
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait_pair(bar(O_FULL), 0, abort_flag, peer_flag, a.err, 42));
+    if (ok && !*abort_flag) {
+      const float l = red[2 * QR + r] + red[3 * QR + r];
+      const float inv = 1.0f / l;
+      tc_fence_after();
+      uint32_t v[32];
+      tmem_ld32(tmem + lane_addr + O_COL + hh * 32, v);
+      const int b_row = b * T + qpos;
+      float *dst = a.out + (size_t)b_row * a.D + h * HD + hh * 32;
+#pragma unroll
+      for (int e = 0; e < 32; e += 4)
+        *reinterpret_cast<float4 *>(dst + e) =
+            make_float4(__uint_as_float(v[e]) * inv, __uint_as_float(v[e + 1]) * inv,
+                        __uint_as_float(v[e + 2]) * inv, __uint_as_float(v[e + 3]) * inv);
+      if (hh == 0) a.lse[(size_t)bh * T + qpos] = m + logf(l);
+    }
+  }
+  tc_fence_before();
+  cluster_sync_all();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+  }
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 g_enc = nullptr;
+
+static int map2d(CUtensorMap *m, const float *p, uint64_t inner, uint64_t outer, uint32_t bx, uint32_t by,
+                 CUtensorMapSwizzle sw) {
+  if (!g_enc) {
+    void *fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !fn)
+      return set_error(TL_ECUDA, "cuTensorMapEncodeTiled not available from the driver");
+    g_enc = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  }
+  cuuint64_t dims[2] = {inner, outer}, strides[1] = {inner * 4};
+  cuuint32_t box[2] = {bx, by}, es[2] = {1, 1};
+  CUresult r = g_enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(p), dims, strides, box, es,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(TL_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return TL_OK;
+}
+
+}  // namespace atc
+
+// True when the tensor-core forward takes this shape.
+bool attn_fwd_tc_supported(const float *q, const float *k, const float *v, int T, int hd, int H, int KV) {
+  const uintptr_t al = reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v);
+  return T == atc::T && hd == atc::HD && (al & 15) == 0 && KV > 0 && H % KV == 0;
+}
+
+int attn_fwd_tc(DeviceCtx *c, const float *q, const float *k, const float *v, float *out, float *lse, int B, int T,
+                int H, int KV, int hd) {
+  (void)T;
+  (void)hd;
+  static bool attr[kMaxDevices] = {};
+  if (!attr[c->device]) {
+    TL_TRY_CUDA(cudaFuncSetAttribute(atc::attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     atc::SMEM_BYTES));
+    attr[c->device] = true;
+  }
+  const int D = H * atc::HD, KD = KV * atc::HD;
+  const uint64_t rows = (uint64_t)B * atc::T;
+  CUtensorMap mq, mk, mv;
+  int rc;
+  if ((rc = atc::map2d(&mq, q, D, rows, 32, atc::QR, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
+  if ((rc = atc::map2d(&mk, k, KD, rows, 32, atc::QR, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
+  if ((rc = atc::map2d(&mv, v, KD, rows, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))) return rc;
+  atc::Args a;
+  a.out = out; a.lse = lse; a.H = H; a.KV = KV; a.D = D;
+  a.scale = 1.0f / sqrtf((float)atc::HD);
+  a.err = c->err_flag;
+  TraceScope ts(c, "k_attn_fwd_tc");
+  atc::attn_fwd_tc_kernel<<<2 * B * H, atc::NUM_THREADS, atc::SMEM_BYTES, c->stream>>>(mq, mk, mv, a);
+  TL_TRY_CUDA(cudaGetLastError());
+  return TL_OK;
+}
+
+int attn_tc_prepare(DeviceCtx *c) {
+  TL_TRY_CUDA(cudaFuncSetAttribute(atc::attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   atc::SMEM_BYTES));
+  (void)c;
+  return TL_OK;
+}
+
+}  // namespace tl

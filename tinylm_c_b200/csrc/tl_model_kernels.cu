@@ -725,9 +725,16 @@ size_t attn_smem_fwd() { return sizeof(float) * 4 * mk::ATILE; }
 size_t attn_smem_dq() { return sizeof(float) * 2 * mk::ATILE; }
 size_t attn_smem_dkdv() { return sizeof(float) * (6 * mk::ATILE + 2 * mk::AT); }
 
+int attn_tc_prepare(DeviceCtx *c);
+
 int mk_setup(int device) {
   static bool done[kMaxDevices] = {};
   if (done[device]) return TL_OK;
+  {
+    DeviceCtx *c = ctx();
+    int rc = c ? attn_tc_prepare(c) : TL_OK;
+    if (rc) return rc;
+  }
   TL_TRY_CUDA(cudaFuncSetAttribute(mk::attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    (int)attn_smem_fwd()));
   TL_TRY_CUDA(cudaFuncSetAttribute(mk::attn_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -838,8 +845,16 @@ int k_loss_final(DeviceCtx *c, const double *acc, double denom, float *out) {
   MK_LAUNCH_CHECK();
   return TL_OK;
 }
+bool attn_fwd_tc_supported(const float *q, const float *k, const float *v, int T, int hd, int H, int KV);
+int attn_fwd_tc(DeviceCtx *c, const float *q, const float *k, const float *v, float *out, float *lse, int B, int T,
+                int H, int KV, int hd);
+static thread_local int g_attn_engine = 0;   // 0 automatic, 1 CUDA cores, 2 tensor cores
+
 int k_attn_fwd(DeviceCtx *c, const float *q, const float *k, const float *v, float *out, float *lse, int B, int T,
                int H, int KV, int hd) {
+  if (g_attn_engine != 1 && attn_fwd_tc_supported(q, k, v, T, hd, H, KV))
+    return attn_fwd_tc(c, q, k, v, out, lse, B, T, H, KV, hd);
+  if (g_attn_engine == 2) return set_error(TL_EINVAL, "tensor-core attention needs T = 256 and head_dim 64");
   TraceScope ts(c, "k_attn_fwd");
   const float scale = 1.0f / sqrtf((float)hd);
   mk::attn_fwd_kernel<<<B * H * (T / mk::AT), 256, attn_smem_fwd(), c->stream>>>(q, k, v, out, lse, T, H, KV, hd,
@@ -864,3 +879,9 @@ int k_attn_bwd(DeviceCtx *c, const float *q, const float *k, const float *v, con
 }
 
 }  // namespace tl
+
+TL_API int tl_set_attn_engine(int engine) {
+  if (engine < 0 || engine > 2) return tl::set_error(TL_EINVAL, "engine must be 0, 1 or 2");
+  tl::g_attn_engine = engine;
+  return TL_OK;
+}

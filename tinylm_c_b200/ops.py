@@ -93,6 +93,11 @@ def set_gemm_engine(engine):
     check(lib().tl_set_gemm_engine(int(engine)))
 
 
+def set_attn_engine(engine):
+    """Attention forward: 0 automatic, 1 CUDA cores, 2 tensor cores (T=256, hd=64)."""
+    check(lib().tl_set_attn_engine(int(engine)))
+
+
 def last_gemm_engine():
     return lib().tl_last_gemm_engine()
 
