@@ -91,6 +91,16 @@ int tl_matmul_bt(float *dX, const float *dY, const float *W, int M, int K, int N
 /* dW[K,N] += X[M,K]^T @ dY[M,N]  (accumulate, beta = 1).  tinylm.c:510-537 (mm_atb). */
 int tl_matmul_at(float *dW, const float *X, const float *dY, int M, int K, int N);
 
+/* dX[M,K] = sum over t < nprod of dY[t][M,N[t]] @ W[t][K,N[t]]^T (overwrite),
+ * 1 <= nprod <= 3; dY and W are host arrays of device pointers.  Where the
+ * CTA-pair tensor-core kernel takes every product this is one launch whose
+ * reduction runs through the products in turn; otherwise one mm_bt per
+ * product.  Replaces the reference's memset followed by consecutive mm_bt
+ * calls into one gradient: tinylm.c:1135-1138 (dq, dk, dv into the attention
+ * norm's gradient) and 1113-1115 (the two FFN input projections). */
+int tl_matmul_bt_sum(float *dX, int nprod, const float *const *dY, const float *const *W, const int *N, int M,
+                     int K);
+
 /* GEMM engine selection, for tests and benchmarks: 0 = automatic (tensor-core
  * 3xTF32 where the shape allows, else CUDA-core fp32), 1 = CUDA-core fp32 only,
  * 2 = tensor-core 3xTF32, one CTA per 128 x 128 tile, 3 = tensor-core 3xTF32,

@@ -139,6 +139,43 @@ def test_tensor_core_engine_forced(cuda, tc_engine, M, K, N):
     assert gemm_rel(dW.cpu().numpy(), dW64) <= GEMM_REL_TOL
 
 
+@pytest.mark.parametrize("eng", [0, 1, 3])
+@pytest.mark.parametrize("M,K,Ns", [(512, 384, (96, 40, 72)), (300, 260, (256, 512)), (256, 256, (2048, 1024, 1024)),
+                                    (100, 64, (64, 64, 64)), (384, 256, (64, 0, 32)), (257, 1024, (2816,))])
+def test_mm_bt_sum(cuda, eng, M, K, Ns):
+    """dX = sum_t dY_t @ W_t^T as one pair launch walking the products'
+    k-blocks (engine 3, and auto where the pair kernel takes the shape), or
+    consecutive mm_bt: reductions that end inside a k-block (N=40, 72), a
+    product with no columns, partial tiles and split-K (few output tiles,
+    long reduction)."""
+    rng = np.random.default_rng(M + K + sum(Ns))
+    dYs = [rng.standard_normal(M * n, dtype=np.float32) for n in Ns]
+    Ws = [rng.standard_normal(K * n, dtype=np.float32) * np.float32(0.02) for n in Ns]
+    dX = torch.full((M * K,), float("nan"), device=cuda)
+    ops.set_gemm_engine(eng)
+    try:
+        ops.mm_bt_sum(dX, [dev(a, cuda) for a in dYs], [dev(w, cuda) for w in Ws], list(Ns), M, K)
+        last = ops.last_gemm_engine()
+        torch.cuda.synchronize()
+        device_ok()
+    finally:
+        ops.set_gemm_engine(0)
+    if eng == 3 or (eng == 0 and M > 128 and K > 128):
+        assert last == 3
+    want = np.zeros((M, K))
+    for a, w, n in zip(dYs, Ws, Ns):
+        want += a.astype(np.float64).reshape(M, n) @ w.astype(np.float64).reshape(K, n).T
+    assert gemm_rel(dX.cpu().numpy(), want.ravel()) <= GEMM_REL_TOL
+
+
+def test_mm_bt_sum_rejects_bad_args(cuda):
+    z = torch.zeros(64, device=cuda)
+    with pytest.raises(TLError):
+        ops.mm_bt_sum(z, [z] * 4, [z] * 4, [4] * 4, 4, 4)   # at most three products
+    with pytest.raises(TLError):
+        ops.mm_bt_sum(z, [z], [z], [-1], 4, 4)
+
+
 @pytest.mark.parametrize("tc_engine", list(TC_ENGINES))
 def test_tensor_core_engine_rejects_unaligned(cuda, tc_engine):
     ops.set_gemm_engine(TC_ENGINES[tc_engine])

@@ -41,6 +41,7 @@ SIGNATURES = {
     "tl_matmul": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_int, _c_int, _c_int]),
     "tl_matmul_bt": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_int, _c_int, _c_int]),
     "tl_matmul_at": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_int, _c_int, _c_int]),
+    "tl_matmul_bt_sum": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_void_p, _c_void_p, _c_int, _c_int]),
     "tl_set_gemm_engine": (_c_int, [_c_int]),
     "tl_last_gemm_engine": (_c_int, []),
     "tl_grad_norm": (_c_int, [_c_void_p, _c_size, _c_void_p]),

@@ -59,6 +59,23 @@ int tl::gemm_run_add(DeviceCtx *c, GemmOp op, float *C, const float *A, const fl
   return gemm_simt(c, op, C, A, B, M, K, N, add);
 }
 
+int tl::gemm_run_nt_sum(DeviceCtx *c, float *C, int nprod, const float *const *A, const float *const *B,
+                        const int *N, int M, int K) {
+  bool fused = nprod >= 1 && nprod <= 3 && M > 0 && K > 0 && (g_engine_pref == 0 || g_engine_pref == 3);
+  for (int t = 0; fused && t < nprod; t++)
+    fused = N[t] > 0 && gemm_tc_supported(GemmOp::NT, C, A[t], B[t], M, K, N[t]) &&
+            (g_engine_pref == 3 || gemm_tc_prefer_pair(M, K, N[t]));
+  if (fused) {
+    g_engine_last = 3;
+    return gemm_tc_nt_sum(c, C, nprod, A, B, N, M, K);
+  }
+  for (int t = 0; t < nprod; t++) {
+    const int rc = gemm_run_add(c, GemmOp::NT, C, A[t], B[t], M, K, N[t], t == 0 ? nullptr : C);
+    if (rc) return rc;
+  }
+  return TL_OK;
+}
+
 using namespace tl;
 
 TL_API int tl_matmul(float *Y, const float *X, const float *W, int M, int K, int N) {
@@ -69,6 +86,34 @@ TL_API int tl_matmul_bt(float *dX, const float *dY, const float *W, int M, int K
 }
 TL_API int tl_matmul_at(float *dW, const float *X, const float *dY, int M, int K, int N) {
   return gemm_entry(GemmOp::TN, dW, X, dY, M, K, N, "dW,X,dY");
+}
+TL_API int tl_matmul_bt_sum(float *dX, int nprod, const float *const *dY, const float *const *W, const int *N, int M,
+                            int K) {
+  TL_REQUIRE_CTX(c);
+  if (nprod < 1 || nprod > 3) return set_error(TL_EINVAL, "nprod must be 1, 2 or 3, not %d", nprod);
+  if (!dY || !W || !N) return set_error(TL_EINVAL, "null operand array");
+  if (M < 0 || K < 0) return set_error(TL_EINVAL, "negative GEMM dimension (M=%d K=%d)", M, K);
+  for (int t = 0; t < nprod; t++)
+    if (N[t] < 0) return set_error(TL_EINVAL, "negative GEMM dimension (N[%d]=%d)", t, N[t]);
+  if (M == 0 || K == 0) return TL_OK;
+  int rc;
+  if ((rc = check_device_ptr(dX, "output"))) return rc;
+  for (int t = 0; t < nprod; t++) {
+    if (N[t] == 0) continue;
+    if ((rc = check_device_ptr(dY[t], "first operand"))) return rc;
+    if ((rc = check_device_ptr(W[t], "second operand"))) return rc;
+  }
+  // Products with an empty reduction add nothing.
+  const float *As[3], *Bs[3];
+  int Ns[3], n = 0;
+  for (int t = 0; t < nprod; t++)
+    if (N[t] > 0) { As[n] = dY[t]; Bs[n] = W[t]; Ns[n] = N[t]; n++; }
+  if (n == 0) {
+    g_engine_last = 1;
+    TL_TRY_CUDA(cudaMemsetAsync(dX, 0, sizeof(float) * (size_t)M * K, c->stream));
+    return TL_OK;
+  }
+  return gemm_run_nt_sum(c, dX, n, As, Bs, Ns, M, K);
 }
 TL_API int tl_set_gemm_engine(int engine) {
   if (engine < 0 || engine > 3) return set_error(TL_EINVAL, "engine must be 0, 1, 2 or 3");

@@ -42,4 +42,14 @@ int gemm_tc_prepare(DeviceCtx *c);
 int gemm_tc(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, int M, int K, int N, bool pair,
             const float *add);
 
+// C[M,K] = sum over t < nprod (<= 3) of A_t[M,N_t] @ B_t[K,N_t]^T, one
+// CTA-pair launch whose reduction walks the products' k-blocks in turn
+// (overwrites C).
+int gemm_tc_nt_sum(DeviceCtx *c, float *C, int nprod, const float *const *A, const float *const *B, const int *N,
+                   int M, int K);
+// The same sum through the engine choice: one launch when the pair kernel
+// would take every product, else one NT GEMM per product accumulating in turn.
+int gemm_run_nt_sum(DeviceCtx *c, float *C, int nprod, const float *const *A, const float *const *B, const int *N,
+                    int M, int K);
+
 }  // namespace tl

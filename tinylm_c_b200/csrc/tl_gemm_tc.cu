@@ -70,6 +70,10 @@ struct Params {
   int I, J, R, ldc;
   const float *add;      // nullptr, C (accumulate) or a residual, row stride ldc
   int kb_per_split;      // k-blocks per CTA along grid z (split-K)
+  // Pair kernel: the reduction's k-blocks [0, seg_end0) read tmA / tmB,
+  // [seg_end0, seg_end1) tmA1 / tmB1 and the rest tmA2 / tmB2 (several
+  // products summed into one output; INT_MAX when there is one).
+  int seg_end0, seg_end1;
   size_t split_stride;   // floats between the partial outputs of consecutive splits
   int *err;
 };
@@ -358,7 +362,9 @@ __host__ __device__ constexpr uint32_t make_idesc_pair(bool a_mn, bool b_mn) {
 
 template <bool A_MN, bool B_MN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
-gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
+gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const __grid_constant__ CUtensorMap tmA1, const __grid_constant__ CUtensorMap tmB1,
+                    const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2, Params p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t *raw_ring = smem, *lo_ring = smem + RAW_STAGES * RAW_BYTES;
@@ -436,18 +442,23 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         issued = kb + 1;
         const uint32_t st = raw_base + s * RAW_BYTES;
         mbar_arrive_expect_tx(bar_full(s), TX_BYTES);
-        const int k0 = (kb0 + kb) * BK;
+        // The product this k-block belongs to, and its k offset there.
+        int kg = kb0 + kb;
+        const CUtensorMap *ta = &tmA, *tb = &tmB;
+        if (kg >= p.seg_end1) { ta = &tmA2; tb = &tmB2; kg -= p.seg_end1; }
+        else if (kg >= p.seg_end0) { ta = &tmA1; tb = &tmB1; kg -= p.seg_end0; }
+        const int k0 = kg * BK;
         if (A_MN) {
 #pragma unroll
-          for (int b = 0; b < BM / 32; b++) tma_load_2d(st + b * 4096, &tmA, bar_full(s), i0 + 32 * b, k0);
+          for (int b = 0; b < BM / 32; b++) tma_load_2d(st + b * 4096, ta, bar_full(s), i0 + 32 * b, k0);
         } else {
-          tma_load_2d(st, &tmA, bar_full(s), k0, i0);
+          tma_load_2d(st, ta, bar_full(s), k0, i0);
         }
         if (B_MN) {
 #pragma unroll
-          for (int b = 0; b < BN / 32; b++) tma_load_2d(st + TILE_A + b * 4096, &tmB, bar_full(s), jb + 32 * b, k0);
+          for (int b = 0; b < BN / 32; b++) tma_load_2d(st + TILE_A + b * 4096, tb, bar_full(s), jb + 32 * b, k0);
         } else {
-          tma_load_2d(st + TILE_A, &tmB, bar_full(s), k0, jb);
+          tma_load_2d(st + TILE_A, tb, bar_full(s), k0, jb);
         }
       }
       // No copy may still be landing when the CTA exits.
@@ -695,7 +706,8 @@ static int launch(DeviceCtx *c, const CUtensorMap &ma, const CUtensorMap &mb, co
 // CTA pairs: grid x runs over the pairs' CTAs (cluster of 2 along x; the
 // kernel maps pairs to output tiles in grouped order), z over K splits.
 template <bool A_MN, bool B_MN>
-static int launch_pair(DeviceCtx *c, const CUtensorMap &ma, const CUtensorMap &mb, const Params &p, int splits) {
+static int launch_pair(DeviceCtx *c, const CUtensorMap &ma, const CUtensorMap &mb, const Params &p, int splits,
+                       const CUtensorMap *extra = nullptr) {
   static bool attr_set[kMaxDevices] = {};
   if (!attr_set[c->device]) {
     TL_TRY_CUDA(cudaFuncSetAttribute(gemm_tc_pair_kernel<A_MN, B_MN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -705,7 +717,10 @@ static int launch_pair(DeviceCtx *c, const CUtensorMap &ma, const CUtensorMap &m
   const unsigned pairs = (unsigned)((p.I + PM - 1) / PM) * (unsigned)((p.J + PN - 1) / PN);
   dim3 grid(2 * pairs, 1, splits);
   TraceScope ts(c, "gemm_tc_pair");
-  gemm_tc_pair_kernel<A_MN, B_MN><<<grid, NUM_THREADS, PAIR_SMEM_BYTES, c->stream>>>(ma, mb, p);
+  // extra: the maps of the second and third products (A1, B1, A2, B2)
+  const CUtensorMap &a1 = extra ? extra[0] : ma, &b1 = extra ? extra[1] : mb;
+  const CUtensorMap &a2 = extra ? extra[2] : ma, &b2 = extra ? extra[3] : mb;
+  gemm_tc_pair_kernel<A_MN, B_MN><<<grid, NUM_THREADS, PAIR_SMEM_BYTES, c->stream>>>(ma, mb, a1, b1, a2, b2, p);
   TL_TRY_CUDA(cudaGetLastError());
   return TL_OK;
 }
@@ -747,14 +762,17 @@ bool gemm_tc_prefer_pair(int I, int J, int R) {
   return I > tc::BM && J > tc::BN;
 }
 
-int gemm_tc(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, int M, int K, int N, bool pair,
-            const float *add) {
-  int rc;
-  if ((rc = tc::get_encoder())) return rc;
-  int I, J, R;
-  gemm_dims(op, M, K, N, &I, &J, &R);
+// Split-K choice, launch and (for s > 1) the fixed-order reduction of the
+// partials, for an I x J output whose reduction runs over nk k-blocks read
+// through the prepared tensor maps.  extra / seg_end0 / seg_end1: the maps
+// and k-block boundaries of a second and third product summed into the same
+// output (pair kernel, NT only).
+static int gemm_tc_launch(DeviceCtx *c, GemmOp op, float *C, int I, int J, int nk, int out_ldc,
+                          const CUtensorMap &ma, const CUtensorMap &mb, const CUtensorMap *extra, int seg_end0,
+                          int seg_end1, bool pair, const float *add) {
   tc::Params p;
-  p.C = C; p.I = I; p.J = J; p.R = R; p.err = c->err_flag;
+  p.C = C; p.I = I; p.J = J; p.R = nk * tc::BK; p.err = c->err_flag;
+  p.seg_end0 = seg_end0; p.seg_end1 = seg_end1;
   // Split-K.  A launch takes ceil(CTAs / SMs) waves of (k-blocks per split)
   // k-block times; splitting the reduction over s CTAs multiplies the CTAs by
   // s and divides the k-blocks by s, so the split count is chosen to minimise
@@ -766,7 +784,6 @@ int gemm_tc(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, i
   // workspace.  A pair tile (256 x 256) occupies two SMs.
   const int tm = pair ? tc::PM : tc::BM, tn = pair ? tc::PN : tc::BN, sms_per_tile = pair ? 2 : 1;
   const long long tiles = (long long)((I + tm - 1) / tm) * ((J + tn - 1) / tn);
-  const int nk = (R + tc::BK - 1) / tc::BK;
   int splits = 1;
   if (c->gemm_ws) {
     const size_t cap = c->gemm_ws_floats / ((size_t)I * J);
@@ -789,6 +806,39 @@ int gemm_tc(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, i
     splits = (nk + kb_per - 1) / kb_per;
   }
   p.kb_per_split = kb_per;
+  if (splits > 1) {
+    p.C = c->gemm_ws; p.ldc = J; p.add = nullptr; p.split_stride = (size_t)I * J;
+  } else {
+    p.ldc = out_ldc; p.add = add; p.split_stride = 0;
+  }
+  int rc = TL_OK;
+  switch (op) {
+    case GemmOp::NN:
+      rc = pair ? tc::launch_pair<false, true>(c, ma, mb, p, splits) : tc::launch<false, true>(c, ma, mb, p, splits);
+      break;
+    case GemmOp::NT:
+      rc = pair ? tc::launch_pair<false, false>(c, ma, mb, p, splits, extra)
+                : tc::launch<false, false>(c, ma, mb, p, splits);
+      break;
+    case GemmOp::TN:
+      rc = pair ? tc::launch_pair<true, true>(c, ma, mb, p, splits) : tc::launch<true, true>(c, ma, mb, p, splits);
+      break;
+  }
+  if (rc || splits == 1) return rc;
+  TraceScope ts(c, "gemm_splitk_reduce");
+  const size_t q = (size_t)I * J / 4;
+  unsigned blocks = (unsigned)std::min<size_t>((q + 255) / 256, (size_t)c->num_sms * 8);
+  tc::splitk_reduce_kernel<<<blocks, 256, 0, c->stream>>>(C, out_ldc, add, c->gemm_ws, splits, I, J);
+  TL_TRY_CUDA(cudaGetLastError());
+  return TL_OK;
+}
+
+int gemm_tc(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, int M, int K, int N, bool pair,
+            const float *add) {
+  int rc;
+  if ((rc = tc::get_encoder())) return rc;
+  int I, J, R;
+  gemm_dims(op, M, K, N, &I, &J, &R);
   int out_ldc = 0;
   CUtensorMap ma, mb;
   switch (op) {
@@ -808,29 +858,32 @@ int gemm_tc(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, i
       if ((rc = tc::make_map(&mb, B, N, M, N, 32, 32, true))) return rc;
       break;
   }
-  if (splits > 1) {
-    p.C = c->gemm_ws; p.ldc = J; p.add = nullptr; p.split_stride = (size_t)I * J;
-  } else {
-    p.ldc = out_ldc; p.add = add; p.split_stride = 0;
+  const int nk = (R + tc::BK - 1) / tc::BK;
+  return gemm_tc_launch(c, op, C, I, J, nk, out_ldc, ma, mb, nullptr, 0x7fffffff, 0x7fffffff, pair, add);
+}
+
+int gemm_tc_nt_sum(DeviceCtx *c, float *C, int nprod, const float *const *A, const float *const *B, const int *N,
+                   int M, int K) {
+  if (nprod < 1 || nprod > 3) return set_error(TL_EINVAL, "gemm_tc_nt_sum takes 1 to 3 products, not %d", nprod);
+  int rc;
+  if ((rc = tc::get_encoder())) return rc;
+  // One pair of maps per product; product t covers k-blocks [end[t-1], end[t]).
+  // A product's last k-block reads past its N columns, where the copies fill
+  // zeros for both operands.
+  CUtensorMap maps[6];
+  int end[3];
+  int nk = 0;
+  for (int t = 0; t < nprod; t++) {
+    if ((rc = tc::make_map(&maps[2 * t], A[t], N[t], M, N[t], 32, tc::BM, false))) return rc;
+    if ((rc = tc::make_map(&maps[2 * t + 1], B[t], N[t], K, N[t], 32, tc::BN, false))) return rc;
+    nk += (N[t] + tc::BK - 1) / tc::BK;
+    end[t] = nk;
   }
-  switch (op) {
-    case GemmOp::NN:
-      rc = pair ? tc::launch_pair<false, true>(c, ma, mb, p, splits) : tc::launch<false, true>(c, ma, mb, p, splits);
-      break;
-    case GemmOp::NT:
-      rc = pair ? tc::launch_pair<false, false>(c, ma, mb, p, splits) : tc::launch<false, false>(c, ma, mb, p, splits);
-      break;
-    case GemmOp::TN:
-      rc = pair ? tc::launch_pair<true, true>(c, ma, mb, p, splits) : tc::launch<true, true>(c, ma, mb, p, splits);
-      break;
+  for (int t = nprod; t < 3; t++) {  // unused products: never reached
+    maps[2 * t] = maps[0]; maps[2 * t + 1] = maps[1];
+    end[t] = 0x7fffffff;
   }
-  if (rc || splits == 1) return rc;
-  TraceScope ts(c, "gemm_splitk_reduce");
-  const size_t q = (size_t)I * J / 4;
-  unsigned blocks = (unsigned)std::min<size_t>((q + 255) / 256, (size_t)c->num_sms * 8);
-  tc::splitk_reduce_kernel<<<blocks, 256, 0, c->stream>>>(C, out_ldc, add, c->gemm_ws, splits, I, J);
-  TL_TRY_CUDA(cudaGetLastError());
-  return TL_OK;
+  return gemm_tc_launch(c, GemmOp::NT, C, M, K, nk, K, maps[0], maps[1], maps + 2, end[0], end[1], true, nullptr);
 }
 
 }  // namespace tl

@@ -159,8 +159,11 @@ static int micro_step(DeviceCtx *c, Model &m, const float *P, float *G, const in
     TRY(gemm(c, GemmOp::TN, G + m.o_w2[l], m.act[l], m.dout, N, F, D));
     TRY(gemm_add(c, GemmOp::NT, m.dact, m.dout, P + m.o_w2[l], N, F, D, nullptr));
     TRY(k_swiglu_bwd(c, m.g[l], m.u[l], m.dact, m.dgb, m.du, NF));
-    TRY(gemm_add(c, GemmOp::NT, m.dfnorm, m.dgb, P + m.o_w1[l], N, D, F, nullptr));
-    TRY(gemm(c, GemmOp::NT, m.dfnorm, m.du, P + m.o_w3[l], N, D, F));
+    {  // dfnorm = dgb @ W1^T + du @ W3^T
+      const float *As[2] = {m.dgb, m.du}, *Bs[2] = {P + m.o_w1[l], P + m.o_w3[l]};
+      const int Ns[2] = {F, F};
+      TRY(gemm_run_nt_sum(c, m.dfnorm, 2, As, Bs, Ns, N, D));
+    }
     TRY(gemm(c, GemmOp::TN, G + m.o_w1[l], m.f_norm[l], m.dgb, N, D, F));
     TRY(gemm(c, GemmOp::TN, G + m.o_w3[l], m.f_norm[l], m.du, N, D, F));
     // dfin = dout + rmsnorm2 backward
@@ -174,9 +177,11 @@ static int micro_step(DeviceCtx *c, Model &m, const float *P, float *G, const in
                    m.KV, m.hd));
     TRY(k_rope(c, m.dq, m.rope_cos, m.rope_sin, N, m.H, m.hd, m.T, 1));
     TRY(k_rope(c, m.dk, m.rope_cos, m.rope_sin, N, m.KV, m.hd, m.T, 1));
-    TRY(gemm_add(c, GemmOp::NT, m.dnorm, m.dq, P + m.o_wq[l], N, D, D, nullptr));
-    TRY(gemm(c, GemmOp::NT, m.dnorm, m.dk, P + m.o_wk[l], N, D, KD));
-    TRY(gemm(c, GemmOp::NT, m.dnorm, m.dv, P + m.o_wv[l], N, D, KD));
+    {  // dnorm = dq @ Wq^T + dk @ Wk^T + dv @ Wv^T
+      const float *As[3] = {m.dq, m.dk, m.dv}, *Bs[3] = {P + m.o_wq[l], P + m.o_wk[l], P + m.o_wv[l]};
+      const int Ns[3] = {D, KD, KD};
+      TRY(gemm_run_nt_sum(c, m.dnorm, 3, As, Bs, Ns, N, D));
+    }
     TRY(gemm(c, GemmOp::TN, G + m.o_wq[l], m.a_norm[l], m.dq, N, D, D));
     TRY(gemm(c, GemmOp::TN, G + m.o_wk[l], m.a_norm[l], m.dk, N, D, KD));
     TRY(gemm(c, GemmOp::TN, G + m.o_wv[l], m.a_norm[l], m.dv, N, D, KD));

@@ -81,6 +81,19 @@ def mm_bt(dX, dY, W, M, K, N):
     check(lib().tl_matmul_bt(_ptr(dX, "dX", M * K), _ptr(dY, "dY", M * N), _ptr(W, "W", K * N), M, K, N))
 
 
+def mm_bt_sum(dX, dYs, Ws, Ns, M, K):
+    """dX[M,K] = sum_t dYs[t][M,Ns[t]] @ Ws[t][K,Ns[t]]^T (overwrite), 1 to 3 products."""
+    _prep(dX)
+    n = len(Ns)
+    if not (len(dYs) == len(Ws) == n):
+        raise ValueError("dYs, Ws and Ns must have the same length")
+    arr = ctypes.c_void_p * max(n, 1)
+    a = arr(*[_ptr(x, "dY", M * nt) for x, nt in zip(dYs, Ns)])
+    b = arr(*[_ptr(w, "W", K * nt) for w, nt in zip(Ws, Ns)])
+    nn = (ctypes.c_int * max(n, 1))(*Ns)
+    check(lib().tl_matmul_bt_sum(_ptr(dX, "dX", M * K), n, a, b, nn, M, K))
+
+
 def mm_atb(dW, X, dY, M, K, N):
     """dW[K,N] += X[M,K]^T @ dY[M,N] (accumulate)."""
     _prep(dW)
