@@ -78,6 +78,38 @@ struct Params {
   int *err;
 };
 
+// One thread's output row of BN accumulators, `valid` of them inside the
+// matrix.  The addend (nullptr, the output itself, or a residual) is read 32
+// columns at a time before those columns are stored: with each load followed
+// by its store, a possibly aliasing store orders every load behind the
+// previous one, and the row takes 32 memory round trips instead of 4.
+// (An L2 prefetch of the addend rows from the producer thread measured
+// slower.)
+__device__ __forceinline__ void store_row(float *dst, const float *addp, float (&acc)[BN], int valid) {
+  if (valid >= BN) {
+    // In quarters of 32 columns: four round trips, and no registers beyond
+    // the accumulators' held for the loads in flight (wider groups spill).
+#pragma unroll
+    for (int e0 = 0; e0 < BN; e0 += 32) {
+      if (addp) {
+#pragma unroll
+        for (int e = e0; e < e0 + 32; e += 4) {
+          const float4 old = *reinterpret_cast<const float4 *>(addp + e);
+          acc[e] = old.x + acc[e]; acc[e + 1] = old.y + acc[e + 1];
+          acc[e + 2] = old.z + acc[e + 2]; acc[e + 3] = old.w + acc[e + 3];
+        }
+      }
+#pragma unroll
+      for (int e = e0; e < e0 + 32; e += 4)
+        *reinterpret_cast<float4 *>(dst + e) = make_float4(acc[e], acc[e + 1], acc[e + 2], acc[e + 3]);
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < BN; e++)
+      if (e < valid) dst[e] = addp ? addp[e] + acc[e] : acc[e];
+  }
+}
+
 template <bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
@@ -282,22 +314,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       if (row < p.I) {
         float *dst = Cout + (size_t)row * p.ldc + j0;
         const float *addp = p.add ? p.add + (size_t)row * p.ldc + j0 : nullptr;
-        if (j0 + BN <= p.J) {
-#pragma unroll
-          for (int e = 0; e < BN; e += 4) {
-            float4 o = make_float4(acc[e], acc[e + 1], acc[e + 2], acc[e + 3]);
-            if (addp) {
-              const float4 old = *reinterpret_cast<const float4 *>(addp + e);
-              o.x = old.x + o.x; o.y = old.y + o.y; o.z = old.z + o.z; o.w = old.w + o.w;
-            }
-            *reinterpret_cast<float4 *>(dst + e) = o;
-          }
-        } else {
-#pragma unroll
-          for (int e = 0; e < BN; e++) {
-            if (j0 + e < p.J) dst[e] = addp ? addp[e] + acc[e] : acc[e];
-          }
-        }
+        store_row(dst, addp, acc, p.J - j0);
       }
     }
   }
@@ -604,22 +621,7 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
       if (row < p.I) {
         float *dst = Cout + (size_t)row * p.ldc + jc;
         const float *addp = p.add ? p.add + (size_t)row * p.ldc + jc : nullptr;
-        if (jc + BN <= p.J) {
-#pragma unroll
-          for (int e = 0; e < BN; e += 4) {
-            float4 o = make_float4(acc[e], acc[e + 1], acc[e + 2], acc[e + 3]);
-            if (addp) {
-              const float4 old = *reinterpret_cast<const float4 *>(addp + e);
-              o.x = old.x + o.x; o.y = old.y + o.y; o.z = old.z + o.z; o.w = old.w + o.w;
-            }
-            *reinterpret_cast<float4 *>(dst + e) = o;
-          }
-        } else {
-#pragma unroll
-          for (int e = 0; e < BN; e++) {
-            if (jc + e < p.J) dst[e] = addp ? addp[e] + acc[e] : acc[e];
-          }
-        }
+        store_row(dst, addp, acc, p.J - jc);
       }
     }
   }
