@@ -340,6 +340,196 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   }
 }
 
+// ------------------------------------------------------------- dQ = dS K
+// The query-side product of the backward (tinylm.c:772-777, dq += dsc * k) for
+// one (sequence, query head, query half r): M = 128 queries, N = 64, the
+// reduction over keys [0, 128(r+1)) in blocks of 32.  A = dS comes from the
+// key-side kernel's dS^T scratch ([b][h][key][query], queries contiguous, so
+// the MN-major A operand), B = K (MN-major B), both by TMA with the 32-byte
+// atom swizzle; one CTA (cta_group::1), two 48 KB stages, so two CTAs share
+// an SM.  Key blocks 0-3 accumulate in TMEM columns 0..63 and 4-7 in 64..127
+// (each sum kept short in the truncating TMEM adds), added in fp32 by the
+// epilogue.  The scratch's tiles above the diagonal are never written by the
+// key-side kernel and stay zero from the model's set-up, which covers the
+// 64-key tile above the diagonal inside each 128 x 128 block read here.
+// Roles (192 threads): warp 0 TMA producer, warp 1 TMEM owner and MMA
+// issuer, warps 2-5 lo split, then the epilogue (warp w: rows 32*(w%4)..).
+constexpr int DQ_KB = 32;
+constexpr int DQ_TILE_A = QR * DQ_KB * 4;                       // 16 KB: 4 boxes of 32 queries x 32 keys
+constexpr int DQ_TILE_B = HD * DQ_KB * 4;                       // 8 KB: 2 boxes of 32 columns x 32 keys
+constexpr int DQ_OFF_AHI = 0, DQ_OFF_ALO = DQ_TILE_A, DQ_OFF_BHI = 2 * DQ_TILE_A,
+              DQ_OFF_BLO = 2 * DQ_TILE_A + DQ_TILE_B;
+constexpr int DQ_STAGE_BYTES = 2 * (DQ_TILE_A + DQ_TILE_B);     // 48 KB
+constexpr int DQ_STAGES = 2;
+constexpr int DQ_THREADS = 192;
+constexpr int DQ_SMEM_BYTES = DQ_STAGES * DQ_STAGE_BYTES + 1024 + 128;
+constexpr int DQ_TMEM_COLS = 128;
+constexpr uint32_t DQ_IDESC = (1u << 4) | (2u << 7) | (2u << 10) | (1u << 15) | (1u << 16) |
+                              ((uint32_t)(HD >> 3) << 17) | ((uint32_t)(QR >> 4) << 24);
+static_assert(2 * DQ_SMEM_BYTES <= 228 * 1024, "two dQ CTAs per SM");
+
+struct DqArgs {
+  float *dq;
+  int H, KV, D;
+  int *err;
+};
+
+__global__ void __launch_bounds__(DQ_THREADS)
+attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmK, DqArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + DQ_STAGES * DQ_STAGE_BYTES);
+  // bars: full[S] (TMA landed), ready[S] (lo parts written), empty[S] (MMAs
+  // done with the stage), acc (every MMA done)
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * DQ_STAGES + 1);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+  const uint32_t base = smem_u32(smem);
+  auto bar_full = [&](int s) { return smem_u32(&bars[s]); };
+  auto bar_ready = [&](int s) { return smem_u32(&bars[DQ_STAGES + s]); };
+  auto bar_empty = [&](int s) { return smem_u32(&bars[2 * DQ_STAGES + s]); };
+  const uint32_t bar_acc = smem_u32(&bars[3 * DQ_STAGES]);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = 1 - (int)(blockIdx.x & 1);     // the half with 8 key blocks first in launch order
+  const int bh = blockIdx.x >> 1, b = bh / a.H, h = bh % a.H, kvh = h / (a.H / a.KV);
+  const int nk = 4 * (r + 1);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < DQ_STAGES; s++) {
+      mbar_init(bar_full(s), 1);
+      mbar_init(bar_ready(s), 4);
+      mbar_init(bar_empty(s), 1);
+    }
+    mbar_init(bar_acc, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(DQ_TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int issued = 0;
+      for (int kb = 0; kb < nk; kb++) {
+        const int s = kb % DQ_STAGES, u = kb / DQ_STAGES;
+        if (u > 0 && !mbar_wait(bar_empty(s), (u - 1) & 1, abort_flag, a.err, 51)) break;
+        issued = kb + 1;
+        const uint32_t st = base + s * DQ_STAGE_BYTES;
+        mbar_arrive_expect_tx(bar_full(s), DQ_TILE_A + DQ_TILE_B);
+        const int key0 = kb * DQ_KB;
+#pragma unroll
+        for (int x = 0; x < QR / 32; x++)
+          tma_load_2d(st + DQ_OFF_AHI + x * 4096, &tmS, bar_full(s), QR * r + 32 * x, bh * T + key0);
+#pragma unroll
+        for (int x = 0; x < HD / 32; x++)
+          tma_load_2d(st + DQ_OFF_BHI + x * 4096, &tmK, bar_full(s), kvh * HD + 32 * x, b * T + key0);
+      }
+      // No copy may still be landing when the CTA exits.
+      for (int kb = issued > DQ_STAGES ? issued - DQ_STAGES : 0; kb < issued; kb++) {
+        const long long t0 = clock64();
+        while (!mbar_try_wait(bar_full(kb % DQ_STAGES), (kb / DQ_STAGES) & 1)) {
+          if (clock64() - t0 > WAIT_LIMIT_CYCLES) { atomicExch(a.err, 56); break; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      for (int kb = 0; kb < nk; kb++) {
+        const int s = kb % DQ_STAGES, u = kb / DQ_STAGES;
+        if (!mbar_wait(bar_ready(s), u & 1, abort_flag, a.err, 52)) break;
+        tc_fence_after();
+        const uint32_t st = base + s * DQ_STAGE_BYTES;
+        const uint32_t d = tmem + (uint32_t)((kb >> 2) * HD);
+#pragma unroll
+        for (int kk = 0; kk < DQ_KB / 8; kk++) {
+          const uint32_t off = kk * 1024;        // eight key rows per MMA step
+          const uint64_t a_hi = smem_desc(st + DQ_OFF_AHI + off, 4096, 512, LAYOUT_SW128_BASE32B);
+          const uint64_t a_lo = smem_desc(st + DQ_OFF_ALO + off, 4096, 512, LAYOUT_SW128_BASE32B);
+          const uint64_t b_hi = smem_desc(st + DQ_OFF_BHI + off, 4096, 512, LAYOUT_SW128_BASE32B);
+          const uint64_t b_lo = smem_desc(st + DQ_OFF_BLO + off, 4096, 512, LAYOUT_SW128_BASE32B);
+          tc_mma(d, a_lo, b_hi, DQ_IDESC, ((kb & 3) > 0 || kk > 0) ? 1u : 0u);
+          tc_mma(d, a_hi, b_lo, DQ_IDESC, 1);
+          tc_mma(d, a_hi, b_hi, DQ_IDESC, 1);
+        }
+        tc_commit(bar_empty(s));
+      }
+      // Every issued MMA finished (also on the abort path) before the
+      // epilogue reads TMEM and before it is released.
+      tc_commit(bar_acc);
+      const long long t0 = clock64();
+      while (!mbar_try_wait(bar_acc, 0)) {
+        if (clock64() - t0 > WAIT_LIMIT_CYCLES) { *abort_flag = 1; atomicExch(a.err, 55); break; }
+      }
+    }
+  } else {
+    // -------------------------------------- lo split, then the epilogue
+    const int t = threadIdx.x - 64;            // 0..127
+    bool ok = true;
+    for (int kb = 0; kb < nk; kb++) {
+      const int s = kb % DQ_STAGES, u = kb / DQ_STAGES;
+      if (!mbar_wait(bar_full(s), u & 1, abort_flag, a.err, 53)) { ok = false; break; }
+      uint8_t *st = smem + s * DQ_STAGE_BYTES;
+      // A then B: 1024 + 512 float4 of raw data, 12 per thread; lo lands at
+      // the same offset of the lo tile (same swizzled layout).
+#pragma unroll 4
+      for (int e = 0; e < 12; e++) {
+        const int idx = e * 128 + t;
+        const int off = idx < 1024 ? DQ_OFF_AHI + idx * 16 : DQ_OFF_BHI + (idx - 1024) * 16;
+        const int lo_off = off + (idx < 1024 ? DQ_TILE_A : DQ_TILE_B);
+        const float4 x = *reinterpret_cast<const float4 *>(st + off);
+        float4 lo;
+        lo.x = x.x - tf32_trunc(x.x); lo.y = x.y - tf32_trunc(x.y);
+        lo.z = x.z - tf32_trunc(x.z); lo.w = x.w - tf32_trunc(x.w);
+        *reinterpret_cast<float4 *>(st + lo_off) = lo;
+      }
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_ready(s));
+    }
+    const bool landed = ok && mbar_wait(bar_acc, 0, abort_flag, a.err, 54);
+    if (__all_sync(0xffffffffu, landed) && !*abort_flag) {
+      tc_fence_after();
+      const int q4 = warp & 3, row = q4 * 32 + lane;
+      const uint32_t lane_addr = (uint32_t)(q4 * 32) << 16;
+      float *dst = a.dq + ((size_t)b * T + QR * r + row) * a.D + (size_t)h * HD;
+#pragma unroll
+      for (int cc = 0; cc < HD / 32; cc++) {
+        uint32_t v0[32];
+        tmem_ld32(tmem + lane_addr + cc * 32, v0);
+        float o[32];
+#pragma unroll
+        for (int e = 0; e < 32; e++) o[e] = __uint_as_float(v0[e]);
+        if (r == 1) {
+          uint32_t v1[32];
+          tmem_ld32(tmem + lane_addr + HD + cc * 32, v1);
+#pragma unroll
+          for (int e = 0; e < 32; e++) o[e] += __uint_as_float(v1[e]);
+        }
+#pragma unroll
+        for (int e = 0; e < 32; e += 4)
+          *reinterpret_cast<float4 *>(dst + cc * 32 + e) = make_float4(o[e], o[e + 1], o[e + 2], o[e + 3]);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(DQ_TMEM_COLS) : "memory");
+  }
+}
+
 static PFN_cuTensorMapEncodeTiled_v12000 g_enc = nullptr;
 
 static int map2d(CUtensorMap *m, const float *p, uint64_t inner, uint64_t outer, uint32_t bx, uint32_t by,
@@ -396,9 +586,39 @@ int attn_fwd_tc(DeviceCtx *c, const float *q, const float *k, const float *v, fl
   return TL_OK;
 }
 
+// True when the tensor-core dQ product takes this shape (the forward's).
+bool attn_bwd_dq_tc_supported(const float *dsT, const float *k, const float *dq, int T, int hd, int H, int KV) {
+  const uintptr_t al =
+      reinterpret_cast<uintptr_t>(dsT) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(dq);
+  return T == atc::T && hd == atc::HD && (al & 15) == 0 && KV > 0 && H % KV == 0;
+}
+
+int attn_bwd_dq_tc(DeviceCtx *c, const float *dsT, const float *k, float *dq, int B, int H, int KV) {
+  static bool attr[kMaxDevices] = {};
+  if (!attr[c->device]) {
+    TL_TRY_CUDA(cudaFuncSetAttribute(atc::attn_bwd_dq_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     atc::DQ_SMEM_BYTES));
+    attr[c->device] = true;
+  }
+  const int KD = KV * atc::HD;
+  CUtensorMap ms, mk;
+  int rc;
+  if ((rc = atc::map2d(&ms, dsT, atc::T, (uint64_t)B * H * atc::T, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B)))
+    return rc;
+  if ((rc = atc::map2d(&mk, k, KD, (uint64_t)B * atc::T, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))) return rc;
+  atc::DqArgs a;
+  a.dq = dq; a.H = H; a.KV = KV; a.D = H * atc::HD; a.err = c->err_flag;
+  TraceScope ts(c, "k_attn_bwd_dq_tc");
+  atc::attn_bwd_dq_tc_kernel<<<2 * B * H, atc::DQ_THREADS, atc::DQ_SMEM_BYTES, c->stream>>>(ms, mk, a);
+  TL_TRY_CUDA(cudaGetLastError());
+  return TL_OK;
+}
+
 int attn_tc_prepare(DeviceCtx *c) {
   TL_TRY_CUDA(cudaFuncSetAttribute(atc::attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    atc::SMEM_BYTES));
+  TL_TRY_CUDA(cudaFuncSetAttribute(atc::attn_bwd_dq_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   atc::DQ_SMEM_BYTES));
   (void)c;
   return TL_OK;
 }

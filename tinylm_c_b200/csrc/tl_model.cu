@@ -254,6 +254,9 @@ static int alloc_model(Model &m) {
   TL_TRY_CUDA(cudaMalloc(&m.arena, floats * sizeof(float)));
   float *base = static_cast<float *>(m.arena);
   for (auto &s : slots) *s.first = base + s.second;
+  // The attention backward writes dS^T only for key tiles at or below the
+  // query tile; the rest is read as zeros by the tensor-core dQ product.
+  TL_TRY_CUDA(cudaMemset(m.dsT, 0, sizeof(float) * att_rows * m.T));
   m.loss_rows = reinterpret_cast<double *>(base + o_loss);
   m.loss_acc = m.loss_rows + N;
   // RoPE table in fp32 exactly as rope_init (tinylm.c:613-623)

@@ -848,6 +848,8 @@ int k_loss_final(DeviceCtx *c, const double *acc, double denom, float *out) {
 bool attn_fwd_tc_supported(const float *q, const float *k, const float *v, int T, int hd, int H, int KV);
 int attn_fwd_tc(DeviceCtx *c, const float *q, const float *k, const float *v, float *out, float *lse, int B, int T,
                 int H, int KV, int hd);
+bool attn_bwd_dq_tc_supported(const float *dsT, const float *k, const float *dq, int T, int hd, int H, int KV);
+int attn_bwd_dq_tc(DeviceCtx *c, const float *dsT, const float *k, float *dq, int B, int H, int KV);
 static thread_local int g_attn_engine = 0;   // 0 automatic, 1 CUDA cores, 2 tensor cores
 
 int k_attn_fwd(DeviceCtx *c, const float *q, const float *k, const float *v, float *out, float *lse, int B, int T,
@@ -873,6 +875,8 @@ int k_attn_bwd(DeviceCtx *c, const float *q, const float *k, const float *v, con
   mk::attn_bwd_dkdv_kernel<<<B * KV * (T / mk::AT), 256, attn_smem_dkdv(), c->stream>>>(
       q, k, v, dout, lse, Drow, dk, dv, dsT, T, H, KV, hd, scale);
   MK_LAUNCH_CHECK();
+  if (g_attn_engine != 1 && attn_bwd_dq_tc_supported(dsT, k, dq, T, hd, H, KV))
+    return attn_bwd_dq_tc(c, dsT, k, dq, B, H, KV);
   mk::attn_bwd_dq_kernel<<<B * H * (T / mk::AT), 256, attn_smem_dq(), c->stream>>>(k, dsT, dq, T, H, KV, hd);
   MK_LAUNCH_CHECK();
   return TL_OK;
