@@ -530,6 +530,382 @@ attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmS, const __grid_cons
   }
 }
 
+// ------------------------------------------------------- dK, dV (key side)
+// The key-side products of the backward (tinylm.c:761-777: dv += p dO and
+// dk += dsc q, with the scores and probabilities recomputed as at 748-758)
+// for one (sequence, kv head, key block kb of 128 keys), looping over the
+// group's query heads and the 32-query chunks at or after the key block.
+// M = 128 keys throughout (cta_group::1):
+//   S^T = K Q_c^T, dP^T = V dO_c^T   N = 32 queries, K = 64 in two blocks;
+//        K and V stay resident (K-major, with lo parts), Q_c and dO_c arrive
+//        by TMA as K-major B tiles; into TMEM buffer i % 2 of chunk i.
+//   P^T = exp(scale s - lse), dS^T = P^T (dP^T - D) scale   (warps 2-5, a key
+//        row per thread): raw and lo parts written back to TMEM (P over S,
+//        dS over dP), and dS^T to the scratch the dQ product reads.
+//   dV += P^T dO_c, dK += dS^T Q_c   A from TMEM, B = dO_c / Q_c as MN-major
+//        tiles (a second TMA copy, 32-byte atom swizzle), N = 64, K = 32; into
+//        the accumulator pair of the current head (two, alternating by head),
+//        which warps 6-9 add into fp32 registers once the head is done.
+// Warps 6-9 also write the lo parts of every staged tile.  Warp 0 is the TMA
+// producer, warp 1 the TMEM owner and MMA issuer.  Every wait is bounded.
+constexpr int BW_THREADS = 320;
+constexpr int BW_NQ = 32;                               // queries per chunk
+constexpr int BW_KTILE = QR * 32 * 4;                   // 16 KB: 128 keys x 32 of head_dim
+constexpr int BW_CTILE = BW_NQ * 32 * 4;                // 4 KB: 32 queries x 32 of head_dim
+constexpr int BW_OFF_K = 0, BW_OFF_V = 4 * BW_KTILE;    // raw (2 tiles), then lo (2 tiles): +32 KB
+constexpr int BW_KV_LO = 2 * BW_KTILE;
+constexpr int BW_OFF_QK = 8 * BW_KTILE;                 // chunk tiles: raw (2), then lo (2): +8 KB
+constexpr int BW_OFF_OK = BW_OFF_QK + 4 * BW_CTILE;
+constexpr int BW_OFF_QM = BW_OFF_OK + 4 * BW_CTILE;
+constexpr int BW_OFF_OM = BW_OFF_QM + 4 * BW_CTILE;
+constexpr int BW_C_LO = 2 * BW_CTILE;
+constexpr int BW_DATA = BW_OFF_OM + 4 * BW_CTILE;       // 192 KB
+constexpr int BW_NBARS = 17;
+constexpr int BW_SMEM_BYTES = BW_DATA + 1024 + BW_NBARS * 8 + 16;
+static_assert(BW_SMEM_BYTES <= 232448, "dK/dV kernel exceeds the opt-in shared memory");
+// TMEM columns: S / P raw of buffer b at 64b, dP / dS raw at 64b + 32; their
+// lo parts 128 further; the dV / dK accumulators of pair a at 256 + 128a
+// (+ 64 for dK).
+constexpr int BW_TMEM_COLS = 512;
+constexpr uint32_t BW_IDESC_SD = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BW_NQ >> 3) << 17) |
+                                 ((uint32_t)(QR >> 4) << 24);
+constexpr uint32_t BW_IDESC_ACC = (1u << 4) | (2u << 7) | (2u << 10) | (1u << 16) | ((uint32_t)(HD >> 3) << 17) |
+                                  ((uint32_t)(QR >> 4) << 24);
+
+struct BwArgs {
+  const float *lse, *Drow;
+  float *dsT, *dk, *dv;
+  int B, H, KV;
+  float scale;
+  int *err;
+};
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+      "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+      "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+      "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+      "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+      "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+      "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+      "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// D (TMEM) (+)= A (TMEM, 128 lanes x 8 columns) * B (shared memory).
+__device__ __forceinline__ void tc_mma_tmem_a(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{ .reg .pred p; setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p; }" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// lo = x - tf32(x) of n16 16-byte words at src, written at src + lo_off.
+__device__ __forceinline__ void split_lo(uint8_t *src, int lo_off, int n16, int t, int nthreads) {
+  for (int idx = t; idx < n16; idx += nthreads) {
+    const float4 x = *reinterpret_cast<const float4 *>(src + idx * 16);
+    float4 lo;
+    lo.x = x.x - tf32_trunc(x.x); lo.y = x.y - tf32_trunc(x.y);
+    lo.z = x.z - tf32_trunc(x.z); lo.w = x.w - tf32_trunc(x.w);
+    *reinterpret_cast<float4 *>(src + lo_off + idx * 16) = lo;
+  }
+}
+
+__global__ void __launch_bounds__(BW_THREADS, 1)
+attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmKk, const __grid_constant__ CUtensorMap tmVk,
+                        const __grid_constant__ CUtensorMap tmQk, const __grid_constant__ CUtensorMap tmOk,
+                        const __grid_constant__ CUtensorMap tmQm, const __grid_constant__ CUtensorMap tmOm, BwArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + BW_DATA);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + BW_NBARS);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+  const uint32_t base = smem_u32(smem);
+  auto bar = [&](int i) { return smem_u32(&bars[i]); };
+  constexpr int KV_FULL = 0, KV_READY = 1, KM_FULL = 2, KM_READY = 3, KM_EMPTY = 4, MN_FULL = 5, MN_READY = 6,
+                MN_EMPTY = 7, SD_FULL = 8, PD_READY = 10, ACC_FULL = 12, ACC_EMPTY = 14, FIN = 16;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nbk = a.B * a.KV;
+  const int kb = (int)blockIdx.x < nbk ? 0 : 1;          // the key blocks with 8 chunks per head first
+  const int bk = (int)blockIdx.x % nbk, bb = bk / a.KV, kvh = bk % a.KV, grp = a.H / a.KV;
+  const int c0 = 4 * kb, nc = T / BW_NQ - c0, n = grp * nc;
+  const int key0 = QR * kb;
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar(KV_FULL), 1);
+    mbar_init(bar(KV_READY), 4);
+    mbar_init(bar(KM_FULL), 1);
+    mbar_init(bar(KM_READY), 4);
+    mbar_init(bar(KM_EMPTY), 1);
+    mbar_init(bar(MN_FULL), 1);
+    mbar_init(bar(MN_READY), 4);
+    mbar_init(bar(MN_EMPTY), 1);
+    for (int x = 0; x < 2; x++) {
+      mbar_init(bar(SD_FULL + x), 1);
+      mbar_init(bar(PD_READY + x), 4);
+      mbar_init(bar(ACC_FULL + x), 1);
+      mbar_init(bar(ACC_EMPTY + x), 4);
+    }
+    mbar_init(bar(FIN), 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(BW_TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const int krow = bb * T + key0;
+      mbar_arrive_expect_tx(bar(KV_FULL), 4 * BW_KTILE);
+      for (int x = 0; x < 2; x++) {
+        tma_load_2d(base + BW_OFF_K + x * BW_KTILE, &tmKk, bar(KV_FULL), kvh * HD + 32 * x, krow);
+        tma_load_2d(base + BW_OFF_V + x * BW_KTILE, &tmVk, bar(KV_FULL), kvh * HD + 32 * x, krow);
+      }
+      int km = 0, mn = 0;
+      for (int i = 0; i < n; i++) {
+        const int h = kvh * grp + i / nc, qrow = bb * T + BW_NQ * (c0 + i % nc);
+        if (i > 0 && !mbar_wait(bar(KM_EMPTY), (i - 1) & 1, abort_flag, a.err, 61)) break;
+        mbar_arrive_expect_tx(bar(KM_FULL), 4 * BW_CTILE);
+        for (int x = 0; x < 2; x++) {
+          tma_load_2d(base + BW_OFF_QK + x * BW_CTILE, &tmQk, bar(KM_FULL), h * HD + 32 * x, qrow);
+          tma_load_2d(base + BW_OFF_OK + x * BW_CTILE, &tmOk, bar(KM_FULL), h * HD + 32 * x, qrow);
+        }
+        km = i + 1;
+        if (i > 0 && !mbar_wait(bar(MN_EMPTY), (i - 1) & 1, abort_flag, a.err, 62)) break;
+        mbar_arrive_expect_tx(bar(MN_FULL), 4 * BW_CTILE);
+        for (int x = 0; x < 2; x++) {
+          tma_load_2d(base + BW_OFF_QM + x * BW_CTILE, &tmQm, bar(MN_FULL), h * HD + 32 * x, qrow);
+          tma_load_2d(base + BW_OFF_OM + x * BW_CTILE, &tmOm, bar(MN_FULL), h * HD + 32 * x, qrow);
+        }
+        mn = i + 1;
+      }
+      // No copy may still be landing when the CTA exits (phases complete in
+      // order, so the last one issued on each barrier covers the rest).
+      const int last[3][2] = {{KV_FULL, 1}, {KM_FULL, km}, {MN_FULL, mn}};
+      for (int w = 0; w < 3; w++) {
+        if (last[w][1] == 0) continue;
+        const long long t0 = clock64();
+        while (!mbar_try_wait(bar(last[w][0]), (last[w][1] - 1) & 1)) {
+          if (clock64() - t0 > WAIT_LIMIT_CYCLES) { atomicExch(a.err, 63); break; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      auto issue_sd = [&](int i) -> bool {
+        const int b = i & 1;
+        // Buffer b was last read by the dV/dK products of chunk i - 2.
+        if (i >= 2 && !mbar_wait(bar(MN_EMPTY), (i - 2) & 1, abort_flag, a.err, 64)) return false;
+        if (!mbar_wait(bar(KM_READY), i & 1, abort_flag, a.err, 65)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int m = 0; m < 2; m++) {            // m = 0: S^T = K Q^T, 1: dP^T = V dO^T
+          const uint32_t d = tmem + 64 * b + 32 * m;
+          const uint32_t at = base + (m ? BW_OFF_V : BW_OFF_K), bt = base + (m ? BW_OFF_OK : BW_OFF_QK);
+#pragma unroll
+          for (int x = 0; x < 2; x++) {
+#pragma unroll
+            for (int kk = 0; kk < 4; kk++) {
+              const uint64_t a_hi = smem_desc(at + x * BW_KTILE + kk * 32, 16, 1024, LAYOUT_SW128);
+              const uint64_t a_lo = smem_desc(at + BW_KV_LO + x * BW_KTILE + kk * 32, 16, 1024, LAYOUT_SW128);
+              const uint64_t b_hi = smem_desc(bt + x * BW_CTILE + kk * 32, 16, 1024, LAYOUT_SW128);
+              const uint64_t b_lo = smem_desc(bt + BW_C_LO + x * BW_CTILE + kk * 32, 16, 1024, LAYOUT_SW128);
+              tc_mma(d, a_lo, b_hi, BW_IDESC_SD, (x > 0 || kk > 0) ? 1u : 0u);
+              tc_mma(d, a_hi, b_lo, BW_IDESC_SD, 1);
+              tc_mma(d, a_hi, b_hi, BW_IDESC_SD, 1);
+            }
+          }
+        }
+        tc_commit(bar(KM_EMPTY));
+        tc_commit(bar(SD_FULL + b));
+        return true;
+      };
+      auto issue_acc = [&](int i) -> bool {
+        const int b = i & 1, g = i / nc, pa = g & 1;
+        const bool first = i % nc == 0, last = i % nc == nc - 1;
+        if (first && g >= 2 && !mbar_wait(bar(ACC_EMPTY + pa), ((g >> 1) - 1) & 1, abort_flag, a.err, 66))
+          return false;
+        if (!mbar_wait(bar(PD_READY + b), (i >> 1) & 1, abort_flag, a.err, 67)) return false;
+        if (!mbar_wait(bar(MN_READY), i & 1, abort_flag, a.err, 68)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int m = 0; m < 2; m++) {            // m = 0: dV += P^T dO, 1: dK += dS^T Q
+          const uint32_t d = tmem + 256 + 128 * pa + 64 * m;
+          const uint32_t a_hi = tmem + 64 * b + 32 * m, a_lo = a_hi + 128;
+          const uint32_t bt = base + (m ? BW_OFF_QM : BW_OFF_OM);
+#pragma unroll
+          for (int kk = 0; kk < BW_NQ / 8; kk++) {
+            const uint64_t b_hi = smem_desc(bt + kk * 1024, 4096, 512, LAYOUT_SW128_BASE32B);
+            const uint64_t b_lo = smem_desc(bt + BW_C_LO + kk * 1024, 4096, 512, LAYOUT_SW128_BASE32B);
+            tc_mma_tmem_a(d, a_lo + kk * 8, b_hi, BW_IDESC_ACC, (!first || kk > 0) ? 1u : 0u);
+            tc_mma_tmem_a(d, a_hi + kk * 8, b_lo, BW_IDESC_ACC, 1);
+            tc_mma_tmem_a(d, a_hi + kk * 8, b_hi, BW_IDESC_ACC, 1);
+          }
+        }
+        tc_commit(bar(MN_EMPTY));
+        if (last) tc_commit(bar(ACC_FULL + pa));
+        return true;
+      };
+      if (mbar_wait(bar(KV_READY), 0, abort_flag, a.err, 69) && issue_sd(0)) {
+        for (int i = 0; i < n; i++) {
+          if (i + 1 < n && !issue_sd(i + 1)) break;
+          if (!issue_acc(i)) break;
+        }
+      }
+      // Every issued MMA finished (also on the abort path) before TMEM is
+      // read for the last time and released.
+      tc_commit(bar(FIN));
+      const long long t0 = clock64();
+      while (!mbar_try_wait(bar(FIN), 0)) {
+        if (clock64() - t0 > WAIT_LIMIT_CYCLES) { *abort_flag = 1; atomicExch(a.err, 70); break; }
+      }
+    }
+  } else if (warp < 6) {
+    // ------------------------------------------ P^T and dS^T (a key row each)
+    const int q4 = warp & 3, row = q4 * 32 + lane, key = key0 + row;
+    const uint32_t lane_addr = (uint32_t)(q4 * 32) << 16;
+    for (int i = 0; i < n; i++) {
+      const int b = i & 1, h = kvh * grp + i / nc, q0 = BW_NQ * (c0 + i % nc);
+      const size_t bh = (size_t)bb * a.H + h;
+      if (!__all_sync(0xffffffffu, mbar_wait(bar(SD_FULL + b), (i >> 1) & 1, abort_flag, a.err, 71))) break;
+      tc_fence_after();
+      uint32_t sv[32], dv[32];
+      tmem_ld32(tmem + lane_addr + 64 * b, sv);
+      tmem_ld32(tmem + lane_addr + 64 * b + 32, dv);
+      const float4 *lp = reinterpret_cast<const float4 *>(a.lse + bh * T + q0);
+      const float4 *dp = reinterpret_cast<const float4 *>(a.Drow + bh * T + q0);
+      // In place: sv becomes P, dv becomes dS; lo parts through one buffer.
+      float ph[32], dh[32], lo[32];
+#pragma unroll
+      for (int e4 = 0; e4 < 8; e4++) {
+        const float4 l4 = __ldg(lp + e4), d4 = __ldg(dp + e4);
+        const float ls[4] = {l4.x, l4.y, l4.z, l4.w}, ds[4] = {d4.x, d4.y, d4.z, d4.w};
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+          const int e = 4 * e4 + u;
+          const float pr = key <= q0 + e ? expf(__uint_as_float(sv[e]) * a.scale - ls[u]) : 0.0f;
+          ph[e] = pr;
+          dh[e] = pr * (__uint_as_float(dv[e]) - ds[u]) * a.scale;
+        }
+      }
+      tmem_st32(tmem + lane_addr + 64 * b, ph);
+      tmem_st32(tmem + lane_addr + 64 * b + 32, dh);
+#pragma unroll
+      for (int e = 0; e < 32; e++) lo[e] = ph[e] - tf32_trunc(ph[e]);
+      tmem_st32(tmem + lane_addr + 128 + 64 * b, lo);
+#pragma unroll
+      for (int e = 0; e < 32; e++) lo[e] = dh[e] - tf32_trunc(dh[e]);
+      tmem_st32(tmem + lane_addr + 128 + 64 * b + 32, lo);
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(PD_READY + b));
+      float4 *dst = reinterpret_cast<float4 *>(a.dsT + (bh * T + key) * T + q0);
+#pragma unroll
+      for (int e = 0; e < 32; e += 4) dst[e / 4] = make_float4(dh[e], dh[e + 1], dh[e + 2], dh[e + 3]);
+    }
+  } else {
+    // ---------------------- lo parts of the staged tiles; dV / dK per head
+    const int t = threadIdx.x - 192, q4 = warp & 3, row = q4 * 32 + lane;
+    const uint32_t lane_addr = (uint32_t)(q4 * 32) << 16;
+    float accv[HD], acck[HD];
+#pragma unroll
+    for (int e = 0; e < HD; e++) { accv[e] = 0.0f; acck[e] = 0.0f; }
+    bool ok = __all_sync(0xffffffffu, mbar_wait(bar(KV_FULL), 0, abort_flag, a.err, 72));
+    if (ok) {
+      split_lo(smem + BW_OFF_K, BW_KV_LO, 2 * BW_KTILE / 16, t, 128);
+      split_lo(smem + BW_OFF_V, BW_KV_LO, 2 * BW_KTILE / 16, t, 128);
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(KV_READY));
+    }
+    auto drain = [&](int g) -> bool {
+      const int pa = g & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(bar(ACC_FULL + pa), (g >> 1) & 1, abort_flag, a.err, 73))) return false;
+      tc_fence_after();
+#pragma unroll
+      for (int m = 0; m < 2; m++) {
+#pragma unroll
+        for (int cc = 0; cc < 4; cc++) {
+          uint32_t v[16];
+          tmem_ld16(tmem + lane_addr + 256 + 128 * pa + 64 * m + 16 * cc, v);
+#pragma unroll
+          for (int e = 0; e < 16; e++) {
+            if (m == 0) accv[16 * cc + e] += __uint_as_float(v[e]);
+            else acck[16 * cc + e] += __uint_as_float(v[e]);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(ACC_EMPTY + pa));
+      return true;
+    };
+    for (int i = 0; i < n && ok; i++) {
+      if (!(ok = __all_sync(0xffffffffu, mbar_wait(bar(KM_FULL), i & 1, abort_flag, a.err, 74)))) break;
+      split_lo(smem + BW_OFF_QK, BW_C_LO, 2 * BW_CTILE / 16, t, 128);
+      split_lo(smem + BW_OFF_OK, BW_C_LO, 2 * BW_CTILE / 16, t, 128);
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(KM_READY));
+      if (!(ok = __all_sync(0xffffffffu, mbar_wait(bar(MN_FULL), i & 1, abort_flag, a.err, 75)))) break;
+      split_lo(smem + BW_OFF_QM, BW_C_LO, 2 * BW_CTILE / 16, t, 128);
+      split_lo(smem + BW_OFF_OM, BW_C_LO, 2 * BW_CTILE / 16, t, 128);
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(MN_READY));
+      // The previous head's accumulators, once this chunk's tiles are ready
+      // (the issuer needs them before it finishes that head).
+      if (i > 0 && (i - 1) % nc == nc - 1) ok = drain((i - 1) / nc);
+    }
+    if (ok) ok = drain(grp - 1);
+    if (ok && !*abort_flag) {
+      const size_t o = ((size_t)bb * T + key0 + row) * (size_t)(a.KV * HD) + (size_t)kvh * HD;
+      float4 *pv = reinterpret_cast<float4 *>(a.dv + o);
+      float4 *pk = reinterpret_cast<float4 *>(a.dk + o);
+#pragma unroll
+      for (int e = 0; e < HD; e += 4) {
+        pv[e / 4] = make_float4(accv[e], accv[e + 1], accv[e + 2], accv[e + 3]);
+        pk[e / 4] = make_float4(acck[e], acck[e + 1], acck[e + 2], acck[e + 3]);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BW_TMEM_COLS) : "memory");
+  }
+}
+
 static PFN_cuTensorMapEncodeTiled_v12000 g_enc = nullptr;
 
 static int map2d(CUtensorMap *m, const float *p, uint64_t inner, uint64_t outer, uint32_t bx, uint32_t by,
@@ -614,7 +990,46 @@ int attn_bwd_dq_tc(DeviceCtx *c, const float *dsT, const float *k, float *dq, in
   return TL_OK;
 }
 
+// True when the tensor-core dK/dV kernel takes this shape (the forward's).
+bool attn_bwd_dkdv_tc_supported(const float *const *ptrs, int nptr, int T, int hd, int H, int KV) {
+  uintptr_t al = 0;
+  for (int i = 0; i < nptr; i++) al |= reinterpret_cast<uintptr_t>(ptrs[i]);
+  return T == atc::T && hd == atc::HD && (al & 15) == 0 && KV > 0 && H % KV == 0;
+}
+
+int attn_bwd_dkdv_tc(DeviceCtx *c, const float *q, const float *k, const float *v, const float *dout,
+                     const float *lse, const float *Drow, float *dsT, float *dk, float *dv, int B, int H, int KV) {
+  static bool attr[kMaxDevices] = {};
+  if (!attr[c->device]) {
+    TL_TRY_CUDA(cudaFuncSetAttribute(atc::attn_bwd_dkdv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     atc::BW_SMEM_BYTES));
+    attr[c->device] = true;
+  }
+  const int D = H * atc::HD, KD = KV * atc::HD;
+  const uint64_t rows = (uint64_t)B * atc::T;
+  CUtensorMap mkk, mvk, mqk, mok, mqm, mom;
+  int rc;
+  if ((rc = atc::map2d(&mkk, k, KD, rows, 32, atc::QR, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
+  if ((rc = atc::map2d(&mvk, v, KD, rows, 32, atc::QR, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
+  if ((rc = atc::map2d(&mqk, q, D, rows, 32, atc::BW_NQ, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
+  if ((rc = atc::map2d(&mok, dout, D, rows, 32, atc::BW_NQ, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
+  if ((rc = atc::map2d(&mqm, q, D, rows, 32, atc::BW_NQ, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))) return rc;
+  if ((rc = atc::map2d(&mom, dout, D, rows, 32, atc::BW_NQ, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))) return rc;
+  atc::BwArgs a;
+  a.lse = lse; a.Drow = Drow; a.dsT = dsT; a.dk = dk; a.dv = dv;
+  a.B = B; a.H = H; a.KV = KV;
+  a.scale = 1.0f / sqrtf((float)atc::HD);
+  a.err = c->err_flag;
+  TraceScope ts(c, "k_attn_bwd_dkdv_tc");
+  atc::attn_bwd_dkdv_tc_kernel<<<2 * B * KV, atc::BW_THREADS, atc::BW_SMEM_BYTES, c->stream>>>(mkk, mvk, mqk, mok,
+                                                                                               mqm, mom, a);
+  TL_TRY_CUDA(cudaGetLastError());
+  return TL_OK;
+}
+
 int attn_tc_prepare(DeviceCtx *c) {
+  TL_TRY_CUDA(cudaFuncSetAttribute(atc::attn_bwd_dkdv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   atc::BW_SMEM_BYTES));
   TL_TRY_CUDA(cudaFuncSetAttribute(atc::attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    atc::SMEM_BYTES));
   TL_TRY_CUDA(cudaFuncSetAttribute(atc::attn_bwd_dq_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
