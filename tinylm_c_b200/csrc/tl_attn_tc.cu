@@ -546,21 +546,29 @@ attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmS, const __grid_cons
 //        tiles (a second TMA copy, 32-byte atom swizzle), N = 64, K = 32; into
 //        the accumulator pair of the current head (two, alternating by head),
 //        which warps 6-9 add into fp32 registers once the head is done.
-// Warps 6-9 also write the lo parts of every staged tile.  Warp 0 is the TMA
-// producer, warp 1 the TMEM owner and MMA issuer.  Every wait is bounded.
-constexpr int BW_THREADS = 320;
+// The chunk tiles land in two raw buffers per kind (chunk i in buffer i % 2,
+// so the next chunk's copies are in flight while this one is used) and have
+// one lo buffer per kind, written once the previous chunk's products are
+// done with it.  Roles (384 threads): warp 0 lane 0 loads K, V and the
+// K-major tiles, lane 1 the MN-major tiles; warp 1 owns TMEM and issues the
+// MMAs; warps 2-5 P and dS; warps 6-9 the lo parts of K, V and the MN-major
+// tiles, and the per-head dV / dK sums; warps 10-11 the lo parts of the
+// K-major tiles.  Every wait is bounded.
+constexpr int BW_THREADS = 384;
 constexpr int BW_NQ = 32;                               // queries per chunk
 constexpr int BW_KTILE = QR * 32 * 4;                   // 16 KB: 128 keys x 32 of head_dim
 constexpr int BW_CTILE = BW_NQ * 32 * 4;                // 4 KB: 32 queries x 32 of head_dim
 constexpr int BW_OFF_K = 0, BW_OFF_V = 4 * BW_KTILE;    // raw (2 tiles), then lo (2 tiles): +32 KB
 constexpr int BW_KV_LO = 2 * BW_KTILE;
-constexpr int BW_OFF_QK = 8 * BW_KTILE;                 // chunk tiles: raw (2), then lo (2): +8 KB
-constexpr int BW_OFF_OK = BW_OFF_QK + 4 * BW_CTILE;
-constexpr int BW_OFF_QM = BW_OFF_OK + 4 * BW_CTILE;
-constexpr int BW_OFF_OM = BW_OFF_QM + 4 * BW_CTILE;
-constexpr int BW_C_LO = 2 * BW_CTILE;
-constexpr int BW_DATA = BW_OFF_OM + 4 * BW_CTILE;       // 192 KB
-constexpr int BW_NBARS = 17;
+// A chunk buffer: Q (2 tiles of 32 head_dim columns), then dO (2 tiles).
+constexpr int BW_CBUF = 4 * BW_CTILE;                   // 16 KB
+constexpr int BW_CB_O = 2 * BW_CTILE;                   // dO's offset in a chunk buffer
+constexpr int BW_OFF_KMR = 8 * BW_KTILE;                // K-major raw buffers 0, 1
+constexpr int BW_OFF_KML = BW_OFF_KMR + 2 * BW_CBUF;    // K-major lo
+constexpr int BW_OFF_MNR = BW_OFF_KML + BW_CBUF;        // MN-major raw buffers 0, 1
+constexpr int BW_OFF_MNL = BW_OFF_MNR + 2 * BW_CBUF;    // MN-major lo
+constexpr int BW_DATA = BW_OFF_MNL + BW_CBUF;           // 224 KB
+constexpr int BW_NBARS = 21;
 constexpr int BW_SMEM_BYTES = BW_DATA + 1024 + BW_NBARS * 8 + 16;
 static_assert(BW_SMEM_BYTES <= 232448, "dK/dV kernel exceeds the opt-in shared memory");
 // TMEM columns: S / P raw of buffer b at 64b, dP / dS raw at 64b + 32; their
@@ -638,8 +646,9 @@ attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmKk, const __grid_c
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
   const uint32_t base = smem_u32(smem);
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
-  constexpr int KV_FULL = 0, KV_READY = 1, KM_FULL = 2, KM_READY = 3, KM_EMPTY = 4, MN_FULL = 5, MN_READY = 6,
-                MN_EMPTY = 7, SD_FULL = 8, PD_READY = 10, ACC_FULL = 12, ACC_EMPTY = 14, FIN = 16;
+  // [2]: one per raw buffer or TMEM buffer
+  constexpr int KV_FULL = 0, KV_READY = 1, KM_FULL = 2, KM_READY = 4, KM_EMPTY = 5, MN_FULL = 7, MN_READY = 9,
+                MN_EMPTY = 10, SD_FULL = 12, PD_READY = 14, ACC_FULL = 16, ACC_EMPTY = 18, FIN = 20;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nbk = a.B * a.KV;
@@ -651,13 +660,13 @@ attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmKk, const __grid_c
   if (threadIdx.x == 0) {
     mbar_init(bar(KV_FULL), 1);
     mbar_init(bar(KV_READY), 4);
-    mbar_init(bar(KM_FULL), 1);
-    mbar_init(bar(KM_READY), 4);
-    mbar_init(bar(KM_EMPTY), 1);
-    mbar_init(bar(MN_FULL), 1);
+    mbar_init(bar(KM_READY), 2);
     mbar_init(bar(MN_READY), 4);
-    mbar_init(bar(MN_EMPTY), 1);
     for (int x = 0; x < 2; x++) {
+      mbar_init(bar(KM_FULL + x), 1);
+      mbar_init(bar(KM_EMPTY + x), 1);
+      mbar_init(bar(MN_FULL + x), 1);
+      mbar_init(bar(MN_EMPTY + x), 1);
       mbar_init(bar(SD_FULL + x), 1);
       mbar_init(bar(PD_READY + x), 4);
       mbar_init(bar(ACC_FULL + x), 1);
@@ -679,39 +688,44 @@ attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmKk, const __grid_c
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      const int krow = bb * T + key0;
-      mbar_arrive_expect_tx(bar(KV_FULL), 4 * BW_KTILE);
-      for (int x = 0; x < 2; x++) {
-        tma_load_2d(base + BW_OFF_K + x * BW_KTILE, &tmKk, bar(KV_FULL), kvh * HD + 32 * x, krow);
-        tma_load_2d(base + BW_OFF_V + x * BW_KTILE, &tmVk, bar(KV_FULL), kvh * HD + 32 * x, krow);
+    // ----------------------------------------------------------- producers
+    if (lane < 2) {
+      const bool mn = lane == 1;
+      const CUtensorMap *mq = mn ? &tmQm : &tmQk, *mo = mn ? &tmOm : &tmOk;
+      const int full = mn ? MN_FULL : KM_FULL, empty = mn ? MN_EMPTY : KM_EMPTY;
+      const uint32_t raw = base + (mn ? BW_OFF_MNR : BW_OFF_KMR);
+      if (!mn) {
+        const int krow = bb * T + key0;
+        mbar_arrive_expect_tx(bar(KV_FULL), 4 * BW_KTILE);
+        for (int x = 0; x < 2; x++) {
+          tma_load_2d(base + BW_OFF_K + x * BW_KTILE, &tmKk, bar(KV_FULL), kvh * HD + 32 * x, krow);
+          tma_load_2d(base + BW_OFF_V + x * BW_KTILE, &tmVk, bar(KV_FULL), kvh * HD + 32 * x, krow);
+        }
       }
-      int km = 0, mn = 0;
+      int issued = 0;
       for (int i = 0; i < n; i++) {
-        const int h = kvh * grp + i / nc, qrow = bb * T + BW_NQ * (c0 + i % nc);
-        if (i > 0 && !mbar_wait(bar(KM_EMPTY), (i - 1) & 1, abort_flag, a.err, 61)) break;
-        mbar_arrive_expect_tx(bar(KM_FULL), 4 * BW_CTILE);
+        const int r = i & 1, h = kvh * grp + i / nc, qrow = bb * T + BW_NQ * (c0 + i % nc);
+        // Raw buffer r was last read by the products of chunk i - 2.
+        if (i >= 2 && !mbar_wait(bar(empty + r), ((i - 2) >> 1) & 1, abort_flag, a.err, mn ? 62 : 61)) break;
+        mbar_arrive_expect_tx(bar(full + r), BW_CBUF);
+        const uint32_t dst = raw + r * BW_CBUF;
         for (int x = 0; x < 2; x++) {
-          tma_load_2d(base + BW_OFF_QK + x * BW_CTILE, &tmQk, bar(KM_FULL), h * HD + 32 * x, qrow);
-          tma_load_2d(base + BW_OFF_OK + x * BW_CTILE, &tmOk, bar(KM_FULL), h * HD + 32 * x, qrow);
+          tma_load_2d(dst + x * BW_CTILE, mq, bar(full + r), h * HD + 32 * x, qrow);
+          tma_load_2d(dst + BW_CB_O + x * BW_CTILE, mo, bar(full + r), h * HD + 32 * x, qrow);
         }
-        km = i + 1;
-        if (i > 0 && !mbar_wait(bar(MN_EMPTY), (i - 1) & 1, abort_flag, a.err, 62)) break;
-        mbar_arrive_expect_tx(bar(MN_FULL), 4 * BW_CTILE);
-        for (int x = 0; x < 2; x++) {
-          tma_load_2d(base + BW_OFF_QM + x * BW_CTILE, &tmQm, bar(MN_FULL), h * HD + 32 * x, qrow);
-          tma_load_2d(base + BW_OFF_OM + x * BW_CTILE, &tmOm, bar(MN_FULL), h * HD + 32 * x, qrow);
-        }
-        mn = i + 1;
+        issued = i + 1;
       }
-      // No copy may still be landing when the CTA exits (phases complete in
-      // order, so the last one issued on each barrier covers the rest).
-      const int last[3][2] = {{KV_FULL, 1}, {KM_FULL, km}, {MN_FULL, mn}};
-      for (int w = 0; w < 3; w++) {
-        if (last[w][1] == 0) continue;
+      // No copy may still be landing when the CTA exits (phases of one
+      // barrier complete in order, so the last one issued covers the rest).
+      for (int i = issued > 2 ? issued - 2 : 0; i < issued; i++) {
         const long long t0 = clock64();
-        while (!mbar_try_wait(bar(last[w][0]), (last[w][1] - 1) & 1)) {
+        while (!mbar_try_wait(bar(full + (i & 1)), (i >> 1) & 1)) {
+          if (clock64() - t0 > WAIT_LIMIT_CYCLES) { atomicExch(a.err, 63); break; }
+        }
+      }
+      if (!mn) {
+        const long long t0 = clock64();
+        while (!mbar_try_wait(bar(KV_FULL), 0)) {
           if (clock64() - t0 > WAIT_LIMIT_CYCLES) { atomicExch(a.err, 63); break; }
         }
       }
@@ -721,29 +735,30 @@ attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmKk, const __grid_c
     if (lane == 0) {
       auto issue_sd = [&](int i) -> bool {
         const int b = i & 1;
-        // Buffer b was last read by the dV/dK products of chunk i - 2.
-        if (i >= 2 && !mbar_wait(bar(MN_EMPTY), (i - 2) & 1, abort_flag, a.err, 64)) return false;
+        // TMEM buffer b was last read by the dV/dK products of chunk i - 2.
+        if (i >= 2 && !mbar_wait(bar(MN_EMPTY + b), ((i - 2) >> 1) & 1, abort_flag, a.err, 64)) return false;
         if (!mbar_wait(bar(KM_READY), i & 1, abort_flag, a.err, 65)) return false;
         tc_fence_after();
+        const uint32_t craw = base + BW_OFF_KMR + b * BW_CBUF, clo = base + BW_OFF_KML;
 #pragma unroll
         for (int m = 0; m < 2; m++) {            // m = 0: S^T = K Q^T, 1: dP^T = V dO^T
           const uint32_t d = tmem + 64 * b + 32 * m;
-          const uint32_t at = base + (m ? BW_OFF_V : BW_OFF_K), bt = base + (m ? BW_OFF_OK : BW_OFF_QK);
+          const uint32_t at = base + (m ? BW_OFF_V : BW_OFF_K), bo = m ? BW_CB_O : 0;
 #pragma unroll
           for (int x = 0; x < 2; x++) {
 #pragma unroll
             for (int kk = 0; kk < 4; kk++) {
               const uint64_t a_hi = smem_desc(at + x * BW_KTILE + kk * 32, 16, 1024, LAYOUT_SW128);
               const uint64_t a_lo = smem_desc(at + BW_KV_LO + x * BW_KTILE + kk * 32, 16, 1024, LAYOUT_SW128);
-              const uint64_t b_hi = smem_desc(bt + x * BW_CTILE + kk * 32, 16, 1024, LAYOUT_SW128);
-              const uint64_t b_lo = smem_desc(bt + BW_C_LO + x * BW_CTILE + kk * 32, 16, 1024, LAYOUT_SW128);
+              const uint64_t b_hi = smem_desc(craw + bo + x * BW_CTILE + kk * 32, 16, 1024, LAYOUT_SW128);
+              const uint64_t b_lo = smem_desc(clo + bo + x * BW_CTILE + kk * 32, 16, 1024, LAYOUT_SW128);
               tc_mma(d, a_lo, b_hi, BW_IDESC_SD, (x > 0 || kk > 0) ? 1u : 0u);
               tc_mma(d, a_hi, b_lo, BW_IDESC_SD, 1);
               tc_mma(d, a_hi, b_hi, BW_IDESC_SD, 1);
             }
           }
         }
-        tc_commit(bar(KM_EMPTY));
+        tc_commit(bar(KM_EMPTY + b));
         tc_commit(bar(SD_FULL + b));
         return true;
       };
@@ -755,21 +770,22 @@ attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmKk, const __grid_c
         if (!mbar_wait(bar(PD_READY + b), (i >> 1) & 1, abort_flag, a.err, 67)) return false;
         if (!mbar_wait(bar(MN_READY), i & 1, abort_flag, a.err, 68)) return false;
         tc_fence_after();
+        const uint32_t craw = base + BW_OFF_MNR + b * BW_CBUF, clo = base + BW_OFF_MNL;
 #pragma unroll
         for (int m = 0; m < 2; m++) {            // m = 0: dV += P^T dO, 1: dK += dS^T Q
           const uint32_t d = tmem + 256 + 128 * pa + 64 * m;
           const uint32_t a_hi = tmem + 64 * b + 32 * m, a_lo = a_hi + 128;
-          const uint32_t bt = base + (m ? BW_OFF_QM : BW_OFF_OM);
+          const uint32_t bo = m ? 0 : BW_CB_O;
 #pragma unroll
           for (int kk = 0; kk < BW_NQ / 8; kk++) {
-            const uint64_t b_hi = smem_desc(bt + kk * 1024, 4096, 512, LAYOUT_SW128_BASE32B);
-            const uint64_t b_lo = smem_desc(bt + BW_C_LO + kk * 1024, 4096, 512, LAYOUT_SW128_BASE32B);
+            const uint64_t b_hi = smem_desc(craw + bo + kk * 1024, 4096, 512, LAYOUT_SW128_BASE32B);
+            const uint64_t b_lo = smem_desc(clo + bo + kk * 1024, 4096, 512, LAYOUT_SW128_BASE32B);
             tc_mma_tmem_a(d, a_lo + kk * 8, b_hi, BW_IDESC_ACC, (!first || kk > 0) ? 1u : 0u);
             tc_mma_tmem_a(d, a_hi + kk * 8, b_lo, BW_IDESC_ACC, 1);
             tc_mma_tmem_a(d, a_hi + kk * 8, b_hi, BW_IDESC_ACC, 1);
           }
         }
-        tc_commit(bar(MN_EMPTY));
+        tc_commit(bar(MN_EMPTY + b));
         if (last) tc_commit(bar(ACC_FULL + pa));
         return true;
       };
@@ -801,7 +817,7 @@ attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmKk, const __grid_c
       tmem_ld32(tmem + lane_addr + 64 * b + 32, dv);
       const float4 *lp = reinterpret_cast<const float4 *>(a.lse + bh * T + q0);
       const float4 *dp = reinterpret_cast<const float4 *>(a.Drow + bh * T + q0);
-      // In place: sv becomes P, dv becomes dS; lo parts through one buffer.
+      // P and dS; lo parts through one buffer.
       float ph[32], dh[32], lo[32];
 #pragma unroll
       for (int e4 = 0; e4 < 8; e4++) {
@@ -831,8 +847,23 @@ attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmKk, const __grid_c
 #pragma unroll
       for (int e = 0; e < 32; e += 4) dst[e / 4] = make_float4(dh[e], dh[e + 1], dh[e + 2], dh[e + 3]);
     }
+  } else if (warp >= 10) {
+    // ------------------------------------------- lo parts of K-major tiles
+    const int t = threadIdx.x - 320;             // 0..63
+    for (int i = 0; i < n; i++) {
+      const int r = i & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(bar(KM_FULL + r), (i >> 1) & 1, abort_flag, a.err, 74))) break;
+      // The lo buffer is free once the previous chunk's S^T / dP^T are done.
+      if (i >= 1 && !__all_sync(0xffffffffu, mbar_wait(bar(KM_EMPTY + (r ^ 1)), ((i - 1) >> 1) & 1, abort_flag,
+                                                        a.err, 76)))
+        break;
+      split_lo(smem + BW_OFF_KMR + r * BW_CBUF, BW_OFF_KML - (BW_OFF_KMR + r * BW_CBUF), BW_CBUF / 16, t, 64);
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(KM_READY));
+    }
   } else {
-    // ---------------------- lo parts of the staged tiles; dV / dK per head
+    // ------- lo parts of K, V and the MN-major tiles; dV / dK per head
     const int t = threadIdx.x - 192, q4 = warp & 3, row = q4 * 32 + lane;
     const uint32_t lane_addr = (uint32_t)(q4 * 32) << 16;
     float accv[HD], acck[HD];
@@ -869,20 +900,18 @@ attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmKk, const __grid_c
       return true;
     };
     for (int i = 0; i < n && ok; i++) {
-      if (!(ok = __all_sync(0xffffffffu, mbar_wait(bar(KM_FULL), i & 1, abort_flag, a.err, 74)))) break;
-      split_lo(smem + BW_OFF_QK, BW_C_LO, 2 * BW_CTILE / 16, t, 128);
-      split_lo(smem + BW_OFF_OK, BW_C_LO, 2 * BW_CTILE / 16, t, 128);
-      fence_proxy_async();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(KM_READY));
-      if (!(ok = __all_sync(0xffffffffu, mbar_wait(bar(MN_FULL), i & 1, abort_flag, a.err, 75)))) break;
-      split_lo(smem + BW_OFF_QM, BW_C_LO, 2 * BW_CTILE / 16, t, 128);
-      split_lo(smem + BW_OFF_OM, BW_C_LO, 2 * BW_CTILE / 16, t, 128);
+      const int r = i & 1;
+      if (!(ok = __all_sync(0xffffffffu, mbar_wait(bar(MN_FULL + r), (i >> 1) & 1, abort_flag, a.err, 75)))) break;
+      // The lo buffer is free once the previous chunk's dV / dK are done.
+      if (i >= 1 && !(ok = __all_sync(0xffffffffu, mbar_wait(bar(MN_EMPTY + (r ^ 1)), ((i - 1) >> 1) & 1,
+                                                              abort_flag, a.err, 77))))
+        break;
+      split_lo(smem + BW_OFF_MNR + r * BW_CBUF, BW_OFF_MNL - (BW_OFF_MNR + r * BW_CBUF), BW_CBUF / 16, t, 128);
       fence_proxy_async();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(MN_READY));
-      // The previous head's accumulators, once this chunk's tiles are ready
-      // (the issuer needs them before it finishes that head).
+      // The previous head's accumulators (its last products are done: the
+      // lo buffer wait above covered them).
       if (i > 0 && (i - 1) % nc == nc - 1) ok = drain((i - 1) / nc);
     }
     if (ok) ok = drain(grp - 1);
