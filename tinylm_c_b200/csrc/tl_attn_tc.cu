@@ -807,29 +807,31 @@ attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmKk, const __grid_c
     // ------------------------------------------ P^T and dS^T (a key row each)
     const int q4 = warp & 3, row = q4 * 32 + lane, key = key0 + row;
     const uint32_t lane_addr = (uint32_t)(q4 * 32) << 16;
+    // The chunk's 32 lse and D values, one per lane, loaded a chunk ahead and
+    // broadcast by shuffles.
+    auto chunk_row = [&](int i) { return ((size_t)bb * a.H + kvh * grp + i / nc) * T + BW_NQ * (c0 + i % nc); };
+    float l_nx = __ldg(a.lse + chunk_row(0) + lane), d_nx = __ldg(a.Drow + chunk_row(0) + lane);
     for (int i = 0; i < n; i++) {
-      const int b = i & 1, h = kvh * grp + i / nc, q0 = BW_NQ * (c0 + i % nc);
-      const size_t bh = (size_t)bb * a.H + h;
+      const int b = i & 1, q0 = BW_NQ * (c0 + i % nc);
+      const size_t crow = chunk_row(i);
+      const float l_me = l_nx, d_me = d_nx;
+      if (i + 1 < n) {
+        l_nx = __ldg(a.lse + chunk_row(i + 1) + lane);
+        d_nx = __ldg(a.Drow + chunk_row(i + 1) + lane);
+      }
       if (!__all_sync(0xffffffffu, mbar_wait(bar(SD_FULL + b), (i >> 1) & 1, abort_flag, a.err, 71))) break;
       tc_fence_after();
       uint32_t sv[32], dv[32];
       tmem_ld32(tmem + lane_addr + 64 * b, sv);
       tmem_ld32(tmem + lane_addr + 64 * b + 32, dv);
-      const float4 *lp = reinterpret_cast<const float4 *>(a.lse + bh * T + q0);
-      const float4 *dp = reinterpret_cast<const float4 *>(a.Drow + bh * T + q0);
       // P and dS; lo parts through one buffer.
       float ph[32], dh[32], lo[32];
 #pragma unroll
-      for (int e4 = 0; e4 < 8; e4++) {
-        const float4 l4 = __ldg(lp + e4), d4 = __ldg(dp + e4);
-        const float ls[4] = {l4.x, l4.y, l4.z, l4.w}, ds[4] = {d4.x, d4.y, d4.z, d4.w};
-#pragma unroll
-        for (int u = 0; u < 4; u++) {
-          const int e = 4 * e4 + u;
-          const float pr = key <= q0 + e ? expf(__uint_as_float(sv[e]) * a.scale - ls[u]) : 0.0f;
-          ph[e] = pr;
-          dh[e] = pr * (__uint_as_float(dv[e]) - ds[u]) * a.scale;
-        }
+      for (int e = 0; e < 32; e++) {
+        const float ls = __shfl_sync(0xffffffffu, l_me, e), ds = __shfl_sync(0xffffffffu, d_me, e);
+        const float pr = key <= q0 + e ? expf(__uint_as_float(sv[e]) * a.scale - ls) : 0.0f;
+        ph[e] = pr;
+        dh[e] = pr * (__uint_as_float(dv[e]) - ds) * a.scale;
       }
       tmem_st32(tmem + lane_addr + 64 * b, ph);
       tmem_st32(tmem + lane_addr + 64 * b + 32, dh);
@@ -843,7 +845,8 @@ attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmKk, const __grid_c
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(PD_READY + b));
-      float4 *dst = reinterpret_cast<float4 *>(a.dsT + (bh * T + key) * T + q0);
+      // crow = (bh * T + q0): the scratch row of this key is bh * T + key.
+      float4 *dst = reinterpret_cast<float4 *>(a.dsT + (crow - q0 + key) * T + q0);
 #pragma unroll
       for (int e = 0; e < 32; e += 4) dst[e / 4] = make_float4(dh[e], dh[e + 1], dh[e + 2], dh[e + 3]);
     }
