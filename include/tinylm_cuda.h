@@ -104,12 +104,14 @@ int tl_matmul_bt_sum(float *dX, int nprod, const float *const *dY, const float *
 /* GEMM engine selection, for tests and benchmarks: 0 = automatic (tensor-core
  * 3xTF32 where the shape allows, else CUDA-core fp32), 1 = CUDA-core fp32 only,
  * 2 = tensor-core 3xTF32, one CTA per 128 x 128 tile, 3 = tensor-core 3xTF32,
- * a CTA pair (two SMs, cta_group::2) per 256 x 256 tile (2 and 3: TL_EINVAL
+ * a CTA pair (two SMs, cta_group::2) per 256 x 256 tile, 4 = the CTA pair with
+ * each operand scaled by a power of two and split into fp16 hi + lo (fp16
+ * MMAs at twice the tf32 rate, at least the same accuracy) (2-4: TL_EINVAL
  * where the shape does not allow the tensor-core engine).
  * No counterpart in the reference (its only engine switch is USE_BLAS,
  * tinylm.c:29-31). */
 int tl_set_gemm_engine(int engine);
-/* Engine the last GEMM call on this thread ran on (1, 2 or 3), 0 if none. */
+/* Engine the last GEMM call on this thread ran on (1 to 4), 0 if none. */
 int tl_last_gemm_engine(void);
 
 /* -------------------------------------------------------------- optimizer */

@@ -98,7 +98,7 @@ def test_gemm_rejects_host_memory(cuda):
         ops.mm(torch.zeros(4, device=cuda), X.ctypes.data, X.ctypes.data, 2, 2, 2)
 
 
-TC_ENGINES = {"tc_1cta": 2, "tc_pair": 3}
+TC_ENGINES = {"tc_1cta": 2, "tc_pair": 3, "tc_pair_f16": 4}
 
 
 @pytest.mark.parametrize("tc_engine", list(TC_ENGINES))
@@ -139,7 +139,7 @@ def test_tensor_core_engine_forced(cuda, tc_engine, M, K, N):
     assert gemm_rel(dW.cpu().numpy(), dW64) <= GEMM_REL_TOL
 
 
-@pytest.mark.parametrize("eng", [0, 1, 3])
+@pytest.mark.parametrize("eng", [0, 1, 3, 4])
 @pytest.mark.parametrize("M,K,Ns", [(512, 384, (96, 40, 72)), (300, 260, (256, 512)), (256, 256, (2048, 1024, 1024)),
                                     (100, 64, (64, 64, 64)), (384, 256, (64, 0, 32)), (257, 1024, (2816,))])
 def test_mm_bt_sum(cuda, eng, M, K, Ns):
@@ -160,12 +160,56 @@ def test_mm_bt_sum(cuda, eng, M, K, Ns):
         device_ok()
     finally:
         ops.set_gemm_engine(0)
-    if eng == 3 or (eng == 0 and M > 128 and K > 128):
-        assert last == 3
+    if eng in (3, 4):
+        assert last == eng
+    elif eng == 0 and M > 128 and K > 128:
+        assert last in (3, 4)
     want = np.zeros((M, K))
     for a, w, n in zip(dYs, Ws, Ns):
         want += a.astype(np.float64).reshape(M, n) @ w.astype(np.float64).reshape(K, n).T
     assert gemm_rel(dX.cpu().numpy(), want.ravel()) <= GEMM_REL_TOL
+
+
+@pytest.mark.parametrize("sa,sb", [(1e5, 1e-7), (1e-20, 1e15), (3e4, 3e4), (0.0, 1.0)])
+def test_f16_split_operand_scales(cuda, sa, sb):
+    """The fp16-split pair kernel scales each operand by a power of two from
+    its max |x|: operands far outside fp16's range, tiny ones, a product
+    whose scales differ by 2^90, and an all-zero operand keep the 1e-4
+    bound, on all three primitives and on a summed mm_bt whose products have
+    different magnitudes."""
+    M, K, N = 384, 320, 288
+    rng = np.random.default_rng(7)
+    X = (rng.standard_normal(M * K) * sa).astype(np.float32)
+    W = (rng.standard_normal(K * N) * sb).astype(np.float32)
+    dY = (rng.standard_normal(M * N) * sb).astype(np.float32)
+    Y = torch.full((M * N,), float("nan"), device=cuda)
+    dX, dW = torch.zeros(M * K, device=cuda), torch.zeros(K * N, device=cuda)
+    W2 = (rng.standard_normal(K * 64) * sa).astype(np.float32)
+    dY2 = (rng.standard_normal(M * 64)).astype(np.float32)
+    dXs = torch.full((M * K,), float("nan"), device=cuda)
+    ops.set_gemm_engine(4)
+    try:
+        ops.mm(Y, dev(X, cuda), dev(W, cuda), M, K, N)
+        ops.mm_bt(dX, dev(dY, cuda), dev(W, cuda), M, K, N)
+        ops.mm_atb(dW, dev(X, cuda), dev(dY, cuda), M, K, N)
+        ops.mm_bt_sum(dXs, [dev(dY, cuda), dev(dY2, cuda)], [dev(W, cuda), dev(W2, cuda)], [N, 64], M, K)
+        torch.cuda.synchronize()
+        device_ok()
+    finally:
+        ops.set_gemm_engine(0)
+    Xd, Wd, dYd = (a.astype(np.float64) for a in (X, W, dY))
+    checks = [(Y, (Xd.reshape(M, K) @ Wd.reshape(K, N)).ravel()),
+              (dX, (dYd.reshape(M, N) @ Wd.reshape(K, N).T).ravel()),
+              (dW, (Xd.reshape(M, K).T @ dYd.reshape(M, N)).ravel()),
+              (dXs, (dYd.reshape(M, N) @ Wd.reshape(K, N).T
+                     + dY2.astype(np.float64).reshape(M, 64) @ W2.astype(np.float64).reshape(K, 64).T).ravel())]
+    for got, want in checks:
+        g = got.cpu().numpy()
+        assert np.isfinite(g).all()
+        if not np.any(want):
+            assert not np.any(g)
+        else:
+            assert gemm_rel(g, want) <= GEMM_REL_TOL
 
 
 def test_mm_bt_sum_rejects_bad_args(cuda):

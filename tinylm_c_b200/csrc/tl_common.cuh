@@ -29,6 +29,7 @@ struct DeviceCtx {
   int *err_flag = nullptr;             // device error word set by bounded waits
   float *gemm_ws = nullptr;            // split-K partial outputs
   size_t gemm_ws_floats = 0;
+  unsigned *gemm_amax = nullptr;       // [8] operand max |x| (float bits) for the fp16-split GEMM
 };
 constexpr size_t kGemmWorkspaceFloats = 16u << 20;  // 64 MiB
 

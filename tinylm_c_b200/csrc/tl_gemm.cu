@@ -3,7 +3,11 @@
 
 namespace tl {
 
-static thread_local int g_engine_pref = 0;   // 0 auto, 1 CUDA-core, 2 tensor-core, 3 tensor-core pair
+// 0 auto, 1 CUDA-core, 2 tensor-core, 3 tensor-core pair (tf32 split),
+// 4 tensor-core pair (fp16 split)
+static thread_local int g_engine_pref = 0;
+// The split the automatic choice gives the pair kernel.
+static constexpr bool kAutoF16 = false;
 static thread_local int g_engine_last = 0;
 
 static int gemm_entry(GemmOp op, float *C, const float *A, const float *B, int M, int K, int N,
@@ -51,9 +55,10 @@ int tl::gemm_run_add(DeviceCtx *c, GemmOp op, float *C, const float *A, const fl
   if (g_engine_pref >= 2 && !tc_ok)
     return set_error(TL_EINVAL, "tensor-core engine forced but shape/alignment unsupported (M=%d K=%d N=%d)", M, K, N);
   if (tc_ok && g_engine_pref != 1) {
-    const bool pair = g_engine_pref == 3 || (g_engine_pref == 0 && gemm_tc_prefer_pair(I, J, R));
-    g_engine_last = pair ? 3 : 2;
-    return gemm_tc(c, op, C, A, B, M, K, N, pair, add);
+    const bool pair = g_engine_pref >= 3 || (g_engine_pref == 0 && gemm_tc_prefer_pair(I, J, R));
+    const bool f16 = pair && (g_engine_pref == 4 || (g_engine_pref == 0 && kAutoF16));
+    g_engine_last = f16 ? 4 : pair ? 3 : 2;
+    return gemm_tc(c, op, C, A, B, M, K, N, pair, add, f16);
   }
   g_engine_last = 1;
   return gemm_simt(c, op, C, A, B, M, K, N, add);
@@ -61,13 +66,14 @@ int tl::gemm_run_add(DeviceCtx *c, GemmOp op, float *C, const float *A, const fl
 
 int tl::gemm_run_nt_sum(DeviceCtx *c, float *C, int nprod, const float *const *A, const float *const *B,
                         const int *N, int M, int K) {
-  bool fused = nprod >= 1 && nprod <= 3 && M > 0 && K > 0 && (g_engine_pref == 0 || g_engine_pref == 3);
+  bool fused = nprod >= 1 && nprod <= 3 && M > 0 && K > 0 && (g_engine_pref == 0 || g_engine_pref >= 3);
   for (int t = 0; fused && t < nprod; t++)
     fused = N[t] > 0 && gemm_tc_supported(GemmOp::NT, C, A[t], B[t], M, K, N[t]) &&
-            (g_engine_pref == 3 || gemm_tc_prefer_pair(M, K, N[t]));
+            (g_engine_pref >= 3 || gemm_tc_prefer_pair(M, K, N[t]));
   if (fused) {
-    g_engine_last = 3;
-    return gemm_tc_nt_sum(c, C, nprod, A, B, N, M, K);
+    const bool f16 = g_engine_pref == 4 || (g_engine_pref == 0 && kAutoF16);
+    g_engine_last = f16 ? 4 : 3;
+    return gemm_tc_nt_sum(c, C, nprod, A, B, N, M, K, f16);
   }
   for (int t = 0; t < nprod; t++) {
     const int rc = gemm_run_add(c, GemmOp::NT, C, A[t], B[t], M, K, N[t], t == 0 ? nullptr : C);
@@ -116,7 +122,7 @@ TL_API int tl_matmul_bt_sum(float *dX, int nprod, const float *const *dY, const 
   return gemm_run_nt_sum(c, dX, n, As, Bs, Ns, M, K);
 }
 TL_API int tl_set_gemm_engine(int engine) {
-  if (engine < 0 || engine > 3) return set_error(TL_EINVAL, "engine must be 0, 1, 2 or 3");
+  if (engine < 0 || engine > 4) return set_error(TL_EINVAL, "engine must be 0, 1, 2, 3 or 4");
   g_engine_pref = engine;
   return TL_OK;
 }

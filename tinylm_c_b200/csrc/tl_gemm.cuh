@@ -38,15 +38,16 @@ bool gemm_tc_prefer_pair(int I, int J, int R);
 // Host-side set-up of every tensor-core kernel (before a CUDA graph capture).
 int gemm_tc_prepare(DeviceCtx *c);
 // pair: the CTA-pair kernel (256 x 256 tiles over two SMs) instead of the
-// one-CTA kernel (128 x 128 tiles).
+// one-CTA kernel (128 x 128 tiles); f16 (pair only): operands split into
+// scaled fp16 hi/lo parts instead of tf32 hi/lo.
 int gemm_tc(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, int M, int K, int N, bool pair,
-            const float *add);
+            const float *add, bool f16);
 
 // C[M,K] = sum over t < nprod (<= 3) of A_t[M,N_t] @ B_t[K,N_t]^T, one
 // CTA-pair launch whose reduction walks the products' k-blocks in turn
 // (overwrites C).
 int gemm_tc_nt_sum(DeviceCtx *c, float *C, int nprod, const float *const *A, const float *const *B, const int *N,
-                   int M, int K);
+                   int M, int K, bool f16);
 // The same sum through the engine choice: one launch when the pair kernel
 // would take every product, else one NT GEMM per product accumulating in turn.
 int gemm_run_nt_sum(DeviceCtx *c, float *C, int nprod, const float *const *A, const float *const *B, const int *N,

@@ -39,6 +39,7 @@
 // memory bytes the tensor pipe reads per flop -- the limit of the one-CTA
 // kernel -- and is the default wherever both output sides exceed 128.
 #include <cuda.h>
+#include <cuda_fp16.h>
 #include <algorithm>
 #include <cudaTypedefs.h>
 #include "tl_gemm.cuh"
@@ -75,6 +76,9 @@ struct Params {
   // products summed into one output; INT_MAX when there is one).
   int seg_end0, seg_end1;
   size_t split_stride;   // floats between the partial outputs of consecutive splits
+  // Pair kernel, fp16 split: max |x| (float bits) of A and B of each product,
+  // [A0, B0, A1, B1, A2, B2].
+  const unsigned *amax;
   int *err;
 };
 
@@ -377,7 +381,30 @@ __host__ __device__ constexpr uint32_t make_idesc_pair(bool a_mn, bool b_mn) {
          ((uint32_t)(PN >> 3) << 17) | ((uint32_t)(PM >> 4) << 24);
 }
 
-template <bool A_MN, bool B_MN>
+// The fp16 split (F16): instead of tf32 hi/lo, each operand is scaled by a
+// power of two (so its largest |x| lies in [2^14, 2^15)) and split into fp16
+// hi = x with its low 13 significand bits cleared (exact in fp16) and
+// lo = rn(x - hi): 11 + 11 significand bits, the accuracy of the tf32 pair,
+// and fp16 MMAs (kind::f16, K = 16) run at twice the tf32 rate.  The split warps write both parts into the lo ring, which then
+// holds the MMA operands: a K-major tile as 128-byte rows [hi 32 | lo 32], an
+// MN-major tile as an hi plane and a lo plane (64 MN elements per 128-byte row,
+// 8-row groups 1 KB apart, 64-element MN blocks 4 KB apart); the raw slot is
+// free once converted.  The epilogue multiplies by the inverse of the product
+// scale (exact).  Products summed into one output share one product scale.
+__host__ __device__ constexpr uint32_t make_idesc_pair_f16(bool a_mn, bool b_mn) {
+  return (1u << 4) | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) | ((uint32_t)(PN >> 3) << 17) |
+         ((uint32_t)(PM >> 4) << 24);
+}
+__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
+// Binary exponent of a max |x| (float bits), limited to +-100 (0 for zero;
+// non-finite and subnormal maxima land on the limits).
+__device__ __forceinline__ int amax_exp(unsigned bits) {
+  return bits == 0 ? 0 : max(-100, min(100, (int)((bits & 0x7fffffffu) >> 23) - 127));
+}
+__device__ __forceinline__ float exp2i(int k) { return __uint_as_float((uint32_t)(k + 127) << 23); }
+
+
+template <bool A_MN, bool B_MN, bool F16>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
 gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmA1, const __grid_constant__ CUtensorMap tmB1,
@@ -393,6 +420,9 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
   constexpr int NBARS = 2 * RAW_STAGES + 2 * LO_STAGES + 4;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + NBARS);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+  // F16: scales of A and B of each product [A0, B0, A1, B1, A2, B2], then the
+  // inverse product scale
+  float *scl = reinterpret_cast<float *>(tmem_slot + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
@@ -423,7 +453,7 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
   if (threadIdx.x == 0) {
     for (int s = 0; s < RAW_STAGES; s++) {
       mbar_init(bar_full(s), 1);
-      mbar_init(bar_rempty(s), 1);
+      mbar_init(bar_rempty(s), F16 ? 8 : 1);   // F16: this CTA's split warps, else the pair's MMAs
     }
     for (int s = 0; s < LO_STAGES; s++) {
       mbar_init(bar_ready(s), PAIR_SIGNALLERS);
@@ -434,6 +464,26 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
       mbar_init(bar_acce(b), PAIR_SIGNALLERS);
     }
     *abort_flag = 0;
+    if (F16) {
+      // Operand scale 2^(14 - e), e = exponent of its max |x|; the products
+      // share the smallest product scale 2^P (A's scale lowered to match).
+      // (P is kept inside the float exponent range; outside it the fp32
+      // result over- or underflows as well.)
+      const int nprod = p.seg_end1 != 0x7fffffff ? 3 : (p.seg_end0 != 0x7fffffff ? 2 : 1);
+      int P = 1 << 20;
+#pragma unroll
+      for (int t = 0; t < 3; t++)
+        if (t < nprod) P = min(P, 28 - amax_exp(p.amax[2 * t]) - amax_exp(p.amax[2 * t + 1]));
+      P = max(-126, min(126, P));
+#pragma unroll
+      for (int t = 0; t < 3; t++) {
+        const int sb = t < nprod ? 14 - amax_exp(p.amax[2 * t + 1]) : 0;
+        const int ea = t < nprod ? max(P - sb, -126) : 0;
+        scl[2 * t] = exp2i(ea);
+        scl[2 * t + 1] = t < nprod ? exp2i(P - ea) : 1.0f;
+      }
+      scl[6] = exp2i(-P);
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
@@ -501,6 +551,28 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         tc_fence_after();
         const uint32_t hi = raw_base + rs * RAW_BYTES, lo = lo_base + ls * RAW_BYTES;
         const uint32_t d = tmem + b * PN;
+        if constexpr (F16) {
+          constexpr uint32_t idesc16 = make_idesc_pair_f16(A_MN, B_MN);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; kk++) {
+            // K-major: hi at 32 bytes per K = 16 step, lo 64 bytes further;
+            // MN-major: planes 8 KB apart, 2 KB (16 K rows) per step.
+            uint64_t op[2][2];   // [A, B][hi, lo]
+#pragma unroll
+            for (int w = 0; w < 2; w++) {
+              const bool mn = w ? B_MN : A_MN;
+              const uint32_t t0 = lo + (w ? TILE_A : 0);
+              op[w][0] = mn ? smem_desc(t0 + kk * 2048, 4096, 1024, LAYOUT_SW128)
+                            : smem_desc(t0 + kk * 32, 16, 1024, LAYOUT_SW128);
+              op[w][1] = mn ? smem_desc(t0 + 8192 + kk * 2048, 4096, 1024, LAYOUT_SW128)
+                            : smem_desc(t0 + 64 + kk * 32, 16, 1024, LAYOUT_SW128);
+            }
+            tc_mma_pair_f16(d, op[0][1], op[1][0], idesc16, (kin > 0 || kk > 0) ? 1u : 0u);
+            tc_mma_pair_f16(d, op[0][0], op[1][1], idesc16, 1);
+            tc_mma_pair_f16(d, op[0][0], op[1][0], idesc16, 1);
+          }
+          tc_commit_pair(bar_lempty(ls));
+        } else {
 #pragma unroll
         for (int kk = 0; kk < BK / 8; kk++) {
           const uint32_t a_off = A_MN ? kk * 1024 : kk * 32;
@@ -519,6 +591,7 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         }
         tc_commit_pair(bar_lempty(ls));
         tc_commit_pair(bar_rempty(rs));
+        }
         if (++kin == PAIR_CHUNK_KB || kb == nk - 1) {
           tc_commit_pair(bar_accf(b));
           last_committed = chunk;
@@ -597,25 +670,79 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         if (!__all_sync(0xffffffffu, landed)) { ok = false; break; }
         const uint8_t *src = raw_ring + rs * RAW_BYTES;
         uint8_t *dst = lo_ring + ls * RAW_BYTES;
-        // A tile then this CTA's B half: 2048 float4 of raw data, 8 per thread;
-        // lo lands at the same offset of the lo slot (same swizzled layout).
+        if constexpr (F16) {
+          const int kg = kb0 + kb;
+          const int tp = kg >= p.seg_end1 ? 2 : (kg >= p.seg_end0 ? 1 : 0);
+          // Warps 2-5 convert the A tile, 6-9 this CTA's B half: one raw
+          // 128-byte row (32 values) per thread, written as 16-byte chunks.
+          const bool is_a = t < 128, mn = is_a ? A_MN : B_MN;
+          const int tt = t & 127;
+          const float sc = scl[2 * tp + (is_a ? 0 : 1)];
+          const uint8_t *sb = src + (is_a ? 0 : TILE_A);
+          uint8_t *db = dst + (is_a ? 0 : TILE_A);
+          // Raw row and its swizzle: K-major row r = tt (chunk c at c ^ (r % 8));
+          // MN-major box tt / 32, K row k = tt % 32 (chunk c at c ^ ((k % 4) * 2)).
+          const int k = tt & 31;
+          const int rbase = mn ? (tt >> 5) * 4096 + k * 128 : tt * 128;
+          const int rxor = mn ? (k & 3) << 1 : (tt & 7);
 #pragma unroll
-        for (int e = 0; e < 8; e++) {
-          const int off = (e * 256 + t) * 16;
-          const float4 x = *reinterpret_cast<const float4 *>(src + off);
-          float4 lo;
-          lo.x = x.x - tf32_trunc(x.x); lo.y = x.y - tf32_trunc(x.y);
-          lo.z = x.z - tf32_trunc(x.z); lo.w = x.w - tf32_trunc(x.w);
-          *reinterpret_cast<float4 *>(dst + off) = lo;
+          for (int j = 0; j < 4; j++) {
+            // fp16 chunk j of hi (and of lo): raw chunks 2j and 2j + 1
+            uint32_t hw[4], lw[4];
+#pragma unroll
+            for (int u = 0; u < 2; u++) {
+              const float4 x = *reinterpret_cast<const float4 *>(sb + rbase + (((2 * j + u) ^ rxor) << 4));
+              // hi = the scaled value with its low 13 significand bits cleared
+              // (11 bits: exact in fp16), lo = the rest (exact in fp32).
+              const float v0 = x.x * sc, v1 = x.y * sc, v2 = x.z * sc, v3 = x.w * sc;
+              const float h0 = tf32_trunc(v0), h1 = tf32_trunc(v1), h2 = tf32_trunc(v2), h3 = tf32_trunc(v3);
+              hw[2 * u] = h2_bits(__floats2half2_rn(h0, h1));
+              hw[2 * u + 1] = h2_bits(__floats2half2_rn(h2, h3));
+              lw[2 * u] = h2_bits(__floats2half2_rn(v0 - h0, v1 - h1));
+              lw[2 * u + 1] = h2_bits(__floats2half2_rn(v2 - h2, v3 - h3));
+            }
+            int hoff, loff;
+            if (!mn) {
+              // packed row r: hi chunks 0-3, lo chunks 4-7, chunk at c ^ (r % 8)
+              hoff = tt * 128 + ((j ^ (tt & 7)) << 4);
+              loff = tt * 128 + (((4 + j) ^ (tt & 7)) << 4);
+            } else {
+              // MN elements 32 * (tt / 32) + 8j.. of K row k: block (tt / 64),
+              // chunk 4 * ((tt / 32) % 2) + j of the row, at chunk ^ (k % 8)
+              const int blk = tt >> 6, ch = 4 * ((tt >> 5) & 1) + j;
+              hoff = blk * 4096 + (k >> 3) * 1024 + (k & 7) * 128 + ((ch ^ (k & 7)) << 4);
+              loff = hoff + 8192;
+            }
+            *reinterpret_cast<uint4 *>(db + hoff) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+            *reinterpret_cast<uint4 *>(db + loff) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+          }
+        } else {
+          // A tile then this CTA's B half: 2048 float4 of raw data, 8 per
+          // thread; lo lands at the same offset of the lo slot (same layout).
+#pragma unroll
+          for (int e = 0; e < 8; e++) {
+            const int off = (e * 256 + t) * 16;
+            const float4 x = *reinterpret_cast<const float4 *>(src + off);
+            float4 lo;
+            lo.x = x.x - tf32_trunc(x.x); lo.y = x.y - tf32_trunc(x.y);
+            lo.z = x.z - tf32_trunc(x.z); lo.w = x.w - tf32_trunc(x.w);
+            *reinterpret_cast<float4 *>(dst + off) = lo;
+          }
         }
         // Every writer orders its stores before the tensor pipe's reads.
         fence_proxy_async();
         __syncwarp();
         if (lane == 0) mbar_arrive_remote(cluster_map(bar_ready(ls), 0));
+        if (F16 && lane == 0) mbar_arrive(bar_rempty(rs));   // the raw slot is converted
         kb++;
       }
     }
     if (ok && !*abort_flag) {
+      if (F16) {
+        const float inv = scl[6];
+#pragma unroll
+        for (int e = 0; e < BN; e++) acc[e] *= inv;
+      }
       const int row = i0 + q * 32 + lane;
       const int jc = j0 + h * BN;
       if (row < p.I) {
@@ -668,6 +795,40 @@ static int make_map(CUtensorMap *m, const float *ptr, uint64_t inner, uint64_t o
   return TL_OK;
 }
 
+// Largest |x| over up to six arrays (blockIdx.y picks one), as float bits in
+// out[y], which is zero beforehand: non-negative floats order like unsigned
+// integers, so atomicMax gives the same bits in any order.  NaN bits exceed
+// infinity's and propagate as "not finite".
+struct AmaxArgs {
+  const float *p[6];
+  size_t n[6];
+};
+__global__ void absmax_kernel(AmaxArgs a, unsigned *out) {
+  const float *x = a.p[blockIdx.y];
+  const size_t n = a.n[blockIdx.y];
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  const size_t n4 = (reinterpret_cast<uintptr_t>(x) & 15) ? 0 : n / 4;
+  unsigned m = 0;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
+    const float4 v = __ldg(reinterpret_cast<const float4 *>(x) + i);
+    m = max(m, max(max(__float_as_uint(v.x) & 0x7fffffffu, __float_as_uint(v.y) & 0x7fffffffu),
+                   max(__float_as_uint(v.z) & 0x7fffffffu, __float_as_uint(v.w) & 0x7fffffffu)));
+  }
+  for (size_t i = n4 * 4 + (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+    m = max(m, __float_as_uint(__ldg(x + i)) & 0x7fffffffu);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+  __shared__ unsigned wm[32];
+  if ((threadIdx.x & 31) == 0) wm[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    m = threadIdx.x < (blockDim.x >> 5) ? wm[threadIdx.x] : 0u;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (threadIdx.x == 0 && m) atomicMax(out + blockIdx.y, m);
+  }
+}
+
 // C[i, j] = add[i, j] + sum_z ws[z][i][j], partials summed in z order (add may
 // be nullptr or C itself).
 __global__ void splitk_reduce_kernel(float *C, int ldc, const float *add, const float *__restrict__ ws,
@@ -707,13 +868,13 @@ static int launch(DeviceCtx *c, const CUtensorMap &ma, const CUtensorMap &mb, co
 
 // CTA pairs: grid x runs over the pairs' CTAs (cluster of 2 along x; the
 // kernel maps pairs to output tiles in grouped order), z over K splits.
-template <bool A_MN, bool B_MN>
+template <bool A_MN, bool B_MN, bool F16>
 static int launch_pair(DeviceCtx *c, const CUtensorMap &ma, const CUtensorMap &mb, const Params &p, int splits,
                        const CUtensorMap *extra = nullptr) {
   static bool attr_set[kMaxDevices] = {};
   if (!attr_set[c->device]) {
-    TL_TRY_CUDA(cudaFuncSetAttribute(gemm_tc_pair_kernel<A_MN, B_MN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     PAIR_SMEM_BYTES));
+    TL_TRY_CUDA(cudaFuncSetAttribute(gemm_tc_pair_kernel<A_MN, B_MN, F16>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, PAIR_SMEM_BYTES));
     attr_set[c->device] = true;
   }
   const unsigned pairs = (unsigned)((p.I + PM - 1) / PM) * (unsigned)((p.J + PN - 1) / PN);
@@ -722,7 +883,8 @@ static int launch_pair(DeviceCtx *c, const CUtensorMap &ma, const CUtensorMap &m
   // extra: the maps of the second and third products (A1, B1, A2, B2)
   const CUtensorMap &a1 = extra ? extra[0] : ma, &b1 = extra ? extra[1] : mb;
   const CUtensorMap &a2 = extra ? extra[2] : ma, &b2 = extra ? extra[3] : mb;
-  gemm_tc_pair_kernel<A_MN, B_MN><<<grid, NUM_THREADS, PAIR_SMEM_BYTES, c->stream>>>(ma, mb, a1, b1, a2, b2, p);
+  gemm_tc_pair_kernel<A_MN, B_MN, F16><<<grid, NUM_THREADS, PAIR_SMEM_BYTES, c->stream>>>(ma, mb, a1, b1, a2, b2,
+                                                                                          p);
   TL_TRY_CUDA(cudaGetLastError());
   return TL_OK;
 }
@@ -752,9 +914,12 @@ int gemm_tc_prepare(DeviceCtx *c) {
   TL_PREP((tc::gemm_tc_kernel<false, true>), tc::SMEM_BYTES);
   TL_PREP((tc::gemm_tc_kernel<false, false>), tc::SMEM_BYTES);
   TL_PREP((tc::gemm_tc_kernel<true, true>), tc::SMEM_BYTES);
-  TL_PREP((tc::gemm_tc_pair_kernel<false, true>), tc::PAIR_SMEM_BYTES);
-  TL_PREP((tc::gemm_tc_pair_kernel<false, false>), tc::PAIR_SMEM_BYTES);
-  TL_PREP((tc::gemm_tc_pair_kernel<true, true>), tc::PAIR_SMEM_BYTES);
+  TL_PREP((tc::gemm_tc_pair_kernel<false, true, false>), tc::PAIR_SMEM_BYTES);
+  TL_PREP((tc::gemm_tc_pair_kernel<false, false, false>), tc::PAIR_SMEM_BYTES);
+  TL_PREP((tc::gemm_tc_pair_kernel<true, true, false>), tc::PAIR_SMEM_BYTES);
+  TL_PREP((tc::gemm_tc_pair_kernel<false, true, true>), tc::PAIR_SMEM_BYTES);
+  TL_PREP((tc::gemm_tc_pair_kernel<false, false, true>), tc::PAIR_SMEM_BYTES);
+  TL_PREP((tc::gemm_tc_pair_kernel<true, true, true>), tc::PAIR_SMEM_BYTES);
 #undef TL_PREP
   return TL_OK;
 }
@@ -769,12 +934,26 @@ bool gemm_tc_prefer_pair(int I, int J, int R) {
 // through the prepared tensor maps.  extra / seg_end0 / seg_end1: the maps
 // and k-block boundaries of a second and third product summed into the same
 // output (pair kernel, NT only).
+// amax: the operand arrays of the fp16-split pair kernel (nullptr: tf32); their
+// max |x| is found first, on the stream, into the context's scratch.
 static int gemm_tc_launch(DeviceCtx *c, GemmOp op, float *C, int I, int J, int nk, int out_ldc,
                           const CUtensorMap &ma, const CUtensorMap &mb, const CUtensorMap *extra, int seg_end0,
-                          int seg_end1, bool pair, const float *add) {
+                          int seg_end1, bool pair, const float *add, const tc::AmaxArgs *amax, int namax) {
   tc::Params p;
   p.C = C; p.I = I; p.J = J; p.R = nk * tc::BK; p.err = c->err_flag;
   p.seg_end0 = seg_end0; p.seg_end1 = seg_end1;
+  p.amax = nullptr;
+  const bool f16 = pair && amax;
+  if (f16) {
+    size_t nmax = 0;
+    for (int t = 0; t < namax; t++) nmax = std::max(nmax, amax->n[t]);
+    TL_TRY_CUDA(cudaMemsetAsync(c->gemm_amax, 0, sizeof(unsigned) * 8, c->stream));
+    TraceScope ts(c, "gemm_absmax");
+    const unsigned bx = (unsigned)std::min<size_t>(std::max<size_t>((nmax / 4 + 255) / 256, 1), 2 * (size_t)c->num_sms);
+    tc::absmax_kernel<<<dim3(bx, namax), 256, 0, c->stream>>>(*amax, c->gemm_amax);
+    TL_TRY_CUDA(cudaGetLastError());
+    p.amax = c->gemm_amax;
+  }
   // Split-K.  A launch takes ceil(CTAs / SMs) waves of (k-blocks per split)
   // k-block times; splitting the reduction over s CTAs multiplies the CTAs by
   // s and divides the k-blocks by s, so the split count is chosen to minimise
@@ -816,14 +995,19 @@ static int gemm_tc_launch(DeviceCtx *c, GemmOp op, float *C, int I, int J, int n
   int rc = TL_OK;
   switch (op) {
     case GemmOp::NN:
-      rc = pair ? tc::launch_pair<false, true>(c, ma, mb, p, splits) : tc::launch<false, true>(c, ma, mb, p, splits);
+      rc = !pair ? tc::launch<false, true>(c, ma, mb, p, splits)
+           : f16 ? tc::launch_pair<false, true, true>(c, ma, mb, p, splits)
+                 : tc::launch_pair<false, true, false>(c, ma, mb, p, splits);
       break;
     case GemmOp::NT:
-      rc = pair ? tc::launch_pair<false, false>(c, ma, mb, p, splits, extra)
-                : tc::launch<false, false>(c, ma, mb, p, splits);
+      rc = !pair ? tc::launch<false, false>(c, ma, mb, p, splits)
+           : f16 ? tc::launch_pair<false, false, true>(c, ma, mb, p, splits, extra)
+                 : tc::launch_pair<false, false, false>(c, ma, mb, p, splits, extra);
       break;
     case GemmOp::TN:
-      rc = pair ? tc::launch_pair<true, true>(c, ma, mb, p, splits) : tc::launch<true, true>(c, ma, mb, p, splits);
+      rc = !pair ? tc::launch<true, true>(c, ma, mb, p, splits)
+           : f16 ? tc::launch_pair<true, true, true>(c, ma, mb, p, splits)
+                 : tc::launch_pair<true, true, false>(c, ma, mb, p, splits);
       break;
   }
   if (rc || splits == 1) return rc;
@@ -836,7 +1020,7 @@ static int gemm_tc_launch(DeviceCtx *c, GemmOp op, float *C, int I, int J, int n
 }
 
 int gemm_tc(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, int M, int K, int N, bool pair,
-            const float *add) {
+            const float *add, bool f16) {
   int rc;
   if ((rc = tc::get_encoder())) return rc;
   int I, J, R;
@@ -861,11 +1045,19 @@ int gemm_tc(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, i
       break;
   }
   const int nk = (R + tc::BK - 1) / tc::BK;
-  return gemm_tc_launch(c, op, C, I, J, nk, out_ldc, ma, mb, nullptr, 0x7fffffff, 0x7fffffff, pair, add);
+  tc::AmaxArgs am = {};
+  am.p[0] = A; am.p[1] = B;
+  switch (op) {   // the arrays' extents: A then B
+    case GemmOp::NN: am.n[0] = (size_t)M * K; am.n[1] = (size_t)K * N; break;
+    case GemmOp::NT: am.n[0] = (size_t)M * N; am.n[1] = (size_t)K * N; break;
+    case GemmOp::TN: am.n[0] = (size_t)M * K; am.n[1] = (size_t)M * N; break;
+  }
+  return gemm_tc_launch(c, op, C, I, J, nk, out_ldc, ma, mb, nullptr, 0x7fffffff, 0x7fffffff, pair, add,
+                        f16 ? &am : nullptr, 2);
 }
 
 int gemm_tc_nt_sum(DeviceCtx *c, float *C, int nprod, const float *const *A, const float *const *B, const int *N,
-                   int M, int K) {
+                   int M, int K, bool f16) {
   if (nprod < 1 || nprod > 3) return set_error(TL_EINVAL, "gemm_tc_nt_sum takes 1 to 3 products, not %d", nprod);
   int rc;
   if ((rc = tc::get_encoder())) return rc;
@@ -885,7 +1077,13 @@ int gemm_tc_nt_sum(DeviceCtx *c, float *C, int nprod, const float *const *A, con
     maps[2 * t] = maps[0]; maps[2 * t + 1] = maps[1];
     end[t] = 0x7fffffff;
   }
-  return gemm_tc_launch(c, GemmOp::NT, C, M, K, nk, K, maps[0], maps[1], maps + 2, end[0], end[1], true, nullptr);
+  tc::AmaxArgs am = {};
+  for (int t = 0; t < nprod; t++) {
+    am.p[2 * t] = A[t]; am.n[2 * t] = (size_t)M * N[t];
+    am.p[2 * t + 1] = B[t]; am.n[2 * t + 1] = (size_t)K * N[t];
+  }
+  return gemm_tc_launch(c, GemmOp::NT, C, M, K, nk, K, maps[0], maps[1], maps + 2, end[0], end[1], true, nullptr,
+                        f16 ? &am : nullptr, 2 * nprod);
 }
 
 }  // namespace tl

@@ -74,6 +74,7 @@ TL_API int tl_init(int device) {
   TL_TRY_CUDA(cudaMemset(c.err_flag, 0, sizeof(int)));
   TL_TRY_CUDA(cudaMalloc(&c.gemm_ws, sizeof(float) * kGemmWorkspaceFloats));
   c.gemm_ws_floats = kGemmWorkspaceFloats;
+  TL_TRY_CUDA(cudaMalloc(&c.gemm_amax, sizeof(unsigned) * 8));
   TL_TRY_CUDA(cudaDeviceSynchronize());
   c.ready = true;
   return TL_OK;
