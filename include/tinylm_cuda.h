@@ -186,10 +186,11 @@ int tl_model_step(void *handle, float *P, float *G, float *M, float *V, const in
  * the bias corrections of step t are copied to the device before each replay.
  * Same results as tl_model_step, bit for bit.  The buffers must stay where
  * they were at capture. */
-/* Attention forward engine, for tests and benchmarks: 0 = automatic (tensor
- * cores -- tcgen05, 3xTF32 -- where T = 256 and head_dim = 64, else CUDA
- * cores), 1 = CUDA cores only, 2 = tensor cores only (TL_EINVAL from the
- * model calls when the shape does not allow it). */
+/* Attention engine (forward and backward), for tests and benchmarks:
+ * 0 = automatic (tensor cores -- tcgen05, 3xTF32 -- where T = 256 and
+ * head_dim = 64, else CUDA cores), 1 = CUDA cores only, 2 = tensor cores
+ * only for the forward (TL_EINVAL from the model calls when the shape does
+ * not allow it; the backward follows the automatic choice). */
 int tl_set_attn_engine(int engine);
 int tl_model_graph_step(void *handle, float *P, float *G, float *M, float *V, const int *tok, const int *tgt,
                         const int *tgt_mtp, int B, float lr, int t, float max_norm, float *loss_dev,

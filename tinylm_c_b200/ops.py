@@ -108,7 +108,8 @@ def set_gemm_engine(engine):
 
 
 def set_attn_engine(engine):
-    """Attention forward: 0 automatic, 1 CUDA cores, 2 tensor cores (T=256, hd=64)."""
+    """Attention forward and backward: 0 automatic, 1 CUDA cores, 2 tensor
+    cores (T=256, hd=64)."""
     check(lib().tl_set_attn_engine(int(engine)))
 
 
