@@ -340,6 +340,24 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   }
 }
 
+// RoPE's backward on one head row held in registers (64 values): the pair
+// (i, i + 32) rotated by the transposed matrix, in the order the separate
+// RoPE kernel uses.
+__device__ __forceinline__ void rope_back_row(float (&v)[HD], const float *cs, const float *sn) {
+#pragma unroll
+  for (int i4 = 0; i4 < HD / 2; i4 += 4) {
+    const float4 c = __ldg(reinterpret_cast<const float4 *>(cs + i4));
+    const float4 s = __ldg(reinterpret_cast<const float4 *>(sn + i4));
+    const float cc[4] = {c.x, c.y, c.z, c.w}, ss[4] = {s.x, s.y, s.z, s.w};
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const float a = v[i4 + u], b = v[i4 + u + HD / 2];
+      v[i4 + u] = a * cc[u] + b * ss[u];
+      v[i4 + u + HD / 2] = -a * ss[u] + b * cc[u];
+    }
+  }
+}
+
 // ------------------------------------------------------------- dQ = dS K
 // The query-side product of the backward (tinylm.c:772-777, dq += dsc * k) for
 // one (sequence, query head, query half r): M = 128 queries, N = 64, the
@@ -370,6 +388,7 @@ static_assert(2 * DQ_SMEM_BYTES <= 228 * 1024, "two dQ CTAs per SM");
 
 struct DqArgs {
   float *dq;
+  const float *cosT, *sinT;   // RoPE table [T][HD/2]: the inverse rotation is applied to dQ; nullptr: none
   int H, KV, D;
   int *err;
 };
@@ -501,24 +520,28 @@ attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmS, const __grid_cons
       tc_fence_after();
       const int q4 = warp & 3, row = q4 * 32 + lane;
       const uint32_t lane_addr = (uint32_t)(q4 * 32) << 16;
-      float *dst = a.dq + ((size_t)b * T + QR * r + row) * a.D + (size_t)h * HD;
+      const int qpos = QR * r + row;
+      float *dst = a.dq + ((size_t)b * T + qpos) * a.D + (size_t)h * HD;
+      float o[HD];
 #pragma unroll
       for (int cc = 0; cc < HD / 32; cc++) {
         uint32_t v0[32];
         tmem_ld32(tmem + lane_addr + cc * 32, v0);
-        float o[32];
 #pragma unroll
-        for (int e = 0; e < 32; e++) o[e] = __uint_as_float(v0[e]);
+        for (int e = 0; e < 32; e++) o[32 * cc + e] = __uint_as_float(v0[e]);
         if (r == 1) {
           uint32_t v1[32];
           tmem_ld32(tmem + lane_addr + HD + cc * 32, v1);
 #pragma unroll
-          for (int e = 0; e < 32; e++) o[e] += __uint_as_float(v1[e]);
+          for (int e = 0; e < 32; e++) o[32 * cc + e] += __uint_as_float(v1[e]);
         }
-#pragma unroll
-        for (int e = 0; e < 32; e += 4)
-          *reinterpret_cast<float4 *>(dst + cc * 32 + e) = make_float4(o[e], o[e + 1], o[e + 2], o[e + 3]);
       }
+      // The gradient through RoPE (tinylm.c:1132-1133): the transposed
+      // rotation of each (i, i + HD/2) pair at this query's position.
+      if (a.cosT) rope_back_row(o, a.cosT + (size_t)qpos * (HD / 2), a.sinT + (size_t)qpos * (HD / 2));
+#pragma unroll
+      for (int e = 0; e < HD; e += 4)
+        *reinterpret_cast<float4 *>(dst + e) = make_float4(o[e], o[e + 1], o[e + 2], o[e + 3]);
     }
   }
   tc_fence_before();
@@ -581,6 +604,7 @@ constexpr uint32_t BW_IDESC_ACC = (1u << 4) | (2u << 7) | (2u << 10) | (1u << 16
                                   ((uint32_t)(QR >> 4) << 24);
 
 struct BwArgs {
+  const float *cosT, *sinT;   // RoPE table [T][HD/2]: the inverse rotation is applied to dK; nullptr: none
   const float *lse, *Drow;
   float *dsT, *dk, *dv;
   int B, H, KV;
@@ -920,6 +944,8 @@ attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmKk, const __grid_c
     if (ok) ok = drain(grp - 1);
     if (ok && !*abort_flag) {
       const size_t o = ((size_t)bb * T + key0 + row) * (size_t)(a.KV * HD) + (size_t)kvh * HD;
+      if (a.cosT)
+        rope_back_row(acck, a.cosT + (size_t)(key0 + row) * (HD / 2), a.sinT + (size_t)(key0 + row) * (HD / 2));
       float4 *pv = reinterpret_cast<float4 *>(a.dv + o);
       float4 *pk = reinterpret_cast<float4 *>(a.dk + o);
 #pragma unroll
@@ -1001,7 +1027,8 @@ bool attn_bwd_dq_tc_supported(const float *dsT, const float *k, const float *dq,
   return T == atc::T && hd == atc::HD && (al & 15) == 0 && KV > 0 && H % KV == 0;
 }
 
-int attn_bwd_dq_tc(DeviceCtx *c, const float *dsT, const float *k, float *dq, int B, int H, int KV) {
+int attn_bwd_dq_tc(DeviceCtx *c, const float *dsT, const float *k, float *dq, int B, int H, int KV, const float *cosT,
+                   const float *sinT) {
   static bool attr[kMaxDevices] = {};
   if (!attr[c->device]) {
     TL_TRY_CUDA(cudaFuncSetAttribute(atc::attn_bwd_dq_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1015,7 +1042,7 @@ int attn_bwd_dq_tc(DeviceCtx *c, const float *dsT, const float *k, float *dq, in
     return rc;
   if ((rc = atc::map2d(&mk, k, KD, (uint64_t)B * atc::T, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))) return rc;
   atc::DqArgs a;
-  a.dq = dq; a.H = H; a.KV = KV; a.D = H * atc::HD; a.err = c->err_flag;
+  a.dq = dq; a.cosT = cosT; a.sinT = sinT; a.H = H; a.KV = KV; a.D = H * atc::HD; a.err = c->err_flag;
   TraceScope ts(c, "k_attn_bwd_dq_tc");
   atc::attn_bwd_dq_tc_kernel<<<2 * B * H, atc::DQ_THREADS, atc::DQ_SMEM_BYTES, c->stream>>>(ms, mk, a);
   TL_TRY_CUDA(cudaGetLastError());
@@ -1030,7 +1057,8 @@ bool attn_bwd_dkdv_tc_supported(const float *const *ptrs, int nptr, int T, int h
 }
 
 int attn_bwd_dkdv_tc(DeviceCtx *c, const float *q, const float *k, const float *v, const float *dout,
-                     const float *lse, const float *Drow, float *dsT, float *dk, float *dv, int B, int H, int KV) {
+                     const float *lse, const float *Drow, float *dsT, float *dk, float *dv, int B, int H, int KV,
+                     const float *cosT, const float *sinT) {
   static bool attr[kMaxDevices] = {};
   if (!attr[c->device]) {
     TL_TRY_CUDA(cudaFuncSetAttribute(atc::attn_bwd_dkdv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1048,6 +1076,7 @@ int attn_bwd_dkdv_tc(DeviceCtx *c, const float *q, const float *k, const float *
   if ((rc = atc::map2d(&mqm, q, D, rows, 32, atc::BW_NQ, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))) return rc;
   if ((rc = atc::map2d(&mom, dout, D, rows, 32, atc::BW_NQ, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))) return rc;
   atc::BwArgs a;
+  a.cosT = cosT; a.sinT = sinT;
   a.lse = lse; a.Drow = Drow; a.dsT = dsT; a.dk = dk; a.dv = dv;
   a.B = B; a.H = H; a.KV = KV;
   a.scale = 1.0f / sqrtf((float)atc::HD);

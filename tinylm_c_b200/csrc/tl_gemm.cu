@@ -64,6 +64,18 @@ int tl::gemm_run_add(DeviceCtx *c, GemmOp op, float *C, const float *A, const fl
   return gemm_simt(c, op, C, A, B, M, K, N, add);
 }
 
+bool tl::gemm_try_rope(DeviceCtx *c, float *C, const float *A, const float *B, int M, int K, int N,
+                       const GemmRope &rope, int *rc) {
+  if (M <= 0 || K <= 0 || N <= 0 || N % 64 || rope.T <= 0 || g_engine_pref == 1 || g_engine_pref == 2) return false;
+  if (((reinterpret_cast<uintptr_t>(rope.cosT) | reinterpret_cast<uintptr_t>(rope.sinT)) & 15) != 0) return false;
+  if (!gemm_tc_supported(GemmOp::NN, C, A, B, M, K, N)) return false;
+  if (g_engine_pref == 0 && !gemm_tc_prefer_pair(M, N, K)) return false;
+  const bool f16 = g_engine_pref == 4 || (g_engine_pref == 0 && kAutoF16);
+  g_engine_last = f16 ? 4 : 3;
+  *rc = gemm_tc(c, GemmOp::NN, C, A, B, M, K, N, true, nullptr, f16, &rope);
+  return true;
+}
+
 int tl::gemm_run_nt_sum(DeviceCtx *c, float *C, int nprod, const float *const *A, const float *const *B,
                         const int *N, int M, int K) {
   bool fused = nprod >= 1 && nprod <= 3 && M > 0 && K > 0 && (g_engine_pref == 0 || g_engine_pref >= 3);

@@ -37,11 +37,23 @@ bool gemm_tc_supported(GemmOp op, const float *C, const float *A, const float *B
 bool gemm_tc_prefer_pair(int I, int J, int R);
 // Host-side set-up of every tensor-core kernel (before a CUDA graph capture).
 int gemm_tc_prepare(DeviceCtx *c);
+// RoPE applied to a product's rows in the pair kernel's epilogue: heads of 64
+// columns, row i at sequence position i % T, tables [T][32].
+struct GemmRope {
+  const float *cosT, *sinT;
+  int T;
+};
 // pair: the CTA-pair kernel (256 x 256 tiles over two SMs) instead of the
 // one-CTA kernel (128 x 128 tiles); f16 (pair only): operands split into
-// scaled fp16 hi/lo parts instead of tf32 hi/lo.
+// scaled fp16 hi/lo parts instead of tf32 hi/lo; rope (pair only): RoPE on
+// the output rows (no split-K then).
 int gemm_tc(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, int M, int K, int N, bool pair,
-            const float *add, bool f16);
+            const float *add, bool f16, const GemmRope *rope = nullptr);
+// C[M,N] = A[M,K] B[K,N] with RoPE on C's rows, in one pair-kernel launch;
+// false (nothing launched) where the engine choice would not give the pair
+// kernel this shape, or N is not whole heads of 64.
+bool gemm_try_rope(DeviceCtx *c, float *C, const float *A, const float *B, int M, int K, int N, const GemmRope &rope,
+                   int *rc);
 
 // C[M,K] = sum over t < nprod (<= 3) of A_t[M,N_t] @ B_t[K,N_t]^T, one
 // CTA-pair launch whose reduction walks the products' k-blocks in turn

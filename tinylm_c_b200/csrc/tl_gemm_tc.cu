@@ -79,6 +79,10 @@ struct Params {
   // Pair kernel, fp16 split: max |x| (float bits) of A and B of each product,
   // [A0, B0, A1, B1, A2, B2].
   const unsigned *amax;
+  // Pair kernel: RoPE on the output (heads of 64 columns; row i at sequence
+  // position i % rope_T), table [T][32]; nullptr: none.
+  const float *rope_cos, *rope_sin;
+  int rope_T;
   int *err;
 };
 
@@ -744,6 +748,26 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         for (int e = 0; e < BN; e++) acc[e] *= inv;
       }
       const int row = i0 + q * 32 + lane;
+      if (p.rope_cos && row < p.I) {
+        // RoPE (tinylm.c:626-640): this thread's 128 columns are two heads;
+        // pairs (i, i + 32) rotate by the angle of the row's position.
+        const size_t tb = (size_t)(row % p.rope_T) * 32;
+#pragma unroll
+        for (int i4 = 0; i4 < 32; i4 += 4) {
+          const float4 c4 = __ldg(reinterpret_cast<const float4 *>(p.rope_cos + tb + i4));
+          const float4 s4 = __ldg(reinterpret_cast<const float4 *>(p.rope_sin + tb + i4));
+          const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, ss[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+          for (int u = 0; u < 4; u++) {
+#pragma unroll
+            for (int hh = 0; hh < 2; hh++) {
+              const float a = acc[64 * hh + i4 + u], b = acc[64 * hh + i4 + u + 32];
+              acc[64 * hh + i4 + u] = a * cc[u] - b * ss[u];
+              acc[64 * hh + i4 + u + 32] = b * cc[u] + a * ss[u];
+            }
+          }
+        }
+      }
       const int jc = j0 + h * BN;
       if (row < p.I) {
         float *dst = Cout + (size_t)row * p.ldc + jc;
@@ -938,11 +962,17 @@ bool gemm_tc_prefer_pair(int I, int J, int R) {
 // max |x| is found first, on the stream, into the context's scratch.
 static int gemm_tc_launch(DeviceCtx *c, GemmOp op, float *C, int I, int J, int nk, int out_ldc,
                           const CUtensorMap &ma, const CUtensorMap &mb, const CUtensorMap *extra, int seg_end0,
-                          int seg_end1, bool pair, const float *add, const tc::AmaxArgs *amax, int namax) {
+                          int seg_end1, bool pair, const float *add, const tc::AmaxArgs *amax, int namax,
+                          const GemmRope *rope = nullptr) {
   tc::Params p;
   p.C = C; p.I = I; p.J = J; p.R = nk * tc::BK; p.err = c->err_flag;
   p.seg_end0 = seg_end0; p.seg_end1 = seg_end1;
   p.amax = nullptr;
+  p.rope_cos = p.rope_sin = nullptr;
+  p.rope_T = 1;
+  if (rope) {
+    p.rope_cos = rope->cosT; p.rope_sin = rope->sinT; p.rope_T = rope->T;
+  }
   const bool f16 = pair && amax;
   if (f16) {
     size_t nmax = 0;
@@ -966,7 +996,7 @@ static int gemm_tc_launch(DeviceCtx *c, GemmOp op, float *C, int I, int J, int n
   const int tm = pair ? tc::PM : tc::BM, tn = pair ? tc::PN : tc::BN, sms_per_tile = pair ? 2 : 1;
   const long long tiles = (long long)((I + tm - 1) / tm) * ((J + tn - 1) / tn);
   int splits = 1;
-  if (c->gemm_ws) {
+  if (c->gemm_ws && !rope) {   // (RoPE needs the whole sum in the epilogue)
     const size_t cap = c->gemm_ws_floats / ((size_t)I * J);
     const int smax = (int)std::min<size_t>(std::min(64, nk / tc::CHUNK_KB), cap);
     const double out_units = (double)I * J * 4.0 / 6.0e6;  // one output pass, in k-block times
@@ -1020,7 +1050,7 @@ static int gemm_tc_launch(DeviceCtx *c, GemmOp op, float *C, int I, int J, int n
 }
 
 int gemm_tc(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, int M, int K, int N, bool pair,
-            const float *add, bool f16) {
+            const float *add, bool f16, const GemmRope *rope) {
   int rc;
   if ((rc = tc::get_encoder())) return rc;
   int I, J, R;
@@ -1053,7 +1083,7 @@ int gemm_tc(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, i
     case GemmOp::TN: am.n[0] = (size_t)M * K; am.n[1] = (size_t)M * N; break;
   }
   return gemm_tc_launch(c, op, C, I, J, nk, out_ldc, ma, mb, nullptr, 0x7fffffff, 0x7fffffff, pair, add,
-                        f16 ? &am : nullptr, 2);
+                        f16 ? &am : nullptr, 2, rope);
 }
 
 int gemm_tc_nt_sum(DeviceCtx *c, float *C, int nprod, const float *const *A, const float *const *B, const int *N,

@@ -91,6 +91,15 @@ struct Rng {
 static int gemm(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, int M, int K, int N) {
   return gemm_run(c, op, C, A, B, M, K, N);
 }
+// C = A @ W, then RoPE on C's rows (nh heads): in the GEMM's epilogue where
+// the pair kernel takes it (head_dim 64), else as a separate pass.
+static int gemm_rope(DeviceCtx *c, const Model &m, float *C, const float *A, const float *W, int M, int K, int N,
+                     int nh) {
+  int rc = TL_OK;
+  if (m.hd == 64 && gemm_try_rope(c, C, A, W, M, K, N, GemmRope{m.rope_cos, m.rope_sin, m.T}, &rc)) return rc;
+  if ((rc = gemm_run(c, GemmOp::NN, C, A, W, M, K, N))) return rc;
+  return k_rope(c, C, m.rope_cos, m.rope_sin, M, nh, m.hd, m.T, 0);
+}
 // C = op(A, B) + add (add: nullptr to overwrite, or a residual); replaces the
 // reference's memset-then-accumulate and GEMM-then-add pairs with one pass.
 static int gemm_add(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, int M, int K, int N,
@@ -111,11 +120,10 @@ static int micro_step(DeviceCtx *c, Model &m, const float *P, float *G, const in
   for (int l = 0; l < m.L; l++) {
     float *xin = m.a_in[l];
     TRY(k_rmsnorm_fwd(c, xin, P + m.o_an1[l], m.a_norm[l], m.rinv1[l], N, D));
-    TRY(gemm(c, GemmOp::NN, m.q[l], m.a_norm[l], P + m.o_wq[l], N, D, D));
-    TRY(gemm(c, GemmOp::NN, m.k[l], m.a_norm[l], P + m.o_wk[l], N, D, KD));
+    // q and k with RoPE, v (tinylm.c:981-989)
+    TRY(gemm_rope(c, m, m.q[l], m.a_norm[l], P + m.o_wq[l], N, D, D, m.H));
+    TRY(gemm_rope(c, m, m.k[l], m.a_norm[l], P + m.o_wk[l], N, D, KD, m.KV));
     TRY(gemm(c, GemmOp::NN, m.v[l], m.a_norm[l], P + m.o_wv[l], N, D, KD));
-    TRY(k_rope(c, m.q[l], m.rope_cos, m.rope_sin, N, m.H, m.hd, m.T, 0));
-    TRY(k_rope(c, m.k[l], m.rope_cos, m.rope_sin, N, m.KV, m.hd, m.T, 0));
     TRY(k_attn_fwd(c, m.q[l], m.k[l], m.v[l], m.att[l], m.lse[l], m.mb, m.T, m.H, m.KV, m.hd));
     TRY(gemm_add(c, GemmOp::NN, m.f_in[l], m.att[l], P + m.o_wo[l], N, D, D, xin));   // + residual
     TRY(k_rmsnorm_fwd(c, m.f_in[l], P + m.o_an2[l], m.f_norm[l], m.rinv2[l], N, D));
@@ -172,11 +180,9 @@ static int micro_step(DeviceCtx *c, Model &m, const float *P, float *G, const in
     // attention output projection
     TRY(gemm_add(c, GemmOp::NT, m.datt, m.dfin, P + m.o_wo[l], N, D, D, nullptr));
     TRY(gemm(c, GemmOp::TN, G + m.o_wo[l], m.att[l], m.dfin, N, D, D));
-    // attention
+    // attention and RoPE's backward (tinylm.c:1130-1133)
     TRY(k_attn_bwd(c, m.q[l], m.k[l], m.v[l], m.att[l], m.datt, m.lse[l], m.Drow, m.dsT, m.dq, m.dk, m.dv, m.mb, m.T, m.H,
-                   m.KV, m.hd));
-    TRY(k_rope(c, m.dq, m.rope_cos, m.rope_sin, N, m.H, m.hd, m.T, 1));
-    TRY(k_rope(c, m.dk, m.rope_cos, m.rope_sin, N, m.KV, m.hd, m.T, 1));
+                   m.KV, m.hd, m.rope_cos, m.rope_sin));
     {  // dnorm = dq @ Wq^T + dk @ Wk^T + dv @ Wv^T
       const float *As[3] = {m.dq, m.dk, m.dv}, *Bs[3] = {P + m.o_wq[l], P + m.o_wk[l], P + m.o_wv[l]};
       const int Ns[3] = {D, KD, KD};

@@ -28,8 +28,9 @@ int k_attn_fwd(DeviceCtx *c, const float *q, const float *k, const float *v, flo
                int H, int KV, int hd);
 // dsT: scratch of B*H*T*T floats (dS^T of the causal tile pairs, written by the
 // key-side kernel and read by the query-side one).
+// Also applies RoPE's backward (tables cosT / sinT) to dQ and dK.
 int k_attn_bwd(DeviceCtx *c, const float *q, const float *k, const float *v, const float *out, const float *dout,
                const float *lse, float *Drow, float *dsT, float *dq, float *dk, float *dv, int B, int T, int H,
-               int KV, int hd);
+               int KV, int hd, const float *cosT, const float *sinT);
 
 }  // namespace tl

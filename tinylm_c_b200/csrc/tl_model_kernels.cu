@@ -849,10 +849,12 @@ bool attn_fwd_tc_supported(const float *q, const float *k, const float *v, int T
 int attn_fwd_tc(DeviceCtx *c, const float *q, const float *k, const float *v, float *out, float *lse, int B, int T,
                 int H, int KV, int hd);
 bool attn_bwd_dq_tc_supported(const float *dsT, const float *k, const float *dq, int T, int hd, int H, int KV);
-int attn_bwd_dq_tc(DeviceCtx *c, const float *dsT, const float *k, float *dq, int B, int H, int KV);
+int attn_bwd_dq_tc(DeviceCtx *c, const float *dsT, const float *k, float *dq, int B, int H, int KV, const float *cosT,
+                   const float *sinT);
 bool attn_bwd_dkdv_tc_supported(const float *const *ptrs, int nptr, int T, int hd, int H, int KV);
 int attn_bwd_dkdv_tc(DeviceCtx *c, const float *q, const float *k, const float *v, const float *dout,
-                     const float *lse, const float *Drow, float *dsT, float *dk, float *dv, int B, int H, int KV);
+                     const float *lse, const float *Drow, float *dsT, float *dk, float *dv, int B, int H, int KV,
+                     const float *cosT, const float *sinT);
 static thread_local int g_attn_engine = 0;   // 0 automatic, 1 CUDA cores, 2 tensor cores
 
 int k_attn_fwd(DeviceCtx *c, const float *q, const float *k, const float *v, float *out, float *lse, int B, int T,
@@ -869,25 +871,36 @@ int k_attn_fwd(DeviceCtx *c, const float *q, const float *k, const float *v, flo
 }
 int k_attn_bwd(DeviceCtx *c, const float *q, const float *k, const float *v, const float *out, const float *dout,
                const float *lse, float *Drow, float *dsT, float *dq, float *dk, float *dv, int B, int T, int H,
-               int KV, int hd) {
+               int KV, int hd, const float *cosT, const float *sinT) {
   TraceScope ts(c, "k_attn_bwd");
   const float scale = 1.0f / sqrtf((float)hd);
   const int rows = B * H * T;
   mk::attn_rowdot_kernel<<<(rows + 7) / 8, 256, 0, c->stream>>>(dout, out, Drow, B, T, H, hd);
   MK_LAUNCH_CHECK();
+  // The tensor-core kernels apply RoPE's backward to dK / dQ as they store
+  // them; after the CUDA-core kernels it is a separate pass.
   const float *ptrs[9] = {q, k, v, dout, lse, Drow, dsT, dk, dv};
+  bool dk_rotated = false, dq_rotated = false;
   if (g_attn_engine != 1 && attn_bwd_dkdv_tc_supported(ptrs, 9, T, hd, H, KV)) {
-    const int rc = attn_bwd_dkdv_tc(c, q, k, v, dout, lse, Drow, dsT, dk, dv, B, H, KV);
+    const int rc = attn_bwd_dkdv_tc(c, q, k, v, dout, lse, Drow, dsT, dk, dv, B, H, KV, cosT, sinT);
     if (rc) return rc;
+    dk_rotated = true;
   } else {
     mk::attn_bwd_dkdv_kernel<<<B * KV * (T / mk::AT), 256, attn_smem_dkdv(), c->stream>>>(
         q, k, v, dout, lse, Drow, dk, dv, dsT, T, H, KV, hd, scale);
     MK_LAUNCH_CHECK();
   }
-  if (g_attn_engine != 1 && attn_bwd_dq_tc_supported(dsT, k, dq, T, hd, H, KV))
-    return attn_bwd_dq_tc(c, dsT, k, dq, B, H, KV);
-  mk::attn_bwd_dq_kernel<<<B * H * (T / mk::AT), 256, attn_smem_dq(), c->stream>>>(k, dsT, dq, T, H, KV, hd);
-  MK_LAUNCH_CHECK();
+  if (g_attn_engine != 1 && attn_bwd_dq_tc_supported(dsT, k, dq, T, hd, H, KV)) {
+    const int rc = attn_bwd_dq_tc(c, dsT, k, dq, B, H, KV, cosT, sinT);
+    if (rc) return rc;
+    dq_rotated = true;
+  } else {
+    mk::attn_bwd_dq_kernel<<<B * H * (T / mk::AT), 256, attn_smem_dq(), c->stream>>>(k, dsT, dq, T, H, KV, hd);
+    MK_LAUNCH_CHECK();
+  }
+  int rc;
+  if (!dq_rotated && (rc = k_rope(c, dq, cosT, sinT, B * T, H, hd, T, 1))) return rc;
+  if (!dk_rotated && (rc = k_rope(c, dk, cosT, sinT, B * T, KV, hd, T, 1))) return rc;
   return TL_OK;
 }
 
