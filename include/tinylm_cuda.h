@@ -249,7 +249,9 @@ size_t tl_zero1_padded(size_t n, int world);
 /* 128-byte NCCL unique id; rank 0 creates it and the caller ships it to the
  * other ranks (e.g. over torch.distributed or a file). */
 int tl_dist_unique_id(void *uid128);
-/* Blocking communicator set-up for this process's current device. */
+/* Blocking communicator set-up for this process's current device, bounded by
+ * TL_DIST_INIT_TIMEOUT_MS (default 120000, never below TL_DIST_TIMEOUT_MS);
+ * TL_ETIMEOUT when a rank never joins. */
 int tl_dist_init(int rank, int world, const void *uid128);
 int tl_dist_finalize(void);
 /* One ZeRO-1 optimizer step over the padded flat buffers:

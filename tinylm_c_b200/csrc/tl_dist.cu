@@ -11,6 +11,7 @@
 // for the stream with a host-side deadline.  A peer that never arrives turns
 // into TL_ETIMEOUT (the communicator is aborted) instead of a hang.
 #include <nccl.h>
+#include <algorithm>
 #include <chrono>
 #include <cstdlib>
 #include <cstring>
@@ -41,6 +42,14 @@ static int timeout_ms() {
   int v = e ? atoi(e) : 0;
   return v > 0 ? v : 120000;
 }
+// Communicator creation (bootstrap, topology and channel set-up) can take
+// seconds on a cold node, whatever bound the steps use: its own limit,
+// TL_DIST_INIT_TIMEOUT_MS, at least the step bound, default 120 s.
+static int init_timeout_ms() {
+  const char *e = getenv("TL_DIST_INIT_TIMEOUT_MS");
+  const int v = e ? atoi(e) : 0;
+  return std::max(v > 0 ? v : 120000, timeout_ms());
+}
 
 static int nccl_fail(DistCtx &d, ncclResult_t r, const char *what) {
   set_error(TL_ENCCL, "%s: %s", what, ncclGetErrorString(r));
@@ -49,10 +58,12 @@ static int nccl_fail(DistCtx &d, ncclResult_t r, const char *what) {
   return TL_ENCCL;
 }
 
-// Poll the communicator until the last call has been accepted or failed.
-static int nccl_settle(DistCtx &d, ncclResult_t r, const char *what) {
+// Poll the communicator until the last call has been accepted or failed
+// (limit_ms: the bound, default the step bound).
+static int nccl_settle(DistCtx &d, ncclResult_t r, const char *what, int limit_ms = 0) {
   if (r != ncclSuccess && r != ncclInProgress) return nccl_fail(d, r, what);
-  const auto deadline = std::chrono::steady_clock::now() + std::chrono::milliseconds(timeout_ms());
+  const int lim = limit_ms > 0 ? limit_ms : timeout_ms();
+  const auto deadline = std::chrono::steady_clock::now() + std::chrono::milliseconds(lim);
   ncclResult_t st = ncclInProgress;
   while (true) {
     ncclResult_t q = ncclCommGetAsyncError(d.comm, &st);
@@ -60,7 +71,7 @@ static int nccl_settle(DistCtx &d, ncclResult_t r, const char *what) {
     if (st == ncclSuccess) return TL_OK;
     if (st != ncclInProgress) return nccl_fail(d, st, what);
     if (std::chrono::steady_clock::now() > deadline) {
-      set_error(TL_ETIMEOUT, "%s: no progress within %d ms", what, timeout_ms());
+      set_error(TL_ETIMEOUT, "%s: no progress within %d ms", what, lim);
       ncclCommAbort(d.comm);
       d.comm = nullptr;
       d.ready = false;
@@ -132,7 +143,7 @@ TL_API int tl_dist_init(int rank, int world, const void *uid128) {
   cfg.blocking = 0;
   d.rank = rank; d.world = world; d.device = c->device;
   ncclResult_t r = ncclCommInitRankConfig(&d.comm, world, id, rank, &cfg);
-  int rc = nccl_settle(d, r, "ncclCommInitRankConfig");
+  int rc = nccl_settle(d, r, "ncclCommInitRankConfig", init_timeout_ms());
   if (rc) return rc;
   d.ready = true;
   return TL_OK;
