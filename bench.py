@@ -35,9 +35,8 @@ import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
-# NCCL prints its version banner on stdout unless told otherwise; rank 0's
-# stdout must carry exactly one JSON line.
 os.environ.setdefault("NCCL_DEBUG", "WARN")
+_JSON_OUT = 1   # file descriptor the JSON line is written to (see the end of the file)
 
 T_CTX = 256
 LR, B1, B2, WD, MAX_NORM = 3e-4, 0.9, 0.95, 0.1, 1.0
@@ -87,7 +86,8 @@ def dist_env():
 
 
 def emit(obj):
-    print(json.dumps(obj), flush=True)
+    sys.stdout.flush()
+    os.write(_JSON_OUT, (json.dumps(obj) + "\n").encode())
 
 
 # --------------------------------------------------------------------- clocks
@@ -753,4 +753,10 @@ def main():
 
 
 if __name__ == "__main__":
+    # Rank 0's stdout must carry exactly one JSON line, but libraries write to
+    # file descriptor 1 on their own (NCCL prints its version banner there at
+    # the WARN level).  So descriptor 1 points at stderr for the whole run and
+    # the JSON line goes to a duplicate of the original stdout.
+    _JSON_OUT = os.dup(1)
+    os.dup2(2, 1)
     sys.exit(main())
