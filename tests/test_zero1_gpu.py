@@ -99,8 +99,9 @@ def test_zero1_p2p_wait_expires_when_a_rank_does_not_join(cuda):
 
 def test_dist_init_reports_timeout_when_peer_never_joins(cuda):
     """A 2-rank communicator whose second rank never arrives: tl_dist_init must
-    come back with TL_ETIMEOUT after the configured deadline (host-side failure
-    injection; no kernel is in flight)."""
+    come back with TL_ETIMEOUT after the configured set-up deadline
+    (TL_DIST_INIT_TIMEOUT_MS; host-side failure injection, no kernel in
+    flight)."""
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     code = (
         "import ctypes, sys\n"
@@ -113,7 +114,7 @@ def test_dist_init_reports_timeout_when_peer_never_joins(cuda):
         "rc = L.tl_dist_init(0, 2, ctypes.addressof(uid))\n"
         "print('RC', rc, L.tl_last_error().decode())\n"
     )
-    env = dict(os.environ, TL_DIST_TIMEOUT_MS="3000", NCCL_NVLS_ENABLE="0")
+    env = dict(os.environ, TL_DIST_TIMEOUT_MS="3000", TL_DIST_INIT_TIMEOUT_MS="3000", NCCL_NVLS_ENABLE="0")
     r = subprocess.run(["timeout", "-k", "10", "120", sys.executable, "-c", code],
                        capture_output=True, text=True, env=env)
     assert "RC -5" in r.stdout, r.stdout[-2000:] + r.stderr[-2000:]

@@ -494,6 +494,12 @@ attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmS, const __grid_cons
     // -------------------------------------- lo split, then the epilogue
     const int t = threadIdx.x - 64;            // 0..127
     bool ok = true;
+    if (a.cosT) {
+      // the epilogue's RoPE table rows (128 bytes each) into L1 meanwhile
+      const size_t trow = (size_t)(QR * r + (warp & 3) * 32 + lane) * (HD / 2);
+      asm volatile("prefetch.global.L1 [%0];" ::"l"(a.cosT + trow));
+      asm volatile("prefetch.global.L1 [%0];" ::"l"(a.sinT + trow));
+    }
     for (int kb = 0; kb < nk; kb++) {
       const int s = kb % DQ_STAGES, u = kb / DQ_STAGES;
       if (!mbar_wait(bar_full(s), u & 1, abort_flag, a.err, 53)) { ok = false; break; }

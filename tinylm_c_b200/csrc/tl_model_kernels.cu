@@ -53,9 +53,10 @@ __global__ void embed_fwd_kernel(const float *__restrict__ emb, const int *__res
 // order (tinylm.c:1148-1153), so the result is deterministic and the same
 // bits as that loop (no atomics).  One warp per vocabulary row scans the
 // batch's tokens 32 at a time (ballot) and adds the matching rows; columns go
-// in chunks of 32*EMB_CHUNK so the sums stay in registers.  Rows of tokens
-// outside [0, V) are never added (embed_fwd reports them).
-constexpr int EMB_CHUNK = 8;
+// in chunks of 32*EMB_CHUNK so the sums stay in registers (one scan of the
+// tokens per row up to D = 1024).  Rows of tokens outside [0, V) are never
+// added (embed_fwd reports them).
+constexpr int EMB_CHUNK = 32;
 __global__ void __launch_bounds__(256)
 embed_bwd_kernel(float *__restrict__ gemb, const int *__restrict__ tok, const float *__restrict__ dout, int N,
                  int D, int V) {
