@@ -1,8 +1,11 @@
-// tl_attn_tc.cu -- causal GQA attention forward on the tensor cores (sm_100a).
+// tl_attn_tc.cu -- causal GQA attention on the tensor cores (sm_100a), for
+// T = 256 and head_dim 64: the forward (below), and the backward's key-side
+// (dK, dV) and query-side (dQ) kernels further down, each with its own
+// description.
 //
-// The reference's attention (tinylm.c:698-783) for T = 256 and head_dim 64:
-// one CTA pair (cluster of 2, tcgen05 cta_group::2) per (sequence, query
-// head).  CTA r holds query rows 128r..128r+127 and key rows 128r..128r+127.
+// Forward, the reference's attn_fwd (tinylm.c:699-733): one CTA pair (cluster
+// of 2, tcgen05 cta_group::2) per (sequence, query head).  CTA r holds query
+// rows 128r..128r+127 and key rows 128r..128r+127.
 //
 //   S = Q K^T      M = 256 queries, N = 256 keys, K = 64: 2 k-blocks x 4 x 3
 //                  tf32 MMAs (3xTF32: lo*hi + hi*lo + hi*hi) into TMEM

@@ -1,5 +1,6 @@
 // tl_gemm_tc.cu -- tensor-core GEMM engine: tcgen05 (kind::tf32) with 3xTF32
-// split accumulation, TMA-staged tiles, accumulator in TMEM (sm_100a).
+// split accumulation, TMA-staged tiles, accumulator in TMEM (sm_100a).  (The
+// CTA-pair kernel also has an fp16-split mode, kind::f16, described with it.)
 //
 // The three reference primitives (tinylm.c:439-537) in one kernel family:
 //   C[I,J] (=|+=) sum_r A(i,r) B(r,j)
