@@ -161,7 +161,6 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   } else if (warp == 1) {
     // ------------------------------------------- MMA issuer (leader CTA only)
     if (lane == 0 && rank == 0) {
-      bool issued_any = false;
       if (mbar_wait_pair(bar(QK_READY), 0, abort_flag, peer_flag, a.err, 32)) {
         tc_fence_after();
         constexpr uint32_t idesc_s = idesc_m256(256, false, false);
@@ -179,7 +178,6 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             tc_mma_pair(tmem, q_hi, k_hi, idesc_s, 1);
           }
         }
-        issued_any = true;
         tc_commit_pair(bar(S_FULL));
         constexpr uint32_t idesc_o = idesc_m256(HD, false, true);
         for (int kb = 0; kb < NKB; kb++) {
@@ -203,7 +201,6 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       // O complete (or, on the abort path, every issued MMA finished) before
       // TMEM can be released.
       tc_commit_pair(bar(O_FULL));
-      (void)issued_any;
       const long long t0 = clock64();
       while (!mbar_try_wait(bar(O_FULL), 0)) {
         if (clock64() - t0 > WAIT_LIMIT_CYCLES) { pair_abort(abort_flag, peer_flag, a.err, 34); break; }
