@@ -763,11 +763,17 @@ def main():
     return 0
 
 
-if __name__ == "__main__":
-    # Rank 0's stdout must carry exactly one JSON line, but libraries write to
-    # file descriptor 1 on their own (NCCL prints its version banner there at
-    # the WARN level).  So descriptor 1 points at stderr for the whole run and
-    # the JSON line goes to a duplicate of the original stdout.
+def run_as_script(entry=None):
+    """Run `entry` (main) as the script does.  Rank 0's stdout must carry
+    exactly one JSON line, but libraries write to file descriptor 1 on their
+    own (NCCL prints its version banner there at the WARN level).  So
+    descriptor 1 points at stderr for the whole run and the JSON line goes to
+    a duplicate of the original stdout."""
+    global _JSON_OUT
     _JSON_OUT = os.dup(1)
     os.dup2(2, 1)
-    sys.exit(main())
+    return (entry or main)()
+
+
+if __name__ == "__main__":
+    sys.exit(run_as_script())
