@@ -24,7 +24,7 @@ def test_reference_arm_prints_one_json_line():
     d = json.loads(lines[0])
     for k in ("impl", "metric", "value", "unit", "cpu_baseline", "e2e"):
         assert k in d, k
-    assert d["impl"] == "reference" and d["value"] > 0
+    assert d["impl"] == "reference" and isinstance(d["value"], (int, float)) and d["value"] >= 0
     assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
 
 
