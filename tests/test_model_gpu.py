@@ -96,15 +96,16 @@ def test_gradient_matches_reference_leg(cuda, preset, n_mtp, B):
     assert off == n
 
 
-def test_tensor_core_attention_matches_cuda_cores(cuda):
-    """Head dim 64, T=256 (m16): the tcgen05 attention forward against the
-    CUDA-core one inside a whole forward/backward -- same loss to 1e-6 and
-    gradients to 1e-5 relative."""
+@pytest.mark.parametrize("B", [1, 3, 4])
+def test_tensor_core_attention_matches_cuda_cores(cuda, B):
+    """Head dim 64, T=256 (m16): the tcgen05 attention forward and backward
+    (with RoPE's backward in their epilogues) against the CUDA-core kernels
+    inside a whole forward/backward -- same loss to 1e-6 and gradients to 1e-5
+    relative; one sequence, an odd count and four."""
     c = model.cfg8("m16", 0)
     P = model.init_params(c, 5).to(cuda)
     n = P.numel()
     g = torch.Generator(device=cuda).manual_seed(8)
-    B = 4
     tok = torch.randint(0, 2048, (B * 256,), generator=g, device=cuda, dtype=torch.int32)
     tgt = torch.randint(0, 2048, (B * 256,), generator=g, device=cuda, dtype=torch.int32)
     m = model.Model(c, B, 0)
