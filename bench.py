@@ -35,7 +35,11 @@ import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
-os.environ.setdefault("NCCL_DEBUG", "WARN")
+# NCCL's communicator set-up lines (rank count, transports, NVLS) go to the log;
+# descriptor 1 is redirected to stderr for the run (run_as_script), so they
+# cannot precede the JSON line.
+os.environ.setdefault("NCCL_DEBUG", "INFO")
+os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
 _JSON_OUT = 1   # file descriptor the JSON line is written to (see the end of the file)
 
 T_CTX = 256

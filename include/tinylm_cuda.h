@@ -20,7 +20,9 @@
  *    row length), exactly as the reference stores them.
  *  - Every float pointer passed to a compute call is a DEVICE pointer (from
  *    tl_alloc, cudaMalloc, or a framework allocator).  There is no CPU fallback:
- *    a host pointer is rejected with TL_EPTR.
+ *    a host pointer is rejected with TL_EPTR, unless host-buffer mode
+ *    (tl_set_host_buffers) stages it through device memory for the five
+ *    reference-facing calls.
  *  - Calls are asynchronous and ordered on the library stream of the current
  *    device (tl_set_stream); tl_sync() is the only call that blocks, except the
  *    few documented to read a result back into host memory.
@@ -68,6 +70,19 @@ int tl_memcpy_h2d(void *dst_dev, const void *src_host, size_t bytes);
 int tl_memcpy_d2h(void *dst_host, const void *src_dev, size_t bytes);
 int tl_memset(void *dst_dev, int value, size_t bytes);
 int tl_sync(void);
+/* Host-buffer mode, for a host program that keeps its buffers in ordinary
+ * host memory and reads each result as soon as the call returns -- tinylm.c
+ * itself, whose buffers are fz() callocs (tinylm.c:137) and whose mm, mm_bt,
+ * mm_atb, adamw and global_gradnorm (439-537, 1159-1176) are the call sites
+ * this library replaces.  When on (for the current device), tl_matmul,
+ * tl_matmul_bt, tl_matmul_at, tl_grad_norm and tl_adamw_step also accept
+ * host pointers: each host operand is copied into a staging arena on the
+ * device (grown to the largest call, kept until exit), the device code runs
+ * as for device pointers, outputs are copied back and the call returns once
+ * they are in host memory.  Device pointers in the same call are used in
+ * place.  Off by default: a host pointer is then TL_EPTR.  The reference has
+ * no counterpart (its primitives always run on the host). */
+int tl_set_host_buffers(int on);
 /* Wait for the stream, then report (and clear) the device error word that
  * bounded waits inside library kernels set when they give up: TL_ETIMEOUT if
  * any kernel since the last call returned early, else TL_OK. */
@@ -119,7 +134,8 @@ int tl_last_gemm_engine(void);
  * `norm_out` may be a device or a host pointer; a host pointer makes the call
  * synchronous (it waits for the result). */
 int tl_grad_norm(const float *G, size_t n, float *norm_out);
-/* The same norm for callers that cannot allocate device memory (a framework
+/* The same norm (up to summation order: the two may differ in the last bit)
+ * for callers that cannot allocate device memory (a framework
  * whose allocator owns the whole GPU, a runtime with a fixed memory budget):
  * no cudaMalloc, no tl_init needed.  No counterpart in the reference.  Uses a
  * scratch array compiled into the library (128 KiB per device that loads it,
@@ -217,8 +233,10 @@ int tl_model_step_zero1(void *handle, float *P, float *G, float *M_shard, float 
 int tl_ckpt_save_bundle(const char *path, const int *hdr11, const float *P, size_t n, const void *tok_blob,
                         int tok_len);
 /* model_load (tinylm.c:1915-1938) for TLM1-TLM4: header into hdr11 (missing
- * fields 0); when P is not NULL, n_expected parameters into P.  *n_in_file
- * (may be NULL) = floats after the header (parameters + tokenizer tail). */
+ * fields 0); when P is not NULL, n_expected parameters into P (TL_EINVAL if
+ * the file is shorter).  *n_in_file (may be NULL) = 4-byte words after the
+ * header (parameters + tokenizer length + tokenizer blob): an upper bound on
+ * the parameter count, not the count. */
 int tl_ckpt_load_bundle(const char *path, int *hdr11, float *P, size_t n_expected, size_t *n_in_file);
 /* TOPT sidecar, opt_save / opt_load (tinylm.c:2526-2539): "TOPT", iter, M[n],
  * V[n].  Create the file once, then write / read any range of M and V -- each
@@ -276,8 +294,11 @@ int tl_zero1_step(float *P, float *G, float *M_shard, float *V_shard, size_t n,
  * memory that CUDA IPC can share) -- a collective call; tl_zero1_step_p2p must
  * then be given exactly those buffers.  Device waits are bounded by
  * TL_DIST_TIMEOUT_MS: on expiry the step records an error that
- * tl_device_status() returns as TL_ETIMEOUT and the rest of the step touches
- * no peer memory.  Up to 8 ranks.  No counterpart in the reference. */
+ * tl_device_status() returns as TL_ETIMEOUT, and from then on no kernel of
+ * this or any later step touches peer memory (each later step records the
+ * error again); once tl_device_status has reported it, tl_zero1_step_p2p
+ * returns TL_ETIMEOUT without launching until tl_zero1_p2p_release and a new
+ * tl_zero1_p2p_register.  Up to 8 ranks.  No counterpart in the reference. */
 int tl_zero1_p2p_register(float *P, float *G, size_t n);
 int tl_zero1_step_p2p(float *P, float *G, float *M_shard, float *V_shard, size_t n,
                       float lr, float b1, float b2, float wd, int t, float max_norm,

@@ -5,6 +5,9 @@ Two CPU legs, loaded with ctypes:
                                      arithmetic (oracle/tl_oracle.c)
   ref()  -> oracle/_ref/libtlref.so  the reference's own tinylm.c compiled
                                      unmodified (oracle/Makefile, ref_harness.c)
+and the drop-in proof (oracle/dropin_patch.py, `make dropin`): the reference
+with libtinylm_cuda at its five seams, as the CLI oracle/_ref/tinylm_cuda and
+the harness oracle/_ref/libtlref_cuda.so (DROPIN_* paths below).
 
 Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline legs may use
 this package, and only as the checker or the timed CPU baseline; the product
@@ -19,7 +22,12 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 PORT_PATH = os.path.join(HERE, "libtl_oracle.so")
 REF_PATH = os.path.join(HERE, "_ref", "libtlref.so")
-REF_SRC = "/root/reference/tinylm.c"
+DROPIN_EXE = os.path.join(HERE, "_ref", "tinylm_cuda")
+DROPIN_LIB = os.path.join(HERE, "_ref", "libtlref_cuda.so")
+# Where the reference sources are read at build time (overridable, like the
+# Makefile's REF_DIR).  Machines without them use the prebuilt _ref files.
+REF_DIR = os.environ.get("TL_REF_DIR", "/root/reference")
+REF_SRC = os.path.join(REF_DIR, "tinylm.c")
 
 _fp = ctypes.POINTER(ctypes.c_float)
 _ip = ctypes.POINTER(ctypes.c_int)
@@ -28,11 +36,13 @@ _f, _i, _sz, _u64, _d = ctypes.c_float, ctypes.c_int, ctypes.c_size_t, ctypes.c_
 
 def build(ref=True):
     """Compile the restatement and, when the reference sources are present, the
-    reference leg.  On a machine without them the prebuilt _ref library is used."""
+    reference leg and the drop-in build (which links the in-tree
+    libtinylm_cuda.so, so build that first).  On a machine without the sources
+    the prebuilt _ref files are used."""
     targets = ["port"]
     if ref and os.path.exists(REF_SRC):
-        targets.append("ref")
-    subprocess.run(["make", "-s", "-C", HERE] + targets, check=True)
+        targets += ["ref", "dropin"]
+    subprocess.run(["make", "-s", "-C", HERE, "REF_DIR=" + REF_DIR] + targets, check=True)
 
 
 def fptr(a):
@@ -79,42 +89,59 @@ def ref():
     if _ref is None:
         if not os.path.exists(REF_PATH):
             raise FileNotFoundError(f"{REF_PATH} not built (needs the reference sources)")
-        L = ctypes.CDLL(REF_PATH)
-        L.tlref_init.argtypes = [_i, _u64]
-        L.tlref_seed.argtypes = [_u64]
-        L.tlref_xorshift.restype = _u64
-        L.tlref_fill_normal.argtypes = [_fp, _sz, _f]
-        for nm in ("tlref_mm", "tlref_mm_bt", "tlref_mm_atb"):
-            getattr(L, nm).argtypes = [_fp, _fp, _fp, _i, _i, _i]
-        L.tlref_adamw.argtypes = [_fp, _fp, _fp, _fp, _sz, _f, _f, _f, _f, _i, _f]
-        L.tlref_gradnorm.argtypes = [_fp, _sz]
-        L.tlref_gradnorm.restype = _f
-        L.tlref_model_new.argtypes = [_ip, _i, _i, _u64]
-        L.tlref_model_new.restype = ctypes.c_void_p
-        L.tlref_model_nparams.argtypes = [ctypes.c_void_p]
-        L.tlref_model_nparams.restype = _sz
-        L.tlref_model_buf.argtypes = [ctypes.c_void_p, _i]
-        L.tlref_model_buf.restype = _fp
-        L.tlref_model_tokens.argtypes = [ctypes.c_void_p, _i]
-        L.tlref_model_tokens.restype = _ip
-        L.tlref_model_logits.argtypes = [ctypes.c_void_p]
-        L.tlref_model_logits.restype = _fp
-        L.tlref_model_forward.argtypes = [ctypes.c_void_p]
-        L.tlref_model_forward.restype = _f
-        L.tlref_model_fwd_bwd.argtypes = [ctypes.c_void_p]
-        L.tlref_model_fwd_bwd.restype = _f
-        L.tlref_model_step.argtypes = [ctypes.c_void_p, _f, _i, ctypes.POINTER(_f)]
-        L.tlref_model_step.restype = _f
-        L.tlref_model_free.argtypes = [ctypes.c_void_p]
-        L.tlref_max_threads.restype = _i
-        _u16p = ctypes.POINTER(ctypes.c_uint16)
-        L.tlref_train.argtypes = [_ip, _i, _i, _i, _f, _u64, _u16p, _sz, _u16p, _sz, ctypes.c_char_p,
-                                  ctypes.c_char_p, ctypes.c_char_p, _i, ctypes.c_char_p, ctypes.c_char_p]
-        L.tlref_train.restype = _i
-        L.tlref_model_load.argtypes = [ctypes.c_char_p, _ip, _fp, _sz]
-        L.tlref_model_load.restype = _sz
-        _ref = L
+        _ref = _bind_ref(ctypes.CDLL(REF_PATH))
     return _ref
+
+
+def has_dropin():
+    return os.path.exists(DROPIN_EXE) and os.path.exists(DROPIN_LIB)
+
+
+def ref_cuda():
+    """The drop-in harness: the reference's step with its GEMMs, norm and AdamW
+    in libtinylm_cuda (host-buffer mode).  Load it in a process of its own:
+    its seams switch the library's host-buffer mode on for the device."""
+    if not os.path.exists(DROPIN_LIB):
+        raise FileNotFoundError(f"{DROPIN_LIB} not built (make -C oracle dropin)")
+    return _bind_ref(ctypes.CDLL(DROPIN_LIB))
+
+
+def _bind_ref(L):
+    """ctypes signatures of the harness exports (ref_harness.c)."""
+    L.tlref_init.argtypes = [_i, _u64]
+    L.tlref_seed.argtypes = [_u64]
+    L.tlref_xorshift.restype = _u64
+    L.tlref_fill_normal.argtypes = [_fp, _sz, _f]
+    for nm in ("tlref_mm", "tlref_mm_bt", "tlref_mm_atb"):
+        getattr(L, nm).argtypes = [_fp, _fp, _fp, _i, _i, _i]
+    L.tlref_adamw.argtypes = [_fp, _fp, _fp, _fp, _sz, _f, _f, _f, _f, _i, _f]
+    L.tlref_gradnorm.argtypes = [_fp, _sz]
+    L.tlref_gradnorm.restype = _f
+    L.tlref_model_new.argtypes = [_ip, _i, _i, _u64]
+    L.tlref_model_new.restype = ctypes.c_void_p
+    L.tlref_model_nparams.argtypes = [ctypes.c_void_p]
+    L.tlref_model_nparams.restype = _sz
+    L.tlref_model_buf.argtypes = [ctypes.c_void_p, _i]
+    L.tlref_model_buf.restype = _fp
+    L.tlref_model_tokens.argtypes = [ctypes.c_void_p, _i]
+    L.tlref_model_tokens.restype = _ip
+    L.tlref_model_logits.argtypes = [ctypes.c_void_p]
+    L.tlref_model_logits.restype = _fp
+    L.tlref_model_forward.argtypes = [ctypes.c_void_p]
+    L.tlref_model_forward.restype = _f
+    L.tlref_model_fwd_bwd.argtypes = [ctypes.c_void_p]
+    L.tlref_model_fwd_bwd.restype = _f
+    L.tlref_model_step.argtypes = [ctypes.c_void_p, _f, _i, ctypes.POINTER(_f)]
+    L.tlref_model_step.restype = _f
+    L.tlref_model_free.argtypes = [ctypes.c_void_p]
+    L.tlref_max_threads.restype = _i
+    _u16p = ctypes.POINTER(ctypes.c_uint16)
+    L.tlref_train.argtypes = [_ip, _i, _i, _i, _f, _u64, _u16p, _sz, _u16p, _sz, ctypes.c_char_p,
+                              ctypes.c_char_p, ctypes.c_char_p, _i, ctypes.c_char_p, ctypes.c_char_p]
+    L.tlref_train.restype = _i
+    L.tlref_model_load.argtypes = [ctypes.c_char_p, _ip, _fp, _sz]
+    L.tlref_model_load.restype = _sz
+    return L
 
 
 # ---- numpy-level helpers (restatement leg) ---------------------------------

@@ -244,6 +244,38 @@ def test_gemm_sweep_shapes_sampled(cuda, tc_engine, M, K, N):
         ops.set_gemm_engine(0)
 
 
+SWEEP = [(M, K, N) for M in (16384, 65536) for K in (256, 512, 1024, 2816) for N in (256, 512, 1024, 2816)]
+
+
+@pytest.mark.parametrize("M,K,N", SWEEP)
+def test_gemm_sweep_every_shape_default_engine(cuda, M, K, N):
+    """All 32 (M, K, N) shapes of BASELINE config 3 x the three primitives on
+    the engine the library picks by itself, at full size, against float64
+    products of sampled rows (Y, dX) and columns (dW) computed on the device."""
+    X = torch.randn(M * K, device=cuda, generator=torch.Generator(device=cuda).manual_seed(M + K))
+    W = torch.randn(K * N, device=cuda, generator=torch.Generator(device=cuda).manual_seed(K + N)) * 0.02
+    dY = torch.randn(M * N, device=cuda, generator=torch.Generator(device=cuda).manual_seed(M + N))
+    Y = torch.empty(M * N, device=cuda)
+    dX = torch.randn(M * K, device=cuda, generator=torch.Generator(device=cuda).manual_seed(7)) * 0.1
+    dW = torch.randn(K * N, device=cuda, generator=torch.Generator(device=cuda).manual_seed(8)) * 0.1
+    dX0, dW0 = dX.double(), dW.double()          # the accumulate primitives add to what is there
+    ops.mm(Y, X, W, M, K, N)
+    ops.mm_bt(dX, dY, W, M, K, N)
+    ops.mm_atb(dW, X, dY, M, K, N)
+    torch.cuda.synchronize()
+    device_ok()
+    g = torch.Generator(device="cpu").manual_seed(M * 7 + K * 3 + N)
+    rows = torch.randperm(M, generator=g)[:128].sort().values.to(cuda)
+    cols = torch.randperm(N, generator=g)[:32].sort().values.to(cuda)
+    Xd, Wd, dYd = X.view(M, K).double(), W.view(K, N).double(), dY.view(M, N).double()
+    want_y = Xd[rows] @ Wd
+    want_dx = dX0.view(M, K)[rows] + dYd[rows] @ Wd.T
+    want_dw = dW0.view(K, N)[:, cols] + Xd.T @ dYd[:, cols]
+    for got, want in ((Y.view(M, N)[rows], want_y), (dX.view(M, K)[rows], want_dx), (dW.view(K, N)[:, cols], want_dw)):
+        assert torch.isfinite(got).all()
+        assert gemm_rel(got.cpu().numpy(), want.cpu().numpy()) <= GEMM_REL_TOL
+
+
 def _sweep_shape_sampled(cuda, M, K, N):
     rng = np.random.default_rng(3)
     X = torch.randn(M * K, device=cuda, generator=torch.Generator(device=cuda).manual_seed(1))

@@ -1,7 +1,7 @@
 """tl_grad_norm_noalloc: the gradient norm for callers that cannot allocate
 device memory (a host framework whose allocator owns the whole GPU, or a
 runtime that fixes its memory budget at start-up).  It must give the same norm
-as tl_grad_norm, through the C ABI, on two calls in a row that share its fixed
+as tl_grad_norm and as the oracle, through the C ABI, on two calls in a row that share its fixed
 scratch array, and refuse sizes beyond that array's limit.
 
 The file name sorts last so that a run stopping at the first failure has
@@ -12,6 +12,7 @@ import ctypes
 import pytest
 import torch
 
+import oracle
 from helpers import NORM_RTOL
 from tinylm_c_b200 import _lib, ops
 
@@ -43,6 +44,9 @@ def test_noalloc_norm_matches_grad_norm_on_consecutive_calls():
         _lib.check(L.tl_grad_norm(g.data_ptr(), n, ref.data_ptr()))
         torch.cuda.synchronize()
         assert out.item() == pytest.approx(ref.item(), rel=NORM_RTOL), (n, out.item(), ref.item())
+        # and against the oracle's norm of the same values (double sum, one rounding)
+        want = oracle.grad_norm(g.cpu().numpy())
+        assert out.item() == pytest.approx(want, rel=NORM_RTOL), (n, out.item(), want)
         assert out.item() > 0
 
 

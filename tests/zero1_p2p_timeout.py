@@ -2,7 +2,8 @@
 each).  Both ranks register; then rank 1 never calls the step (a rank that
 does not join, injected on the host).  Rank 0's step must come back on its
 own: its bounded device wait expires after TL_DIST_TIMEOUT_MS and
-tl_device_status() reports TL_ETIMEOUT.  Rank 1 touches nothing on the device
+tl_device_status() reports TL_ETIMEOUT; a second step is then refused with
+TL_ETIMEOUT.  Rank 1 touches nothing on the device
 meanwhile and both leave through a host barrier."""
 import datetime
 import os
@@ -38,6 +39,14 @@ def main():
         rc = _lib.lib().tl_device_status()
         print("STATUS", rc, _lib.lib().tl_last_error().decode(), flush=True)
         ok = rc == _lib.TL_ETIMEOUT and torch.all(P == 0).item()
+        # A later step is refused (nothing launched) until release + register.
+        try:
+            z.step(P, G, M, V, 1e-3, 0.9, 0.95, 0.1, 2, 1.0, None)
+            again = None
+        except _lib.TLError as e:
+            again = e.code
+        print("SECOND STEP", again, flush=True)
+        ok = ok and again == _lib.TL_ETIMEOUT and torch.all(P == 0).item()
     dist.barrier()                      # rank 1 waited here, idle
     z.close()
     dist.barrier()

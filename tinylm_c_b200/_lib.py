@@ -34,6 +34,7 @@ SIGNATURES = {
     "tl_memset": (_c_int, [_c_void_p, _c_int, _c_size]),
     "tl_sync": (_c_int, []),
     "tl_device_status": (_c_int, []),
+    "tl_set_host_buffers": (_c_int, [_c_int]),
     "tl_trace_enable": (_c_int, [_c_int]),
     "tl_trace_reset": (_c_int, []),
     "tl_trace_get": (_c_int, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_longlong)]),

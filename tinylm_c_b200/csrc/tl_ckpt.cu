@@ -88,7 +88,10 @@ TL_API int tl_ckpt_save_bundle(const char *path, const int *hdr11, const float *
 
 // Reads the header (hdr11 gets V,D,L,H,KV,F,T,eot,tmpl,n_mtp,n_exp; fields the
 // file's version lacks are 0) and, when P is not NULL, the n_expected
-// parameters.  *n_in_file receives the byte count of the parameter block / 4.
+// parameters.  *n_in_file receives the number of 4-byte words after the
+// header: the parameter block plus the int32 tokenizer length and the
+// tokenizer blob, so it is an upper bound on the parameter count (a bundle of
+// n parameters has *n_in_file >= n + 1), not the count itself.
 TL_API int tl_ckpt_load_bundle(const char *path, int *hdr11, float *P, size_t n_expected, size_t *n_in_file) {
   if (!path || !hdr11) return set_error(TL_EINVAL, "NULL argument");
   FILE *f = fopen(path, "rb");
@@ -118,7 +121,10 @@ TL_API int tl_ckpt_load_bundle(const char *path, int *hdr11, float *P, size_t n_
   fseek(f, here, SEEK_SET);
   if (n_in_file) *n_in_file = (size_t)(end - here) / 4;
   int rc = TL_OK;
-  if (P) rc = read_floats(f, P, n_expected, "parameters");
+  if (P && (size_t)(end - here) < n_expected * 4 + 4)
+    rc = set_error(TL_EINVAL, "%s holds fewer than the %zu expected parameters and the tokenizer length", path,
+                   n_expected);
+  if (P && !rc) rc = read_floats(f, P, n_expected, "parameters");
   fclose(f);
   return rc;
 }

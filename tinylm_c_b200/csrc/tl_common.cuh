@@ -30,6 +30,9 @@ struct DeviceCtx {
   float *gemm_ws = nullptr;            // split-K partial outputs
   size_t gemm_ws_floats = 0;
   unsigned *gemm_amax = nullptr;       // [8] operand max |x| (float bits) for the fp16-split GEMM
+  bool host_buffers = false;           // tl_set_host_buffers: compute calls may take host memory
+  char *host_arena = nullptr;          // staging copies of host operands (grown on demand)
+  size_t host_arena_bytes = 0;
 };
 constexpr size_t kGemmWorkspaceFloats = 16u << 20;  // 64 MiB
 
@@ -37,6 +40,15 @@ DeviceCtx *ctx();                          // context of the current device, or 
 int set_error(int code, const char *fmt, ...);
 int cuda_check(cudaError_t e, const char *what);
 int check_device_ptr(const void *p, const char *name);  // TL_EPTR for host memory
+bool is_host_ptr(const void *p);                        // pageable or pinned host memory
+
+// Host-buffer mode (tl_host.cu): the compute entry points with host operands,
+// staged through the context's arena; synchronous.
+enum class GemmOp;
+int host_gemm(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, int M, int K, int N);
+int host_grad_norm(DeviceCtx *c, const float *G, size_t n, float *norm_out);
+int host_adamw(DeviceCtx *c, float *P, const float *G, float *M, float *V, size_t n, float lr, float b1, float b2,
+               float wd, int t, float gscale);
 
 }  // namespace tl
 

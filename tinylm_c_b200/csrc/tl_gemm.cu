@@ -18,6 +18,8 @@ static int gemm_entry(GemmOp op, float *C, const float *A, const float *B, int M
   gemm_dims(op, M, K, N, &I, &J, &R);
   if (I == 0 || J == 0) return TL_OK;
   int rc;
+  if (c->host_buffers && (is_host_ptr(C) || (R > 0 && (is_host_ptr(A) || is_host_ptr(B)))))
+    return host_gemm(c, op, C, A, B, M, K, N);
   if ((rc = check_device_ptr(C, "output"))) return rc;
   if (R > 0) {
     if ((rc = check_device_ptr(A, "first operand"))) return rc;

@@ -19,6 +19,7 @@
 // All calls share the one array: calls that overlap on the GPU (two streams,
 // or two host threads on one device) race on it and must be serialised by the
 // caller.
+#include <atomic>
 #include "tl_common.cuh"
 
 #define TL_NOALLOC_CHUNK 65536u
@@ -34,7 +35,10 @@ struct Scratch {
 
 static __device__ __align__(256) Scratch g_scratch;
 
-static Scratch *g_scratch_addr[kMaxDevices] = {};
+// Device address of g_scratch per device, looked up on first use.  Atomic:
+// two host threads making their first call on one device may both look it up
+// (they store the same value).
+static std::atomic<Scratch *> g_scratch_addr[kMaxDevices] = {};
 
 // Block b sums squares of its chunk [b*CHUNK, min(n, (b+1)*CHUNK)) in double;
 // the last block to finish adds the partials in index order, writes the norm
@@ -86,13 +90,15 @@ static int scratch_for_current_device(Scratch **out) {
   int dev = -1;
   TL_TRY_CUDA(cudaGetDevice(&dev));
   if (dev < 0 || dev >= kMaxDevices) return set_error(TL_EINVAL, "device %d out of range", dev);
-  if (!g_scratch_addr[dev]) {
+  Scratch *addr = g_scratch_addr[dev].load(std::memory_order_acquire);
+  if (!addr) {
     void *p = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_scratch);
     if (e != cudaSuccess || !p) return cuda_check(e != cudaSuccess ? e : cudaErrorInvalidSymbol, "cudaGetSymbolAddress(no-alloc scratch)");
-    g_scratch_addr[dev] = static_cast<Scratch *>(p);
+    addr = static_cast<Scratch *>(p);
+    g_scratch_addr[dev].store(addr, std::memory_order_release);
   }
-  *out = g_scratch_addr[dev];
+  *out = addr;
   return TL_OK;
 }
 
@@ -101,8 +107,10 @@ static int scratch_for_current_device(Scratch **out) {
 
 using namespace tl;
 
-// Same result as tl_grad_norm (sqrt of a double sum of squares, rounded to
-// float) without any device allocation.  norm_dev: device float; stream: a
+// The norm tl_grad_norm computes (sqrt of a double sum of squares, rounded to
+// float), up to summation order -- 64 Ki-element chunks here, a fixed
+// 1184-block grid there, so the two may differ in the last bit -- without any
+// device allocation.  norm_dev: device float; stream: a
 // cudaStream_t (NULL = legacy default stream).  n is limited to
 // TL_NOALLOC_MAX_PARTIALS * TL_NOALLOC_CHUNK = 2^30 elements.  Needs no tl_init.
 TL_API int tl_grad_norm_noalloc(const float *G, size_t n, float *norm_dev, void *stream) {

@@ -207,6 +207,7 @@ TL_API int tl_grad_norm(const float *G, size_t n, float *norm_out) {
   TL_REQUIRE_CTX(c);
   int rc;
   if (!norm_out) return set_error(TL_EINVAL, "norm_out is NULL");
+  if (c->host_buffers && n && is_host_ptr(G)) return host_grad_norm(c, G, n, norm_out);
   if (n && (rc = check_device_ptr(G, "G"))) return rc;
   cudaPointerAttributes at;
   bool host_out = cudaPointerGetAttributes(&at, norm_out) != cudaSuccess ||
@@ -227,6 +228,8 @@ TL_API int tl_adamw_step(float *P, const float *G, float *M, float *V, size_t n,
   if (t < 1) return set_error(TL_EINVAL, "step t must be >= 1 (got %d)", t);
   if (n == 0) return TL_OK;
   int rc;
+  if (c->host_buffers && (is_host_ptr(P) || is_host_ptr(G) || is_host_ptr(M) || is_host_ptr(V)))
+    return host_adamw(c, P, G, M, V, n, lr, b1, b2, wd, t, gscale);
   if ((rc = check_adam_ptrs(P, G, M, V))) return rc;
   return launch_adamw(c, P, G, M, V, n, lr, b1, b2, wd, t, gscale, nullptr);
 }

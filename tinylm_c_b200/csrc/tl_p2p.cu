@@ -21,8 +21,12 @@
 // IPC at registration; the mailboxes (flags and shard sums) are library
 // buffers.  Flags carry the step epoch, so nothing is reset between steps.
 // Every wait is bounded (TL_DIST_TIMEOUT_MS, %globaltimer): on expiry the rank
-// records a device error code (tl_device_status -> TL_ETIMEOUT), sets its
-// abort word and the remaining kernels of the step skip all peer traffic.
+// records a device error code (tl_device_status -> TL_ETIMEOUT) and sets its
+// abort word.  From then on every kernel of this and later steps returns at
+// once, touching no peer memory, and records error 23 again, so each later
+// step is reported too; once tl_device_status has seen one of these codes the
+// host refuses further steps (TL_ETIMEOUT) until the caller releases the
+// peer set and registers again.
 // No TMA and no multicast: peer memory is touched only by plain loads/stores.
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -39,7 +43,7 @@ int dist_allgather_bytes(const void *send_dev, void *recv_dev, size_t bytes);
 
 constexpr int kMaxRanks = 8;
 enum { FLAG_GRAD = 0, FLAG_SUMSQ = 1, FLAG_PARAM = 2, NFLAGS = 3 };
-constexpr int ERR_WAIT_GRAD = 20, ERR_WAIT_SUMSQ = 21, ERR_WAIT_PARAM = 22;
+constexpr int ERR_WAIT_GRAD = 20, ERR_WAIT_SUMSQ = 21, ERR_WAIT_PARAM = 22, ERR_ABORTED = 23;
 
 // One per rank in its own device memory, written by every peer.
 struct Mailbox {
@@ -62,6 +66,7 @@ struct P2PCtx {
   Mailbox *own = nullptr;
   PeerSet peers{};
   unsigned long long epoch = 0;
+  bool aborted = false;   // tl_device_status saw an expired wait of this rank
   std::vector<void *> opened;
 };
 static P2PCtx g_p2p[kMaxDevices];
@@ -74,6 +79,13 @@ static unsigned long long wait_limit_ns() {
 }
 
 // ---------------------------------------------------------------- kernels
+// True (and error 23 recorded) when an earlier wait of this rank expired.
+__device__ __forceinline__ bool p2p_aborted(const Mailbox *own, int *err) {
+  if (!*(volatile const int *)&own->abort) return false;
+  if (threadIdx.x == 0 && blockIdx.x == 0) atomicExch(err, ERR_ABORTED);
+  return true;
+}
+
 __device__ __forceinline__ unsigned long long gtime() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -94,7 +106,7 @@ __global__ void p2p_signal_wait_kernel(PeerSet ps, Mailbox *own, int rank, int w
                                        unsigned long long epoch, unsigned long long limit_ns, int *err,
                                        int code) {
   const int lane = threadIdx.x;
-  if (*(volatile int *)&own->abort) return;
+  if (p2p_aborted(own, err)) return;
   __threadfence_system();
   if (lane < world) st_release_sys(&ps.mb[lane]->flag[kind][rank], epoch);
   bool ok = true;
@@ -115,10 +127,10 @@ __global__ void p2p_signal_wait_kernel(PeerSet ps, Mailbox *own, int rank, int w
 // block publishes the shard total to every mailbox.
 __global__ void __launch_bounds__(kNormThreads)
 p2p_rs_sumsq_kernel(PeerSet ps, Mailbox *own, int rank, int world, size_t shard, double *partials,
-                    unsigned int *ticket, unsigned long long epoch) {
+                    unsigned int *ticket, unsigned long long epoch, int *err) {
   __shared__ double smem[32];
   __shared__ bool is_last;
-  if (*(volatile int *)&own->abort) return;
+  if (p2p_aborted(own, err)) return;
   const size_t off = (size_t)rank * shard;
   const size_t n4 = shard / 4;
   float4 *Gme = reinterpret_cast<float4 *>(ps.G[rank] + off);
@@ -161,7 +173,7 @@ p2p_rs_sumsq_kernel(PeerSet ps, Mailbox *own, int rank, int world, size_t shard,
 __global__ void p2p_clip_kernel(Mailbox *own, int world, unsigned long long epoch, float max_norm,
                                 float *norm_out, float *gscale_out, unsigned long long limit_ns, int *err) {
   const int lane = threadIdx.x;
-  if (*(volatile int *)&own->abort) return;
+  if (p2p_aborted(own, err)) return;
   bool ok = true;
   double mine = 0.0;
   if (lane < world) {
@@ -187,8 +199,8 @@ __global__ void p2p_clip_kernel(Mailbox *own, int world, unsigned long long epoc
 // AdamW on this rank's shard; the updated parameters go to every rank's P.
 __global__ void __launch_bounds__(256)
 p2p_adamw_kernel(PeerSet ps, Mailbox *own, int rank, int world, size_t shard, float4 *__restrict__ M,
-                 float4 *__restrict__ V, AdamArgs a) {
-  if (*(volatile int *)&own->abort) return;
+                 float4 *__restrict__ V, AdamArgs a, int *err) {
+  if (p2p_aborted(own, err)) return;
   const float gs = __ldg(a.gscale_ptr);
   const size_t off = (size_t)rank * shard;
   const size_t n4 = shard / 4;
@@ -235,9 +247,16 @@ static int alloc_base(const void *p, unsigned long long *base) {
 static void release(P2PCtx &x) {
   for (void *p : x.opened) cudaIpcCloseMemHandle(p);
   x.opened.clear();
+  x.aborted = false;
   if (x.own) cudaFree(x.own);
   x.own = nullptr;
   x.ready = false;
+}
+
+// tl_device_status found a peer-wait code (20-23) on `device`.
+void p2p_mark_aborted(int device, int code) {
+  if (device >= 0 && device < kMaxDevices && g_p2p[device].ready && code >= ERR_WAIT_GRAD && code <= ERR_ABORTED)
+    g_p2p[device].aborted = true;
 }
 
 void p2p_release_device(int device) {
@@ -349,6 +368,9 @@ TL_API int tl_zero1_step_p2p(float *P, float *G, float *M_shard, float *V_shard,
   if (!x.ready) return set_error(TL_ENOINIT, "tl_zero1_p2p_register() not called for this device");
   if (P != x.P || G != x.G || n != x.n)
     return set_error(TL_EINVAL, "P, G and n must be the buffers registered with tl_zero1_p2p_register");
+  if (x.aborted)
+    return set_error(TL_ETIMEOUT, "an earlier peer wait of this rank expired; release the peer set "
+                                  "(tl_zero1_p2p_release) and register again");
   if (t < 1) return set_error(TL_EINVAL, "step t must be >= 1 (got %d)", t);
   if (!(max_norm > 0.0f)) return set_error(TL_EINVAL, "max_norm must be > 0");
   int rc;
@@ -366,7 +388,8 @@ TL_API int tl_zero1_step_p2p(float *P, float *G, float *M_shard, float *V_shard,
   {
     TraceScope ts(c, "p2p_rs_sumsq");
     p2p_rs_sumsq_kernel<<<kNormBlocks, kNormThreads, 0, c->stream>>>(x.peers, x.own, x.rank, x.world, x.shard,
-                                                                     c->norm_partials, c->norm_ticket, ep);
+                                                                     c->norm_partials, c->norm_ticket, ep,
+                                                                     c->err_flag);
     TL_TRY_CUDA(cudaGetLastError());
   }
   float *gscale = c->scalars + 1;
@@ -381,7 +404,8 @@ TL_API int tl_zero1_step_p2p(float *P, float *G, float *M_shard, float *V_shard,
     if (blocks < 1) blocks = 1;
     p2p_adamw_kernel<<<(unsigned)blocks, 256, 0, c->stream>>>(x.peers, x.own, x.rank, x.world, x.shard,
                                                                reinterpret_cast<float4 *>(M_shard),
-                                                               reinterpret_cast<float4 *>(V_shard), a);
+                                                               reinterpret_cast<float4 *>(V_shard), a,
+                                                               c->err_flag);
     TL_TRY_CUDA(cudaGetLastError());
   }
   {

@@ -5,6 +5,8 @@
 
 namespace tl {
 
+void p2p_mark_aborted(int device, int code);   // tl_p2p.cu
+
 static DeviceCtx g_ctx[kMaxDevices];
 static thread_local char g_err[512] = "";
 
@@ -140,6 +142,7 @@ TL_API int tl_device_status(void) {
     TL_TRY_CUDA(cudaMemset(c->err_flag, 0, sizeof(int)));
     if (code >= 100)
       return set_error(TL_EINVAL, "a device-side input check failed (code %d: token id outside [0, V))", code);
+    p2p_mark_aborted(c->device, code);
     return set_error(TL_ETIMEOUT, "a bounded device-side wait expired (site %d); the kernel returned early", code);
   }
   return TL_OK;
