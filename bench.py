@@ -72,6 +72,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-adamw-line", action="store_true", help="train: skip the config-2 AdamW sub-measurement")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="train at N=1: skip the sub-measurements of BASELINE configs 1-4 in the same line")
     ap.add_argument("--shape", default="", help="gemm workload: one M,K,N instead of the sweep")
     ap.add_argument("--op", default="all", choices=["all", "mm", "mm_bt", "mm_atb"], help="gemm workload: primitive")
     ap.add_argument("--zero1", default="nccl", choices=["nccl", "p2p"],
@@ -599,9 +601,10 @@ def gemm_shapes(args):
     return [(M, K, N) for M in GEMM_SWEEP_M for K in GEMM_SWEEP_KN for N in GEMM_SWEEP_KN]
 
 
-def run_gemm(args, rk):
+def run_gemm(args, rk, shapes=None):
     """X@W, X@W^T, X^T@W over the config-3 sweep (X~N(0,1), W~N(0,0.02),
-    dY~N(0,1)); per shape and primitive: warm-up, then K timed calls."""
+    dY~N(0,1)), or over `shapes`; per shape and primitive: warm-up, then K
+    timed calls."""
     torch, ops = rk.torch, rk.ops
     dev = rk.dev
     ops_sel = ["mm", "mm_bt", "mm_atb"] if args.op == "all" else [args.op]
@@ -609,7 +612,7 @@ def run_gemm(args, rk):
     tot_flop = tot_ms = 0.0
     launches = 0
     clocks_all = []
-    for (M, K, N) in gemm_shapes(args):
+    for (M, K, N) in (shapes or gemm_shapes(args)):
         g = torch.Generator(device=dev).manual_seed(M + K + N)
         X = torch.randn(M * K, device=dev, generator=g)
         W = torch.randn(K * N, device=dev, generator=g) * 0.02
@@ -646,8 +649,11 @@ def run_gemm(args, rk):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(tot_ms / max(1, len(results)), 4),
             "higher_is_better": True, "scaling": "replicas", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (X~N(0,1), W~N(0,0.02), dY~N(0,1), seeded)",
-            "config": {"workload": "config3_gemm_sweep" if not args.shape else "config3_gemm_one",
-                       "shapes": len(results), "value_is": "total FLOP / total time over the sweep"},
+            "config": {"workload": ("config3_gemm_sample" if shapes else "config3_gemm_sweep") if not args.shape
+                       else "config3_gemm_one",
+                       "shapes": len(results), "value_is": "total FLOP / total time over the sweep",
+                       "l2": "sample: >= 248 MB of operands per call (> 126 MB L2), no flush; full sweep: "
+                             "the smallest shapes (16384 x 256 x 256: 33 MB) repeat from L2"},
             "roofline": {"kernel": kname, "bound": "tensor", "unit": "TFLOP/s",
                          "achieved": round(agg, 2), "best_shape": best, "peak": round(peak, 1),
                          "peak_source": f"{peak_kind} bf16 burst {bf16} TFLOP/s / {div:g} ({why})",
@@ -655,16 +661,17 @@ def run_gemm(args, rk):
             "clocks": clocks_all[-1] if clocks_all else {}, "gpu_launches": launches, "sweep": results}
 
 
-def reference_gemm(args):
+def reference_gemm(args, shapes=None):
     """The reference's mm/mm_bt/mm_atb (tinylm.c:439-537) on a row sample of
-    the sweep (M scaled down to 1024 rows; per-row work identical)."""
+    the sweep or of `shapes` (M scaled down to 1024 rows; per-row work
+    identical)."""
     import numpy as np
     import oracle
     R = oracle.ref()
     threads = cpu_threads()
     R.tlref_init(threads, 0)
     tot_flop = tot_s = 0.0
-    shapes = gemm_shapes(args)
+    shapes = shapes or gemm_shapes(args)
     for (M, K, N) in shapes[: (1 if args.shape else len(shapes))]:
         Ms = min(M, 1024)
         rng = np.random.default_rng(0)
@@ -741,7 +748,7 @@ def main():
     elif args.workload == "adamw":
         out = run_adamw(args, rk, args.n)
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
-            steps = int(os.environ.get("TL_CPU_BASELINE_STEPS", "5"))
+            steps = cpu_baseline_steps()
             gbs, sec, threads = reference_adamw(args.n, steps, 1)
             out["cpu_baseline"] = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "reference",
                                    "sample": f"tinylm.c adamw+global_gradnorm (oracle/_ref), n={args.n}, median of {steps} steps"}
@@ -755,16 +762,77 @@ def main():
                      "config2_frac_of_hbm": a["roofline"]["frac"], "config2_ms_per_step": a["ms_per_step"],
                      "metric": ADAMW_METRIC})
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
-            steps = int(os.environ.get("TL_CPU_BASELINE_STEPS", "1"))
-            tps, sec, threads, B = reference_train(args.workload, steps, 1)
-            out["cpu_baseline"] = {"value": round(tps, 2), "unit": "tokens/s", "cores": threads, "kind": "reference",
-                                   "sample": f"tinylm.c step at batch {B}x{T_CTX} (same per-token work), "
-                                             f"median of {steps} step(s) after 1 warm-up",
-                                   "s_per_step": round(sec, 3)}
+            out["cpu_baseline"] = cpu_baseline_train(args.workload)
+        if world == 1 and args.workload == "train" and not args.no_configs:
+            configs = run_other_configs(args, rk)
+            if rank == 0:
+                out["configs"] = configs
     if rank == 0:
         emit(out)
     rk.close()
     return 0
+
+
+def cpu_baseline_steps():
+    """Timed reference steps per CPU baseline (median taken; at least 3)."""
+    return max(3, int(os.environ.get("TL_CPU_BASELINE_STEPS", "3")))
+
+
+def cpu_baseline_train(workload):
+    steps = cpu_baseline_steps()
+    tps, sec, threads, B = reference_train(workload, steps, 1)
+    return {"value": round(tps, 2), "unit": "tokens/s", "cores": threads, "kind": "reference",
+            "sample": f"tinylm.c forward+backward+gradnorm+adamw at batch {B}x{T_CTX} (same per-token work), "
+                      f"median of {steps} steps after 1 warm-up",
+            "s_per_step": round(sec, 3)}
+
+
+# The BASELINE configs other than the headline, measured in the same run (N=1):
+# config 1 and 4 training steps, config 2 AdamW+clip with its own CPU baseline
+# and end-to-end figure, and a sample of the config-3 GEMM sweep.
+# Every sampled shape moves at least 248 MB of operands per call, about twice
+# the 126 MB L2, so repeats start cold without a flush.
+GEMM_SAMPLE = ((16384, 2816, 2816), (16384, 1024, 2816), (16384, 2816, 1024), (65536, 1024, 2816),
+               (65536, 2816, 1024), (65536, 512, 512))
+
+
+def _compact(line, keep=("metric", "value", "unit", "ms_per_step", "steps", "warmup", "config", "e2e", "roofline",
+                         "cpu_baseline", "gpu_launches", "clocks", "loss", "eager_ms_per_step")):
+    return {k: line[k] for k in keep if k in line}
+
+
+def run_other_configs(args, rk):
+    rank = rk.rank
+    out = {}
+    base = dict(vars(args), batch=0, no_e2e=False, no_graph=False, gemm_engine=args.gemm_engine)
+    for wl, steps in (("train_m1", 30), ("train_m8", 20)):
+        line = run_train(argparse.Namespace(**dict(base, workload=wl, steps=steps, warmup=3)), rk)
+        if rank == 0:
+            line = _compact(line)
+            if not args.no_cpu_baseline:
+                line["cpu_baseline"] = cpu_baseline_train(wl)
+            out[TRAIN[wl][5]] = line
+    line = run_adamw(argparse.Namespace(**dict(base, workload="adamw", steps=20, warmup=3)), rk, ADAMW_N)
+    if rank == 0:
+        line = _compact(line)
+        if not args.no_cpu_baseline:
+            steps = cpu_baseline_steps()
+            gbs, sec, threads = reference_adamw(ADAMW_N, steps, 1)
+            line["cpu_baseline"] = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "reference",
+                                    "sample": f"tinylm.c global_gradnorm + adamw at n=2^28, median of {steps} steps "
+                                              "after 1 warm-up"}
+        out["config2_fused_adamw_clip"] = line
+    line = run_gemm(argparse.Namespace(**dict(base, workload="gemm", steps=10, warmup=3, op="all", shape="")), rk,
+                    shapes=GEMM_SAMPLE)
+    if rank == 0:
+        line = _compact(line, keep=("metric", "value", "unit", "config", "roofline", "gpu_launches", "clocks",
+                                    "sweep"))
+        if not args.no_cpu_baseline:
+            tf, threads = reference_gemm(args, shapes=GEMM_SAMPLE)
+            line["cpu_baseline"] = {"value": round(tf, 4), "unit": "TFLOP/s", "cores": threads, "kind": "reference",
+                                    "sample": "tinylm.c mm/mm_bt/mm_atb on the sampled shapes with M cut to 1024 rows"}
+        out["config3_gemm_sample"] = line
+    return out
 
 
 def run_as_script(entry=None):

@@ -252,9 +252,12 @@ def test_gemm_sweep_every_shape_default_engine(cuda, M, K, N):
     """All 32 (M, K, N) shapes of BASELINE config 3 x the three primitives on
     the engine the library picks by itself, at full size, against float64
     products of sampled rows (Y, dX) and columns (dW) computed on the device."""
-    X = torch.randn(M * K, device=cuda, generator=torch.Generator(device=cuda).manual_seed(M + K))
-    W = torch.randn(K * N, device=cuda, generator=torch.Generator(device=cuda).manual_seed(K + N)) * 0.02
-    dY = torch.randn(M * N, device=cuda, generator=torch.Generator(device=cuda).manual_seed(M + N))
+    # Independent draws for X, W and dY (equal seeds would make mm_atb a Gram
+    # matrix whose diagonal dwarfs the mean the metric divides by).
+    base = 3 * M + 5 * K + 7 * N
+    X = torch.randn(M * K, device=cuda, generator=torch.Generator(device=cuda).manual_seed(base))
+    W = torch.randn(K * N, device=cuda, generator=torch.Generator(device=cuda).manual_seed(base + 1)) * 0.02
+    dY = torch.randn(M * N, device=cuda, generator=torch.Generator(device=cuda).manual_seed(base + 2))
     Y = torch.empty(M * N, device=cuda)
     dX = torch.randn(M * K, device=cuda, generator=torch.Generator(device=cuda).manual_seed(7)) * 0.1
     dW = torch.randn(K * N, device=cuda, generator=torch.Generator(device=cuda).manual_seed(8)) * 0.1

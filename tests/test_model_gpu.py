@@ -188,6 +188,41 @@ def test_tensor_core_attention_matches_cuda_cores(cuda, B):
     assert rel < 1e-5, rel
 
 
+@pytest.mark.parametrize("B,pairs", [(4, 3), (5, 7), (12, 0)])
+def test_tensor_core_attention_item_chains(cuda, monkeypatch, B, pairs):
+    """The tensor-core forward's persistent pairs walk chains of (sequence,
+    head) items, reusing K within a kv-head group and overlapping the next
+    item's S with this one's softmax: chains of 10-11 items (3 pairs), chains
+    that start and end inside a group (7 pairs over 40 items), and the default
+    pair count over 96 items -- same loss (1e-6) and gradient (1e-5) as the
+    CUDA-core kernels."""
+    if pairs:
+        monkeypatch.setenv("TL_ATTN_FWD_PAIRS", str(pairs))
+    c = model.cfg8("m16", 0)
+    P = model.init_params(c, 6).to(cuda)
+    n = P.numel()
+    g = torch.Generator(device=cuda).manual_seed(B)
+    tok = torch.randint(0, 2048, (B * 256,), generator=g, device=cuda, dtype=torch.int32)
+    tgt = torch.randint(0, 2048, (B * 256,), generator=g, device=cuda, dtype=torch.int32)
+    m = model.Model(c, B, 0)
+    out = []
+    try:
+        for eng in (1, 2):
+            ops.set_attn_engine(eng)
+            G = torch.zeros(n, device=cuda)
+            loss = torch.zeros(1, device=cuda)
+            m.forward_backward(P, G, tok, tgt, None, B, loss)
+            torch.cuda.synchronize()
+            _lib.check(_lib.lib().tl_device_status())
+            out.append((loss.item(), G.clone()))
+    finally:
+        ops.set_attn_engine(0)
+        m.close()
+    assert out[0][0] == pytest.approx(out[1][0], abs=1e-6)
+    rel = ((out[0][1] - out[1][1]).norm() / out[0][1].norm()).item()
+    assert rel < 1e-5, rel
+
+
 def test_micro_batching_changes_only_rounding(cuda):
     """B=4 as one micro-batch or as four: same loss and gradient up to rounding."""
     c = model.cfg8("nano", 0)

@@ -3,36 +3,48 @@
 // (dK, dV) and query-side (dQ) kernels further down, each with its own
 // description.
 //
-// Forward, the reference's attn_fwd (tinylm.c:699-733): one CTA pair (cluster
-// of 2, tcgen05 cta_group::2) per (sequence, query head).  CTA r holds query
-// rows 128r..128r+127 and key rows 128r..128r+127.
+// Forward, the reference's attn_fwd (tinylm.c:699-733): persistent CTA pairs
+// (clusters of 2, tcgen05 cta_group::2), one per SM pair.  Pair p walks a
+// contiguous range of (sequence, query head) items in (b, h) order, so the
+// query heads of one kv-head group follow each other and share K, loaded and
+// split once per group.  CTA r holds query rows 128r..128r+127 and key rows
+// 128r..128r+127 of the item.
 //
 //   S = Q K^T      M = 256 queries, N = 256 keys, K = 64: 2 k-blocks x 4 x 3
-//                  tf32 MMAs (3xTF32: lo*hi + hi*lo + hi*hi) into TMEM
-//                  columns 0..255; Q and K staged by TMA (K-major, 128-byte
-//                  swizzle), their lo parts written by the split warps.
+//                  tf32 MMAs (3xTF32: lo*hi + hi*lo + hi*hi) into TMEM buffer
+//                  x = item % 2 (columns 256x..256x+255); Q and K staged by
+//                  TMA (K-major, 128-byte swizzle), their lo parts written by
+//                  the softmax warps.
 //   softmax        exact, two passes over S in TMEM: row max over the keys
 //                  <= the query (the two column halves exchange partial maxima
-//                  through shared memory), then p = exp(scale*s - max) and the
-//                  row sum.  P goes to shared memory in 32-key blocks (raw and
-//                  lo, the A operand of the next product).
+//                  through shared memory), then p = 2^(s*scale*log2 e - max*log2 e)
+//                  and the row sum.  P goes to shared memory in 32-key blocks
+//                  (raw and lo, the A operand of the next product).
 //   O = P V        M = 256, N = 64, K = 256 keys in 8 blocks through a 2-slot
 //                  ring (P block + V block, V as the MN-major B operand: each
 //                  CTA holds 32 of the 64 value columns), accumulated in TMEM
-//                  columns 256..319.
+//                  over S's first 64 columns (key blocks 0 and 1, both read
+//                  before the first product).
 //   epilogue       out = O / rowsum, lse = max + log(rowsum) (what the backward
 //                  kernels read).
+// Overlap: Q of the next item is loaded as soon as this item's S products are
+// done, split by the softmax warps after key block SPLIT_KB of this item's
+// second pass, and the next S goes into the other TMEM buffer while this
+// item's P V products and epilogue run; the next item's softmax starts from
+// a finished S.
 //
-// Roles (320 threads): warp 0 TMA producer; warp 1 TMEM owner and, in the
-// leader CTA, MMA issuer; warps 2-9 split Q/K, then run the softmax (warp w:
-// TMEM lanes 32*(w%4).., h = (w-2)/4: row maximum over keys [128h, 128h+128),
-// then P for the key blocks kb with kb % 2 == h and the lo parts of V for the
-// others), then the epilogue for value columns [32h, 32h + 32).  Every wait is bounded; on
-// expiry the pair records an error code (tl_device_status) and winds down.
-// No TMA multicast: the leader's commits use tcgen05.commit multicast, which
-// moves no data.
+// Roles (320 threads): warp 0 lane 0 loads Q (and K), lane 1 the V blocks;
+// warp 1 owns TMEM and, in the leader CTA, issues the MMAs; warps 2-9 split Q/K,
+// run the softmax (warp w: TMEM lanes 32*(w%4).., h = (w-2)/4: row maximum
+// over keys [128h, 128h+128), then P for the key blocks kb with kb % 2 == h
+// and the lo parts of V for the others), then the epilogue for value columns
+// [32h, 32h + 32).  Every wait is bounded; on expiry the pair records an error
+// code (tl_device_status) and winds down.  No TMA multicast: the leader's
+// commits use tcgen05.commit multicast, which moves no data.
 #include <cuda.h>
 #include <cudaTypedefs.h>
+#include <algorithm>
+#include <cstdlib>
 #include "tl_common.cuh"
 #include "tl_tc_ptx.cuh"
 #include "tl_trace.cuh"
@@ -54,8 +66,8 @@ constexpr int NSTAGE = 2;
 constexpr int NBARS = 16;
 constexpr int SMEM_BYTES = STAGE0 + NSTAGE * STAGE_BYTES + 1024 /*align*/ + NBARS * 8 + 64 + 4 * QR * 4;
 constexpr int NUM_THREADS = 320;
-constexpr int TMEM_COLS = 512;                  // S: columns 0..255, O: 256..319
-constexpr int O_COL = 256;
+constexpr int TMEM_COLS = 512;                  // two S buffers of 256 columns (O over the first 64)
+constexpr int SPLIT_KB = 3;                     // key block after which the next item's Q is split
 constexpr int SIGNALLERS = 16;                  // split/softmax warps of the pair
 static_assert(SMEM_BYTES <= 232448, "attention kernel exceeds the opt-in shared memory");
 
@@ -67,6 +79,7 @@ __host__ __device__ constexpr uint32_t idesc_m256(int n, bool a_mn, bool b_mn) {
 struct Args {
   float *out, *lse;
   int H, KV, D;
+  int items;                                    // B * H (sequence, query head) items
   float scale;
   int *err;
 };
@@ -94,27 +107,40 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   float *red = reinterpret_cast<float *>(tmem_slot + 16);   // [2 max/sum][2 halves][128 rows]
   const uint32_t base = smem_u32(smem);
   auto stage = [&](int s) { return base + STAGE0 + s * STAGE_BYTES; };
-  // bars: 0 qk_full, 1 qk_ready, 2 s_full, 3-4 st_full, 5-6 st_ready, 7-8 st_empty, 9 o_full, 10 xch
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
-  constexpr int QK_FULL = 0, QK_READY = 1, S_FULL = 2, ST_FULL = 3, ST_READY = 5, ST_EMPTY = 7, O_FULL = 9,
-                XCH = 10;
+  // QK_FULL: Q (+ K) landed; QK_READY: their lo parts written (pair, leader's
+  // copy); S_FULL[2]: S in TMEM buffer x complete (its Q/K also free again);
+  // ST_FULL / ST_READY / ST_EMPTY [2]: V landed / P and V lo written / PV of
+  // the stage done; O_FULL[2]: O in buffer x complete; O_EMPTY[2]: buffer x
+  // read by the epilogue (pair, leader's copy); XCH: the two column halves'
+  // row maxima and sums; FIN: every MMA done.
+  constexpr int QK_FULL = 0, QK_READY = 1, S_FULL = 2, ST_FULL = 4, ST_READY = 6, ST_EMPTY = 8, O_FULL = 10,
+                O_EMPTY = 12, XCH = 14, FIN = 15;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
-  const int bh = blockIdx.x >> 1, b = bh / a.H, h = bh % a.H, kvh = h / (a.H / a.KV);
+  const int grp = a.H / a.KV;
+  // This pair's items: (sequence, query head) in (b, h) order, so consecutive
+  // items of one kv-head group share K.
+  const int npairs = (int)gridDim.x >> 1, pair = (int)blockIdx.x >> 1;
+  const int it0 = (int)((long long)a.items * pair / npairs);
+  const int n = (int)((long long)a.items * (pair + 1) / npairs) - it0;
+  auto new_k = [&](int jl) { return jl == 0 || (it0 + jl) / grp != (it0 + jl - 1) / grp; };
   const uint32_t peer_flag = cluster_map(smem_u32((const void *)abort_flag), rank ^ 1u);
 
   if (threadIdx.x == 0) {
     mbar_init(bar(QK_FULL), 1);
     mbar_init(bar(QK_READY), SIGNALLERS);
-    mbar_init(bar(S_FULL), 1);
-    for (int s = 0; s < NSTAGE; s++) {
-      mbar_init(bar(ST_FULL + s), 1);
-      mbar_init(bar(ST_READY + s), SIGNALLERS);
-      mbar_init(bar(ST_EMPTY + s), 1);
+    for (int x = 0; x < 2; x++) {
+      mbar_init(bar(S_FULL + x), 1);
+      mbar_init(bar(ST_FULL + x), 1);
+      mbar_init(bar(ST_READY + x), SIGNALLERS);
+      mbar_init(bar(ST_EMPTY + x), 1);
+      mbar_init(bar(O_FULL + x), 1);
+      mbar_init(bar(O_EMPTY + x), SIGNALLERS);
     }
-    mbar_init(bar(O_FULL), 1);
     mbar_init(bar(XCH), 8);
+    mbar_init(bar(FIN), 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -130,30 +156,51 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    // ------------------------------------------------------------ producer
     if (lane == 0) {
-      const int row0 = b * T + QR * (int)rank;
-      mbar_arrive_expect_tx(bar(QK_FULL), 4 * TILE);
-      for (int kb = 0; kb < 2; kb++) {
-        tma_load_2d(base + OFF_QR + kb * TILE, &tmQ, bar(QK_FULL), h * HD + KBLK * kb, row0);
-        tma_load_2d(base + OFF_KR + kb * TILE, &tmK, bar(QK_FULL), kvh * HD + KBLK * kb, row0);
-      }
+      // -------------------------------------------- producer: Q (and K)
       int issued = 0;
-      for (int kb = 0; kb < NKB; kb++) {
-        const int s = kb & 1, u = kb >> 1;
-        if (u > 0 && !mbar_wait_pair(bar(ST_EMPTY + s), (u - 1) & 1, abort_flag, peer_flag, a.err, 31)) break;
-        issued = kb + 1;
-        mbar_arrive_expect_tx(bar(ST_FULL + s), VT);
-        tma_load_2d(stage(s) + OFF_VR, &tmV, bar(ST_FULL + s), kvh * HD + 32 * (int)rank, b * T + KBLK * kb);
+      for (int jl = 0; jl < n; jl++) {
+        const int it = it0 + jl, b = it / a.H, h = it % a.H, kvh = h / grp;
+        // Q / K of the previous item are free once its S products are done.
+        if (jl > 0 && !mbar_wait_pair(bar(S_FULL + ((jl - 1) & 1)), ((jl - 1) >> 1) & 1, abort_flag, peer_flag,
+                                      a.err, 31))
+          break;
+        const bool nk = new_k(jl);
+        const int row0 = b * T + QR * (int)rank;
+        mbar_arrive_expect_tx(bar(QK_FULL), (nk ? 4 : 2) * TILE);
+        for (int kb = 0; kb < 2; kb++) {
+          tma_load_2d(base + OFF_QR + kb * TILE, &tmQ, bar(QK_FULL), h * HD + KBLK * kb, row0);
+          if (nk) tma_load_2d(base + OFF_KR + kb * TILE, &tmK, bar(QK_FULL), kvh * HD + KBLK * kb, row0);
+        }
+        issued = jl + 1;
       }
       // No copy may still be landing when the CTA exits.
-      const long long t0 = clock64();
-      while (!mbar_try_wait(bar(QK_FULL), 0)) {
-        if (clock64() - t0 > WAIT_LIMIT_CYCLES) { atomicExch(a.err, 36); break; }
+      if (issued > 0) {
+        const long long t0 = clock64();
+        while (!mbar_try_wait(bar(QK_FULL), (issued - 1) & 1)) {
+          if (clock64() - t0 > WAIT_LIMIT_CYCLES) { atomicExch(a.err, 36); break; }
+        }
       }
-      for (int kb = issued > NSTAGE ? issued - NSTAGE : 0; kb < issued; kb++) {
+    } else if (lane == 1) {
+      // ------------------------------------------- producer: V blocks
+      int issued = 0;
+      bool ok = true;
+      for (int jl = 0; jl < n && ok; jl++) {
+        const int it = it0 + jl, b = it / a.H, kvh = (it % a.H) / grp;
+        for (int kb = 0; kb < NKB; kb++) {
+          const int g = jl * NKB + kb, s = g & 1, u = g >> 1;
+          if (u > 0 && !mbar_wait_pair(bar(ST_EMPTY + s), (u - 1) & 1, abort_flag, peer_flag, a.err, 31)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(bar(ST_FULL + s), VT);
+          tma_load_2d(stage(s) + OFF_VR, &tmV, bar(ST_FULL + s), kvh * HD + 32 * (int)rank, b * T + KBLK * kb);
+          issued = g + 1;
+        }
+      }
+      for (int g = issued > NSTAGE ? issued - NSTAGE : 0; g < issued; g++) {
         const long long t1 = clock64();
-        while (!mbar_try_wait(bar(ST_FULL + (kb & 1)), (kb >> 1) & 1)) {
+        while (!mbar_try_wait(bar(ST_FULL + (g & 1)), (g >> 1) & 1)) {
           if (clock64() - t1 > WAIT_LIMIT_CYCLES) { atomicExch(a.err, 36); break; }
         }
       }
@@ -161,9 +208,16 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   } else if (warp == 1) {
     // ------------------------------------------- MMA issuer (leader CTA only)
     if (lane == 0 && rank == 0) {
-      if (mbar_wait_pair(bar(QK_READY), 0, abort_flag, peer_flag, a.err, 32)) {
+      constexpr uint32_t idesc_s = idesc_m256(256, false, false);
+      constexpr uint32_t idesc_o = idesc_m256(HD, false, true);
+      // S = Q K^T of item jl into TMEM buffer jl % 2.
+      auto issue_s = [&](int jl) -> bool {
+        const int x = jl & 1;
+        // Buffer x last held item jl - 2, whose O the epilogue must have read.
+        if (jl >= 2 && !mbar_wait_pair(bar(O_EMPTY + x), ((jl - 2) >> 1) & 1, abort_flag, peer_flag, a.err, 30))
+          return false;
+        if (!mbar_wait_pair(bar(QK_READY), jl & 1, abort_flag, peer_flag, a.err, 32)) return false;
         tc_fence_after();
-        constexpr uint32_t idesc_s = idesc_m256(256, false, false);
 #pragma unroll
         for (int kb = 0; kb < 2; kb++) {
 #pragma unroll
@@ -173,16 +227,28 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             const uint64_t q_lo = smem_desc(base + OFF_QL + off, 16, 1024, LAYOUT_SW128);
             const uint64_t k_hi = smem_desc(base + OFF_KR + off, 16, 1024, LAYOUT_SW128);
             const uint64_t k_lo = smem_desc(base + OFF_KL + off, 16, 1024, LAYOUT_SW128);
-            tc_mma_pair(tmem, q_lo, k_hi, idesc_s, (kb > 0 || kk > 0) ? 1u : 0u);
-            tc_mma_pair(tmem, q_hi, k_lo, idesc_s, 1);
-            tc_mma_pair(tmem, q_hi, k_hi, idesc_s, 1);
+            const uint32_t d = tmem + 256 * x;
+            tc_mma_pair(d, q_lo, k_hi, idesc_s, (kb > 0 || kk > 0) ? 1u : 0u);
+            tc_mma_pair(d, q_hi, k_lo, idesc_s, 1);
+            tc_mma_pair(d, q_hi, k_hi, idesc_s, 1);
           }
         }
-        tc_commit_pair(bar(S_FULL));
-        constexpr uint32_t idesc_o = idesc_m256(HD, false, true);
-        for (int kb = 0; kb < NKB; kb++) {
-          const int s = kb & 1;
-          if (!mbar_wait_pair(bar(ST_READY + s), (kb >> 1) & 1, abort_flag, peer_flag, a.err, 33)) break;
+        tc_commit_pair(bar(S_FULL + x));
+        return true;
+      };
+      bool ok = n > 0 && issue_s(0);
+      for (int jl = 0; jl < n && ok; jl++) {
+        const int x = jl & 1;
+        // O overwrites S's first 64 columns (key blocks 0 and 1): both
+        // blocks are read before the first P V product.
+        for (int kb = 0; kb < NKB && ok; kb++) {
+          const int g = jl * NKB + kb, s = g & 1;
+          if (kb == 0)
+            ok = mbar_wait_pair(bar(ST_READY + s), (g >> 1) & 1, abort_flag, peer_flag, a.err, 33) &&
+                 mbar_wait_pair(bar(ST_READY + (s ^ 1)), ((g + 1) >> 1) & 1, abort_flag, peer_flag, a.err, 33);
+          else if (kb != 1)
+            ok = mbar_wait_pair(bar(ST_READY + s), (g >> 1) & 1, abort_flag, peer_flag, a.err, 33);
+          if (!ok) break;
           tc_fence_after();
           const uint32_t st = stage(s);
 #pragma unroll
@@ -191,18 +257,22 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             const uint64_t p_lo = smem_desc(st + OFF_PL + kk * 32, 16, 1024, LAYOUT_SW128);
             const uint64_t v_hi = smem_desc(st + OFF_VR + kk * 1024, 4096, 512, LAYOUT_SW128_BASE32B);
             const uint64_t v_lo = smem_desc(st + OFF_VL + kk * 1024, 4096, 512, LAYOUT_SW128_BASE32B);
-            tc_mma_pair(tmem + O_COL, p_lo, v_hi, idesc_o, (kb > 0 || kk > 0) ? 1u : 0u);
-            tc_mma_pair(tmem + O_COL, p_hi, v_lo, idesc_o, 1);
-            tc_mma_pair(tmem + O_COL, p_hi, v_hi, idesc_o, 1);
+            const uint32_t d = tmem + 256 * x;
+            tc_mma_pair(d, p_lo, v_hi, idesc_o, (kb > 0 || kk > 0) ? 1u : 0u);
+            tc_mma_pair(d, p_hi, v_lo, idesc_o, 1);
+            tc_mma_pair(d, p_hi, v_hi, idesc_o, 1);
           }
           tc_commit_pair(bar(ST_EMPTY + s));
+          // The next item's S, while this item's softmax runs on.
+          if (kb == SPLIT_KB && jl + 1 < n) ok = issue_s(jl + 1);
         }
+        if (ok) tc_commit_pair(bar(O_FULL + x));
       }
-      // O complete (or, on the abort path, every issued MMA finished) before
-      // TMEM can be released.
-      tc_commit_pair(bar(O_FULL));
+      // Every issued MMA finished (also on the abort path) before TMEM is
+      // released.
+      tc_commit_pair(bar(FIN));
       const long long t0 = clock64();
-      while (!mbar_try_wait(bar(O_FULL), 0)) {
+      while (!mbar_try_wait(bar(FIN), 0)) {
         if (clock64() - t0 > WAIT_LIMIT_CYCLES) { pair_abort(abort_flag, peer_flag, a.err, 34); break; }
       }
     }
@@ -214,113 +284,134 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     const int qpos = QR * (int)rank + r;         // its position in the sequence
     const int tl = q4 * 32 + lane;               // 0..127 within the half
     const uint32_t lane_addr = (uint32_t)(q4 * 32) << 16;
-    bool ok = true;
-    // Q, K lo parts
-    {
-      const bool landed = mbar_wait_pair(bar(QK_FULL), 0, abort_flag, peer_flag, a.err, 35);
-      ok = __all_sync(0xffffffffu, landed);
-      if (ok) {
+    const float c2 = a.scale * 1.4426950408889634f;   // scale * log2(e)
+    // This thread's share of the lo parts of the landed Q (and K) tiles.
+    auto split_qk = [&](int jl) -> bool {
+      const bool landed = mbar_wait_pair(bar(QK_FULL), jl & 1, abort_flag, peer_flag, a.err, 35);
+      if (!__all_sync(0xffffffffu, landed)) return false;
+      const int nq = new_k(jl) ? 16 : 8;
 #pragma unroll 4
-        for (int e = 0; e < 16; e++) {
-          const int idx = e * 256 + t;          // 0..4095: Q then K, 2048 float4 each
-          const int src = (idx < 2048 ? OFF_QR : OFF_KR) + (idx & 2047) * 16;
-          const int dst = (idx < 2048 ? OFF_QL : OFF_KL) + (idx & 2047) * 16;
-          const float4 x = *reinterpret_cast<const float4 *>(smem + src);
-          float4 lo;
-          lo.x = x.x - tf32_trunc(x.x); lo.y = x.y - tf32_trunc(x.y);
-          lo.z = x.z - tf32_trunc(x.z); lo.w = x.w - tf32_trunc(x.w);
-          *reinterpret_cast<float4 *>(smem + dst) = lo;
-        }
-        fence_proxy_async();
-        __syncwarp();
-        if (lane == 0) mbar_arrive_remote(cluster_map(bar(QK_READY), 0));
+      for (int e = 0; e < nq; e++) {
+        const int idx = e * 256 + t;          // 0..4095: Q then K, 2048 float4 each
+        const int src = (idx < 2048 ? OFF_QR : OFF_KR) + (idx & 2047) * 16;
+        const int dst = (idx < 2048 ? OFF_QL : OFF_KL) + (idx & 2047) * 16;
+        const float4 x = *reinterpret_cast<const float4 *>(smem + src);
+        float4 lo;
+        lo.x = x.x - tf32_trunc(x.x); lo.y = x.y - tf32_trunc(x.y);
+        lo.z = x.z - tf32_trunc(x.z); lo.w = x.w - tf32_trunc(x.w);
+        *reinterpret_cast<float4 *>(smem + dst) = lo;
       }
-    }
-    float m = -1e30f, lsum = 0.0f;
-    if (ok) ok = __all_sync(0xffffffffu, mbar_wait_pair(bar(S_FULL), 0, abort_flag, peer_flag, a.err, 37));
-    if (ok) {
-      // pass 1: partial row max over this half's keys <= qpos
-      tc_fence_after();
-      float mx = -1e30f;
-#pragma unroll 1
-      for (int c = 0; c < 4; c++) {
-        uint32_t v[32];
-        const int j0 = hh * 128 + c * 32;
-        tmem_ld32(tmem + lane_addr + j0, v);
-#pragma unroll
-        for (int e = 0; e < 32; e++)
-          if (j0 + e <= qpos) mx = fmaxf(mx, __uint_as_float(v[e]) * a.scale);
-      }
-      red[hh * QR + r] = mx;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(XCH));
-      ok = __all_sync(0xffffffffu, mbar_wait_pair(bar(XCH), 0, abort_flag, peer_flag, a.err, 38));
-      if (ok) m = fmaxf(red[r], red[QR + r]);
-    }
-    // pass 2: key blocks in order; half h writes P for the blocks kb with
-    // kb % 2 == h and the lo parts of V for the others, so both halves
-    // produce P blocks at the same time.
-#pragma unroll 1
-    for (int kb = 0; kb < NKB && ok; kb++) {
-      const int s = kb & 1;
-      const uint32_t st = stage(s);
-      if ((kb & 1) == hh) {
-        bool w = true;
-        if (kb >= 2) w = mbar_wait_pair(bar(ST_EMPTY + s), ((kb >> 1) - 1) & 1, abort_flag, peer_flag, a.err, 39);
-        if (!(ok = __all_sync(0xffffffffu, w))) break;
-        tc_fence_after();
-        uint32_t v[32];
-        tmem_ld32(tmem + lane_addr + kb * 32, v);
-        float pr[32];
-#pragma unroll
-        for (int e = 0; e < 32; e++) {
-          const int key = kb * 32 + e;
-          pr[e] = key <= qpos ? expf(__uint_as_float(v[e]) * a.scale - m) : 0.0f;
-          lsum += pr[e];
-        }
-        // row r of the 128 x 32 K-major tile: logical chunk c at c ^ (r % 8)
-#pragma unroll
-        for (int c = 0; c < 8; c++) {
-          const uint32_t off = (uint32_t)r * 128 + (uint32_t)((c ^ (r & 7)) * 16);
-          const float4 x = make_float4(pr[4 * c], pr[4 * c + 1], pr[4 * c + 2], pr[4 * c + 3]);
-          float4 lo;
-          lo.x = x.x - tf32_trunc(x.x); lo.y = x.y - tf32_trunc(x.y);
-          lo.z = x.z - tf32_trunc(x.z); lo.w = x.w - tf32_trunc(x.w);
-          *reinterpret_cast<float4 *>(smem + (st - base) + OFF_PR + off) = x;
-          *reinterpret_cast<float4 *>(smem + (st - base) + OFF_PL + off) = lo;
-        }
-      } else {
-        const bool w = mbar_wait_pair(bar(ST_FULL + s), (kb >> 1) & 1, abort_flag, peer_flag, a.err, 40);
-        if (!(ok = __all_sync(0xffffffffu, w))) break;
-#pragma unroll
-        for (int e = 0; e < 2; e++) {
-          const int off = (e * 128 + tl) * 16;
-          const float4 x = *reinterpret_cast<const float4 *>(smem + (st - base) + OFF_VR + off);
-          float4 lo;
-          lo.x = x.x - tf32_trunc(x.x); lo.y = x.y - tf32_trunc(x.y);
-          lo.z = x.z - tf32_trunc(x.z); lo.w = x.w - tf32_trunc(x.w);
-          *reinterpret_cast<float4 *>(smem + (st - base) + OFF_VL + off) = lo;
-        }
-      }
-      tc_fence_before();
       fence_proxy_async();
       __syncwarp();
-      if (lane == 0) mbar_arrive_remote(cluster_map(bar(ST_READY + s), 0));
-    }
-    if (ok) {
+      if (lane == 0) mbar_arrive_remote(cluster_map(bar(QK_READY), 0));
+      return true;
+    };
+    bool ok = n > 0 && split_qk(0);
+    for (int jl = 0; jl < n && ok; jl++) {
+      const int it = it0 + jl, b = it / a.H, h = it % a.H, x = jl & 1;
+      const uint32_t sbase = tmem + lane_addr + 256 * x;
+      float m = -1e30f, lsum = 0.0f;
+      ok = __all_sync(0xffffffffu, mbar_wait_pair(bar(S_FULL + x), (jl >> 1) & 1, abort_flag, peer_flag, a.err, 37));
+      if (!ok) break;
+      {
+        // pass 1: partial row max over this half's keys <= qpos (keys of
+        // the upper half are all masked for the first 128 queries)
+        tc_fence_after();
+        float mx = -1e30f;
+        if (!(rank == 0 && hh == 1)) {
+#pragma unroll 1
+          for (int c = 0; c < 4; c++) {
+            uint32_t v[32];
+            const int j0 = hh * 128 + c * 32;
+            tmem_ld32(sbase + j0, v);
+#pragma unroll
+            for (int e = 0; e < 32; e++)
+              if (j0 + e <= qpos) mx = fmaxf(mx, __uint_as_float(v[e]));
+          }
+        }
+        red[hh * QR + r] = mx;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(XCH));
+        ok = __all_sync(0xffffffffu, mbar_wait_pair(bar(XCH), 0, abort_flag, peer_flag, a.err, 38));
+        if (!ok) break;
+        m = fmaxf(red[r], red[QR + r]) * a.scale;
+      }
+      const float mc = m * 1.4426950408889634f;
+      // pass 2: key blocks in order; half h writes P for the blocks kb with
+      // kb % 2 == h and the lo parts of V for the others, so both halves
+      // produce P blocks at the same time.  After block SPLIT_KB every warp
+      // also splits its share of the next item's Q (and K).
+#pragma unroll 1
+      for (int kb = 0; kb < NKB && ok; kb++) {
+        const int g = jl * NKB + kb, s = g & 1;
+        const uint32_t st = stage(s);
+        if ((kb & 1) == hh) {
+          bool w = true;
+          if (g >= 2) w = mbar_wait_pair(bar(ST_EMPTY + s), ((g >> 1) - 1) & 1, abort_flag, peer_flag, a.err, 39);
+          if (!(ok = __all_sync(0xffffffffu, w))) break;
+          tc_fence_after();
+          float pr[32];
+          if (kb * 32 > QR * (int)rank + QR - 1) {
+            // every key of the block is after every query of this CTA
+#pragma unroll
+            for (int e = 0; e < 32; e++) pr[e] = 0.0f;
+          } else {
+            uint32_t v[32];
+            tmem_ld32(sbase + kb * 32, v);
+#pragma unroll
+            for (int e = 0; e < 32; e++) {
+              const int key = kb * 32 + e;
+              pr[e] = key <= qpos ? exp2f(fmaf(__uint_as_float(v[e]), c2, -mc)) : 0.0f;
+              lsum += pr[e];
+            }
+          }
+          // row r of the 128 x 32 K-major tile: logical chunk c at c ^ (r % 8)
+#pragma unroll
+          for (int c = 0; c < 8; c++) {
+            const uint32_t off = (uint32_t)r * 128 + (uint32_t)((c ^ (r & 7)) * 16);
+            const float4 xv = make_float4(pr[4 * c], pr[4 * c + 1], pr[4 * c + 2], pr[4 * c + 3]);
+            float4 lo;
+            lo.x = xv.x - tf32_trunc(xv.x); lo.y = xv.y - tf32_trunc(xv.y);
+            lo.z = xv.z - tf32_trunc(xv.z); lo.w = xv.w - tf32_trunc(xv.w);
+            *reinterpret_cast<float4 *>(smem + (st - base) + OFF_PR + off) = xv;
+            *reinterpret_cast<float4 *>(smem + (st - base) + OFF_PL + off) = lo;
+          }
+        } else {
+          const bool w = mbar_wait_pair(bar(ST_FULL + s), (g >> 1) & 1, abort_flag, peer_flag, a.err, 40);
+          if (!(ok = __all_sync(0xffffffffu, w))) break;
+#pragma unroll
+          for (int e = 0; e < 2; e++) {
+            const int off = (e * 128 + tl) * 16;
+            const float4 xv = *reinterpret_cast<const float4 *>(smem + (st - base) + OFF_VR + off);
+            float4 lo;
+            lo.x = xv.x - tf32_trunc(xv.x); lo.y = xv.y - tf32_trunc(xv.y);
+            lo.z = xv.z - tf32_trunc(xv.z); lo.w = xv.w - tf32_trunc(xv.w);
+            *reinterpret_cast<float4 *>(smem + (st - base) + OFF_VL + off) = lo;
+          }
+        }
+        tc_fence_before();
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote(cluster_map(bar(ST_READY + s), 0));
+        if (kb == SPLIT_KB && jl + 1 < n) ok = split_qk(jl + 1);
+      }
+      if (!ok) break;
       // row sum: both halves, added in half order
       red[2 * QR + hh * QR + r] = lsum;
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(XCH));
       ok = __all_sync(0xffffffffu, mbar_wait_pair(bar(XCH), 1, abort_flag, peer_flag, a.err, 41));
-    }
-    if (ok) ok = __all_sync(0xffffffffu, mbar_wait_pair(bar(O_FULL), 0, abort_flag, peer_flag, a.err, 42));
-    if (ok && !*abort_flag) {
+      if (ok) ok = __all_sync(0xffffffffu, mbar_wait_pair(bar(O_FULL + x), (jl >> 1) & 1, abort_flag, peer_flag,
+                                                          a.err, 42));
+      if (!ok || *abort_flag) break;
       const float l = red[2 * QR + r] + red[3 * QR + r];
       const float inv = 1.0f / l;
       tc_fence_after();
       uint32_t v[32];
-      tmem_ld32(tmem + lane_addr + O_COL + hh * 32, v);
+      tmem_ld32(sbase + hh * 32, v);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(cluster_map(bar(O_EMPTY + x), 0));
       const int b_row = b * T + qpos;
       float *dst = a.out + (size_t)b_row * a.D + h * HD + hh * 32;
 #pragma unroll
@@ -328,7 +419,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         *reinterpret_cast<float4 *>(dst + e) =
             make_float4(__uint_as_float(v[e]) * inv, __uint_as_float(v[e + 1]) * inv,
                         __uint_as_float(v[e + 2]) * inv, __uint_as_float(v[e + 3]) * inv);
-      if (hh == 0) a.lse[(size_t)bh * T + qpos] = m + logf(l);
+      if (hh == 0) a.lse[(size_t)it * T + qpos] = m + logf(l);
     }
   }
   tc_fence_before();
@@ -1018,10 +1109,19 @@ int attn_fwd_tc(DeviceCtx *c, const float *q, const float *k, const float *v, fl
   if ((rc = atc::map2d(&mv, v, KD, rows, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))) return rc;
   atc::Args a;
   a.out = out; a.lse = lse; a.H = H; a.KV = KV; a.D = D;
+  a.items = B * H;
   a.scale = 1.0f / sqrtf((float)atc::HD);
   a.err = c->err_flag;
+  // One pair per SM pair, each walking its share of the items.  Tests cap the
+  // pair count (TL_ATTN_FWD_PAIRS) to give each pair long item chains at small
+  // batch sizes.
+  int npairs = std::min(a.items, std::max(1, c->num_sms / 2));
+  if (const char *e = getenv("TL_ATTN_FWD_PAIRS")) {
+    const int cap = atoi(e);
+    if (cap > 0 && cap < npairs) npairs = cap;
+  }
   TraceScope ts(c, "k_attn_fwd_tc");
-  atc::attn_fwd_tc_kernel<<<2 * B * H, atc::NUM_THREADS, atc::SMEM_BYTES, c->stream>>>(mq, mk, mv, a);
+  atc::attn_fwd_tc_kernel<<<2 * npairs, atc::NUM_THREADS, atc::SMEM_BYTES, c->stream>>>(mq, mk, mv, a);
   TL_TRY_CUDA(cudaGetLastError());
   return TL_OK;
 }
