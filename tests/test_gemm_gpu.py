@@ -212,6 +212,44 @@ def test_f16_split_operand_scales(cuda, sa, sb):
             assert gemm_rel(g, want) <= GEMM_REL_TOL
 
 
+@pytest.mark.parametrize("eng", [0, 4])
+@pytest.mark.parametrize("M,K,Ns,accumulate", [(16384, 1024, (1024, 256, 256), False), (16384, 1024, (2816, 2816), False),
+                                               (16384, 1024, (1024,), True), (65536, 256, (256,), True),
+                                               (16128, 1000, (512,), False)])
+def test_tail_split_tiles(cuda, eng, M, K, Ns, accumulate):
+    """Outputs of 256 (or 252) pair tiles fill three waves of resident CTA
+    pairs and leave a partial one: the last tiles run as two pairs over half
+    the reduction each, summed by the tail pass.  The config-5 attention and
+    FFN input-norm gradients (summed products), an accumulating mm_bt, and
+    ragged edges (16128 x 1000), against float64 on sampled rows."""
+    g = torch.Generator(device=cuda).manual_seed(M + K + sum(Ns))
+    dYs = [torch.randn(M * n, device=cuda, generator=g) for n in Ns]
+    Ws = [torch.randn(K * n, device=cuda, generator=g) * 0.02 for n in Ns]
+    dX0 = torch.randn(M * K, device=cuda, generator=g) * 0.1
+    dX = dX0.clone()
+    ops.set_gemm_engine(eng)
+    try:
+        if accumulate:
+            ops.mm_bt(dX, dYs[0], Ws[0], M, K, Ns[0])
+        else:
+            ops.mm_bt_sum(dX, dYs, Ws, list(Ns), M, K)
+        torch.cuda.synchronize()
+        device_ok()
+    finally:
+        ops.set_gemm_engine(0)
+    rows = torch.randperm(M, generator=torch.Generator().manual_seed(K))[:256].sort().values.to(cuda)
+    want = dX0.view(M, K)[rows].double() if accumulate else torch.zeros(256, K, device=cuda, dtype=torch.float64)
+    for a, w, n in zip(dYs, Ws, Ns):
+        want += a.view(M, n)[rows].double() @ w.view(K, n).double().T
+    assert gemm_rel(dX.view(M, K)[rows].cpu().numpy(), want.cpu().numpy()) <= GEMM_REL_TOL
+    # rows of the last tiles (the tail) too
+    tail = dX.view(M, K)[-256:].double()
+    want_t = dX0.view(M, K)[-256:].double() if accumulate else torch.zeros(256, K, device=cuda, dtype=torch.float64)
+    for a, w, n in zip(dYs, Ws, Ns):
+        want_t += a.view(M, n)[-256:].double() @ w.view(K, n).double().T
+    assert gemm_rel(tail.cpu().numpy(), want_t.cpu().numpy()) <= GEMM_REL_TOL
+
+
 def test_mm_bt_sum_rejects_bad_args(cuda):
     z = torch.zeros(64, device=cuda)
     with pytest.raises(TLError):

@@ -77,6 +77,12 @@ struct Params {
   // products summed into one output; INT_MAX when there is one).
   int seg_end0, seg_end1;
   size_t split_stride;   // floats between the partial outputs of consecutive splits
+  // Pair kernel, tail split: pair-tiles [0, full_tiles) in grouped order run
+  // whole; each later tile runs as tail_splits CTA pairs of tail_kb k-blocks,
+  // pair u after the full tiles writing its part of the tile into the 256 x 256
+  // slot u of tail_ws (tail_splits <= 1: no tail split).
+  int full_tiles, tail_splits, tail_kb;
+  float *tail_ws;
   // Pair kernel, fp16 split: max |x| (float bits) of A and B of each product,
   // [A0, B0, A1, B1, A2, B2].
   const unsigned *amax;
@@ -381,6 +387,19 @@ constexpr int PAIR_DRAIN_LAG = 2;                       // k-blocks split ahead 
 constexpr int PAIR_GROUP_M = TL_PAIR_GROUP_M;           // pair-rows per tile group
 static_assert(PAIR_SMEM_BYTES <= 232448, "pair kernel exceeds the opt-in shared memory per block");
 
+// Grouped order of the pair kernel's output tiles: pair-tile L (launch order)
+// -> tile row pm (256 rows) and tile column tn (256 columns), PAIR_GROUP_M
+// tile rows at a time, so pairs resident together share rows of A and
+// columns of B in L2.
+__host__ __device__ inline void pair_tile(int L, int I, int J, int *pm, int *tn) {
+  const int npm = (I + PM - 1) / PM, ntn = (J + PN - 1) / PN;
+  const int group = L / (PAIR_GROUP_M * ntn), first_pm = group * PAIR_GROUP_M;
+  const int gsz = min(npm - first_pm, PAIR_GROUP_M);
+  const int in_group = L - group * PAIR_GROUP_M * ntn;
+  *pm = first_pm + in_group % gsz;
+  *tn = in_group / gsz;
+}
+
 __host__ __device__ constexpr uint32_t make_idesc_pair(bool a_mn, bool b_mn) {
   return (1u << 4) | (2u << 7) | (2u << 10) | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) |
          ((uint32_t)(PN >> 3) << 17) | ((uint32_t)(PM >> 4) << 24);
@@ -431,19 +450,26 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
-  // Grouped tile order over the pairs: pair L (launch order) -> (pm, tn).
-  const int npm = (p.I + PM - 1) / PM, ntn = (p.J + PN - 1) / PN;
-  const int L = blockIdx.x >> 1;
-  const int group = L / (PAIR_GROUP_M * ntn), first_pm = group * PAIR_GROUP_M;
-  const int gsz = min(npm - first_pm, PAIR_GROUP_M);
-  const int in_group = L - group * PAIR_GROUP_M * ntn;
-  const int pm = first_pm + in_group % gsz, tn = in_group / gsz;
+  // The pair's tile and k-block range: grid z splits every tile's reduction
+  // (split-K), or the pairs after the full tiles each take a part of a tail
+  // tile.
+  int L = blockIdx.x >> 1;
+  int kb0 = blockIdx.z * p.kb_per_split, kb_len = p.kb_per_split;
+  int tail_slot = -1;
+  if (p.tail_splits > 1 && L >= p.full_tiles) {
+    const int u = L - p.full_tiles;
+    L = p.full_tiles + u / p.tail_splits;
+    kb0 = (u % p.tail_splits) * p.tail_kb;
+    kb_len = p.tail_kb;
+    tail_slot = u;
+  }
+  int pm, tn;
+  pair_tile(L, p.I, p.J, &pm, &tn);
   const int i0 = (2 * pm + (int)rank) * BM;    // this CTA's 128 output rows
   const int j0 = tn * PN;                      // the pair's 256 output columns
   const int jb = j0 + (int)rank * BN;          // this CTA's 128 columns of B
   const int nk_all = (p.R + BK - 1) / BK;
-  const int kb0 = blockIdx.z * p.kb_per_split;
-  const int nk = max(0, min(nk_all - kb0, p.kb_per_split));
+  const int nk = max(0, min(nk_all - kb0, kb_len));
   const int nchunks = (nk + PAIR_CHUNK_KB - 1) / PAIR_CHUNK_KB;
   float *const Cout = p.C + (size_t)blockIdx.z * p.split_stride;
   const uint32_t raw_base = smem_u32(raw_ring), lo_base = smem_u32(lo_ring);
@@ -770,7 +796,11 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         }
       }
       const int jc = j0 + h * BN;
-      if (row < p.I) {
+      if (row < p.I && tail_slot >= 0) {
+        // a part of a tail tile: this row of the tile's slot, no addend
+        float *dst = p.tail_ws + (size_t)tail_slot * (PM * PN) + (size_t)(row - pm * PM) * PN + h * BN;
+        store_row(dst, nullptr, acc, p.J - jc);
+      } else if (row < p.I) {
         float *dst = Cout + (size_t)row * p.ldc + jc;
         const float *addp = p.add ? p.add + (size_t)row * p.ldc + jc : nullptr;
         store_row(dst, addp, acc, p.J - jc);
@@ -779,6 +809,355 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
   }
   // Neither CTA releases TMEM or exits while the pair's MMAs, TMEM reads or
   // cross-CTA signals may still be in flight.
+  tc_fence_before();
+  cluster_sync_all();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(PAIR_TMEM_COLS) : "memory");
+  }
+}
+
+// ------------------------------- CTA pair, fp16 split, specialised warps
+// The fp16-split engine (kind::f16, twice the tf32 MMA rate) with its work
+// spread over dedicated warps.  In the pair kernel above the same eight warps
+// convert every landed tile and drain the TMEM accumulator, and at the f16
+// MMA rate they become the bottleneck.  Here (512 threads, 4 warpgroups):
+//   warp 0          TMA producer (raw fp32 tiles, as in the pair kernel)
+//   warp 1          TMEM owner and, in the leader CTA, MMA issuer
+//   warps 2-3, 12-15  six converter warps: scale, split and pack each landed
+//                   raw tile into the fp16 hi/lo operand tile (the layouts of
+//                   the pair kernel's fp16 path), in 16-byte tasks
+//   warps 4-11      eight accumulator warps: drain every TMEM chunk into fp32
+//                   registers (128 columns per thread) and store the tile
+// Registers follow the roles (setmaxnreg): warpgroups 0 and 3 run with 56 per
+// thread, warpgroups 1 and 2 (the accumulators) with 200; 128 x 56 x 2 +
+// 256 x 200 = 512 x 128, the launch's own total.
+constexpr int WS_THREADS = 512;
+constexpr int WS_CONV_WARPS = 6;
+constexpr int WS_CONV_THREADS = 32 * WS_CONV_WARPS;
+constexpr int WS_DRAIN_WARPS = 8;
+constexpr int WS_REG_SMALL = 56, WS_REG_ACC = 200;
+static_assert(128 * WS_REG_SMALL * 2 + 256 * WS_REG_ACC == WS_THREADS * 128, "register split must match the launch");
+
+// Accumulator warps (4..11) of the specialised fp16-split kernel: drain every
+// TMEM chunk into fp32 registers, then scale, rotate (RoPE) and store the
+// tile rows.
+template <bool A_MN, bool B_MN>
+__device__ __forceinline__ void ws_accumulate(const Params &p, uint32_t tmem, int warp, int lane, int i0, int j0,
+                                              int pm, int nchunks, int tail_slot, float *Cout, uint64_t *bars,
+                                              volatile int *abort_flag, uint32_t peer_flag, const float *scl) {
+  auto bar_accf = [&](int b) { return smem_u32(&bars[2 * RAW_STAGES + 2 * LO_STAGES + b]); };
+  auto bar_acce = [&](int b) { return smem_u32(&bars[2 * RAW_STAGES + 2 * LO_STAGES + 2 + b]); };
+  const int q = warp & 3, h = (warp - 4) >> 2;
+  float acc[BN];
+#pragma unroll
+  for (int e = 0; e < BN; e++) acc[e] = 0.0f;
+  bool ok = true;
+  for (int c = 0; c < nchunks; c++) {
+    const int b = c & 1;
+    const bool landed = mbar_wait_pair(bar_accf(b), (c >> 1) & 1, abort_flag, peer_flag, p.err, 5);
+    if (!__all_sync(0xffffffffu, landed)) { ok = false; break; }
+    tc_fence_after();
+#pragma unroll
+    for (int cc = 0; cc < BN / 32; cc++) {
+      uint32_t v[32];
+      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + b * PN + h * BN + cc * 32;
+      asm volatile(
+          "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+          "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+          : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+            "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]),
+            "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]),
+            "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]),
+            "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+          : "r"(taddr));
+      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+      for (int e = 0; e < 32; e++) acc[cc * 32 + e] += __uint_as_float(v[e]);
+    }
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive_remote(cluster_map(bar_acce(b), 0));
+  }
+  if (ok && !*abort_flag) {
+    const float inv = scl[6];
+#pragma unroll
+    for (int e = 0; e < BN; e++) acc[e] *= inv;
+    const int row = i0 + q * 32 + lane;
+    if (p.rope_cos && row < p.I) {
+      // RoPE (tinylm.c:626-640): this thread's 128 columns are two heads;
+      // pairs (i, i + 32) rotate by the angle of the row's position.
+      const size_t tb = (size_t)(row % p.rope_T) * 32;
+#pragma unroll
+      for (int i4 = 0; i4 < 32; i4 += 4) {
+        const float4 c4 = __ldg(reinterpret_cast<const float4 *>(p.rope_cos + tb + i4));
+        const float4 s4 = __ldg(reinterpret_cast<const float4 *>(p.rope_sin + tb + i4));
+        const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, ss[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+#pragma unroll
+          for (int hh = 0; hh < 2; hh++) {
+            const float a = acc[64 * hh + i4 + u], bb = acc[64 * hh + i4 + u + 32];
+            acc[64 * hh + i4 + u] = a * cc[u] - bb * ss[u];
+            acc[64 * hh + i4 + u + 32] = bb * cc[u] + a * ss[u];
+          }
+        }
+      }
+    }
+    const int jc = j0 + h * BN;
+    if (row < p.I && tail_slot >= 0) {
+      float *dst = p.tail_ws + (size_t)tail_slot * (PM * PN) + (size_t)(row - pm * PM) * PN + h * BN;
+      store_row(dst, nullptr, acc, p.J - jc);
+    } else if (row < p.I) {
+      float *dst = Cout + (size_t)row * p.ldc + jc;
+      const float *addp = p.add ? p.add + (size_t)row * p.ldc + jc : nullptr;
+      store_row(dst, addp, acc, p.J - jc);
+    }
+  }
+}
+
+template <bool A_MN, bool B_MN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WS_THREADS, 1)
+gemm_tc_pair_f16ws_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                          const __grid_constant__ CUtensorMap tmA1, const __grid_constant__ CUtensorMap tmB1,
+                          const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
+                          Params p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *raw_ring = smem, *lo_ring = smem + RAW_STAGES * RAW_BYTES;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(lo_ring + LO_STAGES * RAW_BYTES);
+  // bars: full[R], rempty[R] (this CTA's converters done with the raw slot),
+  // ready[L] (both CTAs' operand slot written; leader's copy used), lempty[L]
+  // (pair MMAs done with the operand slot), accf[2], acce[2] (leader's copy)
+  constexpr int NBARS = 2 * RAW_STAGES + 2 * LO_STAGES + 4;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + NBARS);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+  float *scl = reinterpret_cast<float *>(tmem_slot + 4);   // [A0, B0, A1, B1, A2, B2], inverse product scale
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  int L = blockIdx.x >> 1;
+  int kb0 = blockIdx.z * p.kb_per_split, kb_len = p.kb_per_split;
+  int tail_slot = -1;
+  if (p.tail_splits > 1 && L >= p.full_tiles) {
+    const int u = L - p.full_tiles;
+    L = p.full_tiles + u / p.tail_splits;
+    kb0 = (u % p.tail_splits) * p.tail_kb;
+    kb_len = p.tail_kb;
+    tail_slot = u;
+  }
+  int pm, tn;
+  pair_tile(L, p.I, p.J, &pm, &tn);
+  const int i0 = (2 * pm + (int)rank) * BM;
+  const int j0 = tn * PN;
+  const int jb = j0 + (int)rank * BN;
+  const int nk_all = (p.R + BK - 1) / BK;
+  const int nk = max(0, min(nk_all - kb0, kb_len));
+  const int nchunks = (nk + PAIR_CHUNK_KB - 1) / PAIR_CHUNK_KB;
+  float *const Cout = p.C + (size_t)blockIdx.z * p.split_stride;
+  const uint32_t raw_base = smem_u32(raw_ring), lo_base = smem_u32(lo_ring);
+  auto bar_full = [&](int s) { return smem_u32(&bars[s]); };
+  auto bar_rempty = [&](int s) { return smem_u32(&bars[RAW_STAGES + s]); };
+  auto bar_ready = [&](int s) { return smem_u32(&bars[2 * RAW_STAGES + s]); };
+  auto bar_lempty = [&](int s) { return smem_u32(&bars[2 * RAW_STAGES + LO_STAGES + s]); };
+  auto bar_accf = [&](int b) { return smem_u32(&bars[2 * RAW_STAGES + 2 * LO_STAGES + b]); };
+  auto bar_acce = [&](int b) { return smem_u32(&bars[2 * RAW_STAGES + 2 * LO_STAGES + 2 + b]); };
+  const uint32_t peer_flag = cluster_map(smem_u32((const void *)abort_flag), rank ^ 1u);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < RAW_STAGES; s++) {
+      mbar_init(bar_full(s), 1);
+      mbar_init(bar_rempty(s), WS_CONV_WARPS);
+    }
+    for (int s = 0; s < LO_STAGES; s++) {
+      mbar_init(bar_ready(s), 2 * WS_CONV_WARPS);
+      mbar_init(bar_lempty(s), 1);
+    }
+    for (int b = 0; b < 2; b++) {
+      mbar_init(bar_accf(b), 1);
+      mbar_init(bar_acce(b), 2 * WS_DRAIN_WARPS);
+    }
+    *abort_flag = 0;
+    // Operand scales as in the pair kernel's fp16 path.
+    const int nprod = p.seg_end1 != 0x7fffffff ? 3 : (p.seg_end0 != 0x7fffffff ? 2 : 1);
+    int P = 1 << 20;
+#pragma unroll
+    for (int t = 0; t < 3; t++)
+      if (t < nprod) P = min(P, 28 - amax_exp(p.amax[2 * t]) - amax_exp(p.amax[2 * t + 1]));
+    P = max(-126, min(126, P));
+#pragma unroll
+    for (int t = 0; t < 3; t++) {
+      const int sb = t < nprod ? 14 - amax_exp(p.amax[2 * t + 1]) : 0;
+      const int ea = t < nprod ? max(P - sb, -126) : 0;
+      scl[2 * t] = exp2i(ea);
+      scl[2 * t + 1] = t < nprod ? exp2i(P - ea) : 1.0f;
+    }
+    scl[6] = exp2i(-P);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(PAIR_TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int wg = warp >> 2;
+  // Each role's register budget is set at the top of its branch (the register
+  // allocator sees the new limit for everything the branch dominates).
+  if (wg == 1 || wg == 2) {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(WS_REG_ACC));
+    ws_accumulate<A_MN, B_MN>(p, tmem, warp, lane, i0, j0, pm, nchunks, tail_slot, Cout, bars, abort_flag,
+                              peer_flag, scl);
+  } else {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(WS_REG_SMALL));
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int issued = 0;
+      for (int kb = 0; kb < nk; kb++) {
+        const int s = kb % RAW_STAGES, u = kb / RAW_STAGES;
+        if (u > 0 && !mbar_wait_pair(bar_rempty(s), (u - 1) & 1, abort_flag, peer_flag, p.err, 1)) break;
+        issued = kb + 1;
+        const uint32_t st = raw_base + s * RAW_BYTES;
+        mbar_arrive_expect_tx(bar_full(s), TX_BYTES);
+        int kg = kb0 + kb;
+        const CUtensorMap *ta = &tmA, *tb = &tmB;
+        if (kg >= p.seg_end1) { ta = &tmA2; tb = &tmB2; kg -= p.seg_end1; }
+        else if (kg >= p.seg_end0) { ta = &tmA1; tb = &tmB1; kg -= p.seg_end0; }
+        const int k0 = kg * BK;
+        if (A_MN) {
+#pragma unroll
+          for (int b = 0; b < BM / 32; b++) tma_load_2d(st + b * 4096, ta, bar_full(s), i0 + 32 * b, k0);
+        } else {
+          tma_load_2d(st, ta, bar_full(s), k0, i0);
+        }
+        if (B_MN) {
+#pragma unroll
+          for (int b = 0; b < BN / 32; b++) tma_load_2d(st + TILE_A + b * 4096, tb, bar_full(s), jb + 32 * b, k0);
+        } else {
+          tma_load_2d(st + TILE_A, tb, bar_full(s), k0, jb);
+        }
+      }
+      for (int kb = issued > RAW_STAGES ? issued - RAW_STAGES : 0; kb < issued; kb++) {
+        const long long t0 = clock64();
+        while (!mbar_try_wait(bar_full(kb % RAW_STAGES), (kb / RAW_STAGES) & 1)) {
+          if (clock64() - t0 > WAIT_LIMIT_CYCLES) { atomicExch(p.err, 6); break; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------- MMA issuer (leader CTA only)
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc16 = make_idesc_pair_f16(A_MN, B_MN);
+      int chunk = 0, kin = 0, last_committed = -1;
+      for (int kb = 0; kb < nk; kb++) {
+        const int ls = kb % LO_STAGES;
+        const int b = chunk & 1;
+        if (kin == 0 && chunk >= 2 &&
+            !mbar_wait_pair(bar_acce(b), ((chunk >> 1) - 1) & 1, abort_flag, peer_flag, p.err, 7))
+          break;
+        if (!mbar_wait_pair(bar_ready(ls), (kb / LO_STAGES) & 1, abort_flag, peer_flag, p.err, 2)) break;
+        tc_fence_after();
+        const uint32_t lo = lo_base + ls * RAW_BYTES;
+        const uint32_t d = tmem + b * PN;
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; kk++) {
+          uint64_t op[2][2];   // [A, B][hi, lo]
+#pragma unroll
+          for (int w = 0; w < 2; w++) {
+            const bool mn = w ? B_MN : A_MN;
+            const uint32_t t0 = lo + (w ? TILE_A : 0);
+            op[w][0] = mn ? smem_desc(t0 + kk * 2048, 4096, 1024, LAYOUT_SW128)
+                          : smem_desc(t0 + kk * 32, 16, 1024, LAYOUT_SW128);
+            op[w][1] = mn ? smem_desc(t0 + 8192 + kk * 2048, 4096, 1024, LAYOUT_SW128)
+                          : smem_desc(t0 + 64 + kk * 32, 16, 1024, LAYOUT_SW128);
+          }
+          tc_mma_pair_f16(d, op[0][1], op[1][0], idesc16, (kin > 0 || kk > 0) ? 1u : 0u);
+          tc_mma_pair_f16(d, op[0][0], op[1][1], idesc16, 1);
+          tc_mma_pair_f16(d, op[0][0], op[1][0], idesc16, 1);
+        }
+        tc_commit_pair(bar_lempty(ls));
+        if (++kin == PAIR_CHUNK_KB || kb == nk - 1) {
+          tc_commit_pair(bar_accf(b));
+          last_committed = chunk;
+          chunk++;
+          kin = 0;
+        }
+      }
+      if (kin > 0 || last_committed < chunk - 1 || last_committed < 0) {
+        tc_commit_pair(bar_accf(chunk & 1));
+        last_committed = chunk;
+      }
+      const int b = last_committed & 1;
+      const long long t0 = clock64();
+      while (!mbar_try_wait(bar_accf(b), (last_committed >> 1) & 1)) {
+        if (clock64() - t0 > WAIT_LIMIT_CYCLES) { pair_abort(abort_flag, peer_flag, p.err, 3); break; }
+      }
+    }
+  } else {
+    // ------------------------- converter warps (2, 3, 12..15): 6 x 32 threads
+    const int ct = warp < 4 ? (warp - 2) * 32 + lane : 64 + (warp - 12) * 32 + lane;
+    for (int kb = 0; kb < nk; kb++) {
+      const int rs = kb % RAW_STAGES, ls = kb % LO_STAGES;
+      bool landed = mbar_wait_pair(bar_full(rs), (kb / RAW_STAGES) & 1, abort_flag, peer_flag, p.err, 4);
+      if (landed && kb >= LO_STAGES)
+        landed = mbar_wait_pair(bar_lempty(ls), ((kb / LO_STAGES) - 1) & 1, abort_flag, peer_flag, p.err, 8);
+      if (!__all_sync(0xffffffffu, landed)) break;
+      const uint8_t *src = raw_ring + rs * RAW_BYTES;
+      uint8_t *dst = lo_ring + ls * RAW_BYTES;
+      const int kg = kb0 + kb;
+      const int tp = kg >= p.seg_end1 ? 2 : (kg >= p.seg_end0 ? 1 : 0);
+      const float sca = scl[2 * tp], scb = scl[2 * tp + 1];
+      // Task = (tile, raw row tt, fp16 chunk j): 8 values of raw row tt (raw
+      // chunks 2j, 2j + 1) into hi chunk j and lo chunk j.  Raw row: K-major
+      // row tt (chunk c at c ^ (tt % 8)); MN-major box tt / 32, K row k =
+      // tt % 32 (chunk c at c ^ ((k % 4) * 2)).
+      for (int task = ct; task < 1024; task += WS_CONV_THREADS) {
+        const bool is_a = task < 512, mn = is_a ? A_MN : B_MN;
+        const int tt = (task & 511) >> 2, j = task & 3;
+        const float sc = is_a ? sca : scb;
+        const uint8_t *sb = src + (is_a ? 0 : TILE_A);
+        uint8_t *db = dst + (is_a ? 0 : TILE_A);
+        const int k = tt & 31;
+        const int rbase = mn ? (tt >> 5) * 4096 + k * 128 : tt * 128;
+        const int rxor = mn ? (k & 3) << 1 : (tt & 7);
+        uint32_t hw[4], lw[4];
+#pragma unroll
+        for (int u = 0; u < 2; u++) {
+          const float4 x = *reinterpret_cast<const float4 *>(sb + rbase + (((2 * j + u) ^ rxor) << 4));
+          const float v0 = x.x * sc, v1 = x.y * sc, v2 = x.z * sc, v3 = x.w * sc;
+          const float h0 = tf32_trunc(v0), h1 = tf32_trunc(v1), h2 = tf32_trunc(v2), h3 = tf32_trunc(v3);
+          hw[2 * u] = h2_bits(__floats2half2_rn(h0, h1));
+          hw[2 * u + 1] = h2_bits(__floats2half2_rn(h2, h3));
+          lw[2 * u] = h2_bits(__floats2half2_rn(v0 - h0, v1 - h1));
+          lw[2 * u + 1] = h2_bits(__floats2half2_rn(v2 - h2, v3 - h3));
+        }
+        int hoff, loff;
+        if (!mn) {
+          hoff = tt * 128 + ((j ^ (tt & 7)) << 4);
+          loff = tt * 128 + (((4 + j) ^ (tt & 7)) << 4);
+        } else {
+          const int blk = tt >> 6, ch = 4 * ((tt >> 5) & 1) + j;
+          hoff = blk * 4096 + (k >> 3) * 1024 + (k & 7) * 128 + ((ch ^ (k & 7)) << 4);
+          loff = hoff + 8192;
+        }
+        *reinterpret_cast<uint4 *>(db + hoff) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        *reinterpret_cast<uint4 *>(db + loff) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+      }
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive_remote(cluster_map(bar_ready(ls), 0));
+        mbar_arrive(bar_rempty(rs));
+      }
+    }
+  }
+  }
   tc_fence_before();
   cluster_sync_all();
   if (warp == 1) {
@@ -876,6 +1255,63 @@ __global__ void splitk_reduce_kernel(float *C, int ldc, const float *add, const 
   }
 }
 
+// The tail tiles of a tail-split pair launch: C = add + the tile's parts
+// summed in part order (add may be nullptr or C itself).  blockIdx.y = tail
+// tile.
+__global__ void tail_reduce_kernel(float *C, int ldc, const float *add, const float *__restrict__ ws, int full_tiles,
+                                   int splits, int I, int J) {
+  const int t = blockIdx.y;
+  int pm, tn;
+  pair_tile(full_tiles + t, I, J, &pm, &tn);
+  const int r0 = pm * PM, c0 = tn * PN;
+  const int rows = min(PM, I - r0), cols = min(PN, J - c0);
+  const float *src0 = ws + (size_t)t * splits * (PM * PN);
+  for (int q = blockIdx.x * blockDim.x + threadIdx.x; q < PM * PN / 4; q += gridDim.x * blockDim.x) {
+    const int r = q / (PN / 4), cc = (q % (PN / 4)) * 4;
+    if (r >= rows || cc >= cols) continue;     // cols is a multiple of 4 (row strides of 16 bytes)
+    const float *src = src0 + (size_t)r * PN + cc;
+    float4 acc = *reinterpret_cast<const float4 *>(src);
+    for (int z = 1; z < splits; z++) {
+      const float4 w = *reinterpret_cast<const float4 *>(src + (size_t)z * (PM * PN));
+      acc.x += w.x; acc.y += w.y; acc.z += w.z; acc.w += w.w;
+    }
+    const size_t o = (size_t)(r0 + r) * ldc + c0 + cc;
+    if (add) {
+      const float4 a4 = *reinterpret_cast<const float4 *>(add + o);
+      acc.x = a4.x + acc.x; acc.y = a4.y + acc.y; acc.z = a4.z + acc.z; acc.w = a4.w + acc.w;
+    }
+    *reinterpret_cast<float4 *>(C + o) = acc;
+  }
+}
+
+// CTA pairs of the pair kernel that can be resident at once on this device
+// (clusters of two must sit on one GPC, so this can be below SMs / 2);
+// 0 if unknown.
+static int pair_slots(DeviceCtx *c) {
+  static int slots[kMaxDevices] = {};
+  if (slots[c->device]) return slots[c->device] > 0 ? slots[c->device] : 0;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = 2; attr.val.clusterDim.y = 1; attr.val.clusterDim.z = 1;
+  cfg.gridDim = dim3(2 * 1024, 1, 1);
+  cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = PAIR_SMEM_BYTES;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  cudaError_t e = cudaFuncSetAttribute(gemm_tc_pair_kernel<false, true, false>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, PAIR_SMEM_BYTES);
+  if (e == cudaSuccess) e = cudaOccupancyMaxActiveClusters(&n, gemm_tc_pair_kernel<false, true, false>, &cfg);
+  if (e != cudaSuccess || n <= 0) {
+    cudaGetLastError();
+    slots[c->device] = -1;
+    return 0;
+  }
+  slots[c->device] = n;
+  return n;
+}
+
 template <bool A_MN, bool B_MN>
 static int launch(DeviceCtx *c, const CUtensorMap &ma, const CUtensorMap &mb, const Params &p, int splits) {
   static bool attr_set[kMaxDevices] = {};
@@ -898,18 +1334,39 @@ static int launch_pair(DeviceCtx *c, const CUtensorMap &ma, const CUtensorMap &m
                        const CUtensorMap *extra = nullptr) {
   static bool attr_set[kMaxDevices] = {};
   if (!attr_set[c->device]) {
-    TL_TRY_CUDA(cudaFuncSetAttribute(gemm_tc_pair_kernel<A_MN, B_MN, F16>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, PAIR_SMEM_BYTES));
+    if (F16)
+      TL_TRY_CUDA(cudaFuncSetAttribute(gemm_tc_pair_f16ws_kernel<A_MN, B_MN>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, PAIR_SMEM_BYTES));
+    else
+      TL_TRY_CUDA(cudaFuncSetAttribute(gemm_tc_pair_kernel<A_MN, B_MN, false>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, PAIR_SMEM_BYTES));
     attr_set[c->device] = true;
   }
-  const unsigned pairs = (unsigned)((p.I + PM - 1) / PM) * (unsigned)((p.J + PN - 1) / PN);
+  unsigned pairs = (unsigned)((p.I + PM - 1) / PM) * (unsigned)((p.J + PN - 1) / PN);
+  if (p.tail_splits > 1) pairs = (unsigned)(p.full_tiles + (pairs - p.full_tiles) * p.tail_splits);
   dim3 grid(2 * pairs, 1, splits);
   TraceScope ts(c, "gemm_tc_pair");
   // extra: the maps of the second and third products (A1, B1, A2, B2)
   const CUtensorMap &a1 = extra ? extra[0] : ma, &b1 = extra ? extra[1] : mb;
   const CUtensorMap &a2 = extra ? extra[2] : ma, &b2 = extra ? extra[3] : mb;
-  gemm_tc_pair_kernel<A_MN, B_MN, F16><<<grid, NUM_THREADS, PAIR_SMEM_BYTES, c->stream>>>(ma, mb, a1, b1, a2, b2,
-                                                                                          p);
+  if (F16) {
+    // The kernel moves registers between its warpgroups (setmaxnreg); the
+    // split adds up to 128 per thread at launch.  A build with any other
+    // launch count would wait forever in setmaxnreg.inc, so refuse it.
+    static int regs[kMaxDevices] = {};
+    if (!regs[c->device]) {
+      cudaFuncAttributes fa;
+      TL_TRY_CUDA(cudaFuncGetAttributes(&fa, gemm_tc_pair_f16ws_kernel<A_MN, B_MN>));
+      regs[c->device] = fa.numRegs;
+    }
+    if (regs[c->device] != 128)
+      return set_error(TL_EINVAL, "fp16-split kernel built with %d registers per thread, its register split needs 128",
+                       regs[c->device]);
+    gemm_tc_pair_f16ws_kernel<A_MN, B_MN><<<grid, WS_THREADS, PAIR_SMEM_BYTES, c->stream>>>(ma, mb, a1, b1, a2, b2, p);
+  }
+  else
+    gemm_tc_pair_kernel<A_MN, B_MN, false><<<grid, NUM_THREADS, PAIR_SMEM_BYTES, c->stream>>>(ma, mb, a1, b1, a2, b2,
+                                                                                              p);
   TL_TRY_CUDA(cudaGetLastError());
   return TL_OK;
 }
@@ -932,9 +1389,9 @@ bool gemm_tc_supported(GemmOp op, const float *C, const float *A, const float *B
 // Everything the launches set up lazily on the host (driver entry point,
 // shared-memory attributes), done ahead of a CUDA graph capture.
 int gemm_tc_prepare(DeviceCtx *c) {
-  (void)c;
   int rc = tc::get_encoder();
   if (rc) return rc;
+  (void)tc::pair_slots(c);
 #define TL_PREP(K, BYTES) TL_TRY_CUDA(cudaFuncSetAttribute(K, cudaFuncAttributeMaxDynamicSharedMemorySize, BYTES))
   TL_PREP((tc::gemm_tc_kernel<false, true>), tc::SMEM_BYTES);
   TL_PREP((tc::gemm_tc_kernel<false, false>), tc::SMEM_BYTES);
@@ -942,9 +1399,9 @@ int gemm_tc_prepare(DeviceCtx *c) {
   TL_PREP((tc::gemm_tc_pair_kernel<false, true, false>), tc::PAIR_SMEM_BYTES);
   TL_PREP((tc::gemm_tc_pair_kernel<false, false, false>), tc::PAIR_SMEM_BYTES);
   TL_PREP((tc::gemm_tc_pair_kernel<true, true, false>), tc::PAIR_SMEM_BYTES);
-  TL_PREP((tc::gemm_tc_pair_kernel<false, true, true>), tc::PAIR_SMEM_BYTES);
-  TL_PREP((tc::gemm_tc_pair_kernel<false, false, true>), tc::PAIR_SMEM_BYTES);
-  TL_PREP((tc::gemm_tc_pair_kernel<true, true, true>), tc::PAIR_SMEM_BYTES);
+  TL_PREP((tc::gemm_tc_pair_f16ws_kernel<false, true>), tc::PAIR_SMEM_BYTES);
+  TL_PREP((tc::gemm_tc_pair_f16ws_kernel<false, false>), tc::PAIR_SMEM_BYTES);
+  TL_PREP((tc::gemm_tc_pair_f16ws_kernel<true, true>), tc::PAIR_SMEM_BYTES);
 #undef TL_PREP
   return TL_OK;
 }
@@ -997,11 +1454,11 @@ static int gemm_tc_launch(DeviceCtx *c, GemmOp op, float *C, int I, int J, int n
   const int tm = pair ? tc::PM : tc::BM, tn = pair ? tc::PN : tc::BN, sms_per_tile = pair ? 2 : 1;
   const long long tiles = (long long)((I + tm - 1) / tm) * ((J + tn - 1) / tn);
   int splits = 1;
+  double best = 0.0;           // cost of the chosen split, in k-block times
   if (c->gemm_ws && !rope) {   // (RoPE needs the whole sum in the epilogue)
     const size_t cap = c->gemm_ws_floats / ((size_t)I * J);
     const int smax = (int)std::min<size_t>(std::min(64, nk / tc::CHUNK_KB), cap);
     const double out_units = (double)I * J * 4.0 / 6.0e6;  // one output pass, in k-block times
-    double best = 0.0;
     for (int s = 1; s <= std::max(1, smax); s++) {
       const long long ctas = tiles * sms_per_tile * s;
       const long long waves = (ctas + c->num_sms - 1) / c->num_sms;
@@ -1009,6 +1466,32 @@ static int gemm_tc_launch(DeviceCtx *c, GemmOp op, float *C, int I, int J, int n
       if (s > 1) kb = (kb + tc::CHUNK_KB - 1) / tc::CHUNK_KB * tc::CHUNK_KB;
       const double cost = (double)waves * kb + (s > 1 ? (s + 1) * out_units : 0.0);
       if (s == 1 || cost < best * 0.97) { best = cost; splits = s; }
+    }
+  }
+  // Tail split (pair kernel): when the tiles fill `full` waves of co-resident
+  // pairs and leave `rem` tiles for a last, partly empty wave, those rem
+  // tiles run as ts pairs each over a ts-th of the reduction (ts = slots /
+  // rem), their parts summed by a small fixed-order pass: the last wave then
+  // takes 1/ts of a tile's time.  E.g. a 16384 x 1024 output: 256 tiles =
+  // 3 waves of 74 pairs + 34 tiles; split 2 ways, 3.5 tile times instead of 4.
+  p.full_tiles = 0; p.tail_splits = 1; p.tail_kb = 0; p.tail_ws = nullptr;
+  if (pair && c->gemm_ws && !rope) {
+    const int slots = tc::pair_slots(c);
+    const long long full = slots > 0 ? tiles / slots * slots : tiles, rem = tiles - full;
+    if (slots > 0 && rem > 0) {
+      int ts = (int)std::min<long long>(slots / rem, nk / tc::PAIR_CHUNK_KB);
+      ts = (int)std::min<size_t>(ts, c->gemm_ws_floats / ((size_t)rem * tc::PM * tc::PN));
+      if (ts >= 2) {
+        int tkb = (nk + ts - 1) / ts;
+        tkb = (tkb + tc::PAIR_CHUNK_KB - 1) / tc::PAIR_CHUNK_KB * tc::PAIR_CHUNK_KB;
+        ts = (nk + tkb - 1) / tkb;
+        const double tail_units = (double)rem * (ts + 2) * tc::PM * tc::PN * 4.0 / 6.0e6;
+        const double cost = (double)(full / slots) * nk + tkb + tail_units;
+        if (ts >= 2 && cost < best * 0.97) {
+          splits = 1;
+          p.full_tiles = (int)full; p.tail_splits = ts; p.tail_kb = tkb; p.tail_ws = c->gemm_ws;
+        }
+      }
     }
   }
   int kb_per = nk;
@@ -1040,6 +1523,14 @@ static int gemm_tc_launch(DeviceCtx *c, GemmOp op, float *C, int I, int J, int n
            : f16 ? tc::launch_pair<true, true, true>(c, ma, mb, p, splits)
                  : tc::launch_pair<true, true, false>(c, ma, mb, p, splits);
       break;
+  }
+  if (!rc && p.tail_splits > 1) {
+    TraceScope ts(c, "gemm_tail_reduce");
+    const int ntail = (int)(tiles - p.full_tiles);
+    tc::tail_reduce_kernel<<<dim3(16, ntail), 256, 0, c->stream>>>(C, out_ldc, add, p.tail_ws, p.full_tiles,
+                                                                  p.tail_splits, I, J);
+    TL_TRY_CUDA(cudaGetLastError());
+    return TL_OK;
   }
   if (rc || splits == 1) return rc;
   TraceScope ts(c, "gemm_splitk_reduce");
