@@ -662,7 +662,7 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         if (kb >= nk || kb >= c_end + PAIR_DRAIN_LAG) {
           drain = true;
         } else if (kb >= c_end) {
-          const uint32_t done = lane == 0 ? (mbar_try_wait_cl(bar_accf(c & 1), (c >> 1) & 1) ? 1u : 0u) : 0u;
+          const uint32_t done = lane == 0 ? (mbar_test_cl(bar_accf(c & 1), (c >> 1) & 1) ? 1u : 0u) : 0u;
           drain = __shfl_sync(0xffffffffu, done, 0) != 0;
         }
       }
@@ -1101,7 +1101,13 @@ gemm_tc_pair_f16ws_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_
     }
   } else {
     // ------------------------- converter warps (2, 3, 12..15): 6 x 32 threads
-    const int ct = warp < 4 ? (warp - 2) * 32 + lane : 64 + (warp - 12) * 32 + lane;
+    const int cw = warp < 4 ? warp - 2 : warp - 10;   // converter warp 0..5
+    // Lane -> (row of an 8-row group, 16-byte chunk j): a quarter-warp (the
+    // unit of a 16-byte shared-memory access) takes rows r and r ^ 5 of the
+    // group, whose swizzled chunks fall in disjoint banks for the raw loads
+    // and for the hi / lo stores of both layouts.
+    const int qrow = (lane >> 3) ^ (((lane >> 2) & 1) ? 5 : 0), j = lane & 3;
+    const int half = (lane >> 2) & 1;
     for (int kb = 0; kb < nk; kb++) {
       const int rs = kb % RAW_STAGES, ls = kb % LO_STAGES;
       bool landed = mbar_wait_pair(bar_full(rs), (kb / RAW_STAGES) & 1, abort_flag, peer_flag, p.err, 4);
@@ -1113,13 +1119,14 @@ gemm_tc_pair_f16ws_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_
       const int kg = kb0 + kb;
       const int tp = kg >= p.seg_end1 ? 2 : (kg >= p.seg_end0 ? 1 : 0);
       const float sca = scl[2 * tp], scb = scl[2 * tp + 1];
-      // Task = (tile, raw row tt, fp16 chunk j): 8 values of raw row tt (raw
-      // chunks 2j, 2j + 1) into hi chunk j and lo chunk j.  Raw row: K-major
-      // row tt (chunk c at c ^ (tt % 8)); MN-major box tt / 32, K row k =
-      // tt % 32 (chunk c at c ^ ((k % 4) * 2)).
-      for (int task = ct; task < 1024; task += WS_CONV_THREADS) {
-        const bool is_a = task < 512, mn = is_a ? A_MN : B_MN;
-        const int tt = (task & 511) >> 2, j = task & 3;
+      // Unit = 32 tasks = 8 raw rows x 4 chunks; task = (tile, raw row tt,
+      // fp16 chunk j): 8 values of raw row tt (raw chunks 2j, 2j + 1) into hi
+      // chunk j and lo chunk j.  Raw row: K-major row tt (chunk c at
+      // c ^ (tt % 8)); MN-major box tt / 32, K row k = tt % 32 (chunk c at
+      // c ^ ((k % 4) * 2)).  Units 0-15: A tile, 16-31: this CTA's B half.
+      for (int unit = cw; unit < 32; unit += WS_CONV_WARPS) {
+        const bool is_a = unit < 16, mn = is_a ? A_MN : B_MN;
+        const int tt = (unit & 15) * 8 + qrow;
         const float sc = is_a ? sca : scb;
         const uint8_t *sb = src + (is_a ? 0 : TILE_A);
         uint8_t *db = dst + (is_a ? 0 : TILE_A);
@@ -1127,9 +1134,14 @@ gemm_tc_pair_f16ws_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_
         const int rbase = mn ? (tt >> 5) * 4096 + k * 128 : tt * 128;
         const int rxor = mn ? (k & 3) << 1 : (tt & 7);
         uint32_t hw[4], lw[4];
+        // MN-major rows of a quarter-warp share the even (odd) chunks: the
+        // second row of each quarter loads its odd chunk first.
+        const int u0 = mn ? half : 0;
+        const float4 xa = *reinterpret_cast<const float4 *>(sb + rbase + (((2 * j + u0) ^ rxor) << 4));
+        const float4 xb = *reinterpret_cast<const float4 *>(sb + rbase + (((2 * j + (u0 ^ 1)) ^ rxor) << 4));
 #pragma unroll
         for (int u = 0; u < 2; u++) {
-          const float4 x = *reinterpret_cast<const float4 *>(sb + rbase + (((2 * j + u) ^ rxor) << 4));
+          const float4 x = (u == 0) == (u0 == 0) ? xa : xb;
           const float v0 = x.x * sc, v1 = x.y * sc, v2 = x.z * sc, v3 = x.w * sc;
           const float h0 = tf32_trunc(v0), h1 = tf32_trunc(v1), h2 = tf32_trunc(v2), h3 = tf32_trunc(v3);
           hw[2 * u] = h2_bits(__floats2half2_rn(h0, h1));

@@ -25,12 +25,17 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
   asm volatile("{ .reg .b64 st; mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1; }" ::"r"(bar), "r"(bytes)
                : "memory");
 }
+// Waiting threads are suspended by the barrier (up to SUSPEND_NS per try, or
+// until the phase completes) instead of spinning: a spinning wait loop issues
+// an instruction stream of its own that competes with the working warps for
+// issue slots and power.
+constexpr uint32_t SUSPEND_NS = 10000000u;
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
-      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
       : "=r"(ok)
-      : "r"(bar), "r"(parity)
+      : "r"(bar), "r"(parity), "r"(SUSPEND_NS)
       : "memory");
   return ok != 0;
 }
@@ -119,7 +124,17 @@ __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
 __device__ __forceinline__ bool mbar_try_wait_cl(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
-      "{ .reg .pred p; mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+      "{ .reg .pred p; mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(SUSPEND_NS)
+      : "memory");
+  return ok != 0;
+}
+// Non-blocking test of a phase (cluster scope), for polls between work items.
+__device__ __forceinline__ bool mbar_test_cl(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{ .reg .pred p; mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
       : "=r"(ok)
       : "r"(bar), "r"(parity)
       : "memory");
