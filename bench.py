@@ -233,12 +233,13 @@ class Run:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return t.item()
 
-    def timed(self, step, steps, t0):
+    def timed(self, step, steps, t0, trace=True):
         """K steps between barriers; device time from CUDA events on the
-        launching stream, max over ranks; per-kernel times from the tracer."""
+        launching stream, max over ranks; per-kernel times from the tracer
+        (trace=False: no per-launch events inside the timed region)."""
         torch, L = self.torch, self.L
         L.tl_trace_reset()
-        L.tl_trace_enable(1)
+        L.tl_trace_enable(1 if trace else 0)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with ClockSampler(gpu_uuid(torch, self.dev)) as clk:
             self.barrier()
@@ -249,7 +250,7 @@ class Run:
             self.barrier()
         L.tl_trace_enable(0)
         ms = self.max_over_ranks(e0.elapsed_time(e1))
-        return ms / steps, self.kernels(steps), clk.summary()
+        return ms / steps, self.kernels(steps) if trace else {}, clk.summary()
 
     def kernels(self, steps):
         L, _lib = self.L, self._lib
@@ -391,19 +392,17 @@ def run_train(args, rk):
     rk.torch.cuda.synchronize()
     rk.status()
     t0 = 1 + args.warmup
-    ms_step, kernels, clocks = rk.timed(step, args.steps, t0)
+    # The timed steps run without per-launch trace events (at N=1 the step is
+    # one graph replay anyway); the per-kernel breakdown and the GEMM roofline
+    # come from the same step run again, eagerly, with every launch traced.
+    ms_step, _, clocks = rk.timed(step, args.steps, t0, trace=False)
     rk.status()
     value = B_glob * T_CTX / (ms_step * 1e-3)
     loss_val = loss.item()
-    eager_ms = None
-    if use_graph:
-        # A graph replay is one traced launch; the per-kernel breakdown (and the
-        # GEMM roofline) comes from the same step run eagerly with every launch
-        # traced.
-        n_tr = max(1, min(args.steps, 2))
-        eager_ms, kernels, _ = rk.timed(eager_step, n_tr, t0 + args.steps)
-        rk.status()
-        t0 += n_tr
+    n_tr = max(1, min(args.steps, 2))
+    eager_ms, kernels, _ = rk.timed(eager_step if world == 1 else step, n_tr, t0 + args.steps)
+    rk.status()
+    t0 += n_tr
 
     # ---- end to end: tokens from pinned host memory, loss read back, every step
     e2e = None
@@ -448,9 +447,8 @@ def run_train(args, rk):
     if tr:
         roofline["traffic"] = tr.get("bytes_per_step")
         roofline["traffic_source"] = tr.get("source")
-    launches = sum(k["launches"] for k in kernels.values())
-    if use_graph:   # the eager pass ran n_tr steps; the timed region replayed the same kernels args.steps times
-        launches = launches * args.steps // n_tr
+    # the traced pass ran n_tr steps; the timed region ran the same kernels args.steps times
+    launches = sum(k["launches"] for k in kernels.values()) * args.steps // n_tr
 
     adam_line = None
     if kernels.get("adamw_vec", {}).get("ms_per_launch"):
@@ -478,8 +476,7 @@ def run_train(args, rk):
                           "l2": "per-step working set >> 126 MB L2 (no flush needed)"},
                "e2e": e2e, "roofline": roofline, "clocks": clocks, "gpu_launches": launches,
                "loss": round(loss_val, 5), "kernels": kernels}
-        if eager_ms is not None:
-            out["eager_ms_per_step"] = round(eager_ms, 3)
+        out["traced_ms_per_step"] = round(eager_ms, 3)
         if adam_line:
             out["fused_adamw"] = adam_line
     return out
@@ -797,7 +794,7 @@ GEMM_SAMPLE = ((16384, 2816, 2816), (16384, 1024, 2816), (16384, 2816, 1024), (6
 
 
 def _compact(line, keep=("metric", "value", "unit", "ms_per_step", "steps", "warmup", "config", "e2e", "roofline",
-                         "cpu_baseline", "gpu_launches", "clocks", "loss", "eager_ms_per_step")):
+                         "cpu_baseline", "gpu_launches", "clocks", "loss", "traced_ms_per_step")):
     return {k: line[k] for k in keep if k in line}
 
 

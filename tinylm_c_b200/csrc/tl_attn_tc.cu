@@ -931,13 +931,16 @@ attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmKk, const __grid_c
     // The chunk's 32 lse and D values, one per lane, loaded a chunk ahead and
     // broadcast by shuffles.
     auto chunk_row = [&](int i) { return ((size_t)bb * a.H + kvh * grp + i / nc) * T + BW_NQ * (c0 + i % nc); };
-    float l_nx = __ldg(a.lse + chunk_row(0) + lane), d_nx = __ldg(a.Drow + chunk_row(0) + lane);
+    // P = exp(scale s - lse) = 2^(s scale log2(e) - lse log2(e)); lse is kept
+    // pre-multiplied by log2(e).
+    const float c2 = a.scale * 1.4426950408889634f;
+    float l_nx = __ldg(a.lse + chunk_row(0) + lane) * 1.4426950408889634f, d_nx = __ldg(a.Drow + chunk_row(0) + lane);
     for (int i = 0; i < n; i++) {
       const int b = i & 1, q0 = BW_NQ * (c0 + i % nc);
       const size_t crow = chunk_row(i);
       const float l_me = l_nx, d_me = d_nx;
       if (i + 1 < n) {
-        l_nx = __ldg(a.lse + chunk_row(i + 1) + lane);
+        l_nx = __ldg(a.lse + chunk_row(i + 1) + lane) * 1.4426950408889634f;
         d_nx = __ldg(a.Drow + chunk_row(i + 1) + lane);
       }
       if (!__all_sync(0xffffffffu, mbar_wait(bar(SD_FULL + b), (i >> 1) & 1, abort_flag, a.err, 71))) break;
@@ -950,7 +953,7 @@ attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmKk, const __grid_c
 #pragma unroll
       for (int e = 0; e < 32; e++) {
         const float ls = __shfl_sync(0xffffffffu, l_me, e), ds = __shfl_sync(0xffffffffu, d_me, e);
-        const float pr = key <= q0 + e ? expf(__uint_as_float(sv[e]) * a.scale - ls) : 0.0f;
+        const float pr = key <= q0 + e ? exp2f(fmaf(__uint_as_float(sv[e]), c2, -ls)) : 0.0f;
         ph[e] = pr;
         dh[e] = pr * (__uint_as_float(dv[e]) - ds) * a.scale;
       }

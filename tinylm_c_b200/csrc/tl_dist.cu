@@ -18,6 +18,7 @@
 #include <thread>
 #include "tl_common.cuh"
 #include "tl_dist.cuh"
+#include "tl_trace.cuh"
 
 namespace tl {
 int launch_sumsq(DeviceCtx *c, const float *G, size_t n, double *sumsq_out, float *norm_out,
@@ -97,15 +98,18 @@ bool dist_rank_world(int *rank, int *world) {
 }
 
 // All-gather `bytes` bytes per rank between device buffers on the library
-// stream, then wait for it with the host deadline.
+// stream, then wait for it with the host deadline.  Used for set-up exchanges
+// (peer-memory registration), so it is bounded like communicator creation
+// (TL_DIST_INIT_TIMEOUT_MS): the first collective on a communicator also
+// builds its connections, which can take seconds on a cold node.
 int dist_allgather_bytes(const void *send_dev, void *recv_dev, size_t bytes) {
   TL_REQUIRE_CTX(c);
   DistCtx *d = dist();
   if (!d) return set_error(TL_ENOINIT, "tl_dist_init() not called for this device");
   ncclResult_t r = ncclAllGather(send_dev, recv_dev, bytes, ncclInt8, d->comm, c->stream);
-  int rc = nccl_settle(*d, r, "ncclAllGather(bytes)");
+  int rc = nccl_settle(*d, r, "ncclAllGather(bytes)", init_timeout_ms());
   if (rc) return rc;
-  return tl_dist_sync(0);
+  return tl_dist_sync(init_timeout_ms());
 }
 
 }  // namespace tl
@@ -229,8 +233,11 @@ static int zero1_tail(DeviceCtx *c, DistCtx *d, float *P, float *G, float *M_sha
   ncclResult_t r = ncclAllReduce(c->sumsq, c->sumsq, 1, ncclDouble, ncclSum, d->comm, c->stream);
   if ((rc = nccl_settle(*d, r, "ncclAllReduce(sumsq)"))) return rc;
   float *gscale = c->scalars + 1;
-  clip_scale_kernel<<<1, 1, 0, c->stream>>>(c->sumsq, max_norm, norm_dev, gscale);
-  TL_TRY_CUDA(cudaGetLastError());
+  {
+    TraceScope ts(c, "clip_scale");
+    clip_scale_kernel<<<1, 1, 0, c->stream>>>(c->sumsq, max_norm, norm_dev, gscale);
+    TL_TRY_CUDA(cudaGetLastError());
+  }
   if ((rc = launch_adamw(c, Ps, Gs, M_shard, V_shard, shard, lr, b1, b2, wd, t, 1.0f, gscale))) return rc;
   r = ncclAllGather(Ps, P, shard, ncclFloat, d->comm, c->stream);
   return nccl_settle(*d, r, "ncclAllGather(P)");

@@ -768,17 +768,20 @@ int k_rmsnorm_fwd(DeviceCtx *c, const float *x, const float *g, float *out, floa
 }
 int k_rmsnorm_bwd(DeviceCtx *c, const float *x, const float *g, const float *rinv, const float *dy,
                   const float *dres, float *dx, float *dg, float *part, int part_rows, int rows, int D) {
-  TraceScope ts(c, "k_rmsnorm_bwd");
   int nb = (rows + 7) / 8;
   if (nb > part_rows) nb = part_rows;
   const bool vec = D % 4 == 0 &&
                    ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(g) | reinterpret_cast<uintptr_t>(dy) |
                      reinterpret_cast<uintptr_t>(dx) | reinterpret_cast<uintptr_t>(dres)) & 15) == 0;
-  if (vec)
-    mk::rmsnorm_bwd4_kernel<<<nb, 256, sizeof(float) * 8 * D, c->stream>>>(x, g, rinv, dy, dres, dx, part, rows, D);
-  else
-    mk::rmsnorm_bwd_kernel<<<nb, 256, sizeof(float) * 8 * D, c->stream>>>(x, g, rinv, dy, dres, dx, part, rows, D);
-  MK_LAUNCH_CHECK();
+  {
+    TraceScope ts(c, "k_rmsnorm_bwd");
+    if (vec)
+      mk::rmsnorm_bwd4_kernel<<<nb, 256, sizeof(float) * 8 * D, c->stream>>>(x, g, rinv, dy, dres, dx, part, rows, D);
+    else
+      mk::rmsnorm_bwd_kernel<<<nb, 256, sizeof(float) * 8 * D, c->stream>>>(x, g, rinv, dy, dres, dx, part, rows, D);
+    MK_LAUNCH_CHECK();
+  }
+  TraceScope ts(c, "k_colsum_add");
   mk::colsum_add_kernel<<<(D + 31) / 32, 256, 0, c->stream>>>(part, nb, D, dg);
   MK_LAUNCH_CHECK();
   return TL_OK;
@@ -873,11 +876,13 @@ int k_attn_fwd(DeviceCtx *c, const float *q, const float *k, const float *v, flo
 int k_attn_bwd(DeviceCtx *c, const float *q, const float *k, const float *v, const float *out, const float *dout,
                const float *lse, float *Drow, float *dsT, float *dq, float *dk, float *dv, int B, int T, int H,
                int KV, int hd, const float *cosT, const float *sinT) {
-  TraceScope ts(c, "k_attn_bwd");
   const float scale = 1.0f / sqrtf((float)hd);
   const int rows = B * H * T;
-  mk::attn_rowdot_kernel<<<(rows + 7) / 8, 256, 0, c->stream>>>(dout, out, Drow, B, T, H, hd);
-  MK_LAUNCH_CHECK();
+  {
+    TraceScope ts(c, "k_attn_rowdot");
+    mk::attn_rowdot_kernel<<<(rows + 7) / 8, 256, 0, c->stream>>>(dout, out, Drow, B, T, H, hd);
+    MK_LAUNCH_CHECK();
+  }
   // The tensor-core kernels apply RoPE's backward to dK / dQ as they store
   // them; after the CUDA-core kernels it is a separate pass.
   const float *ptrs[9] = {q, k, v, dout, lse, Drow, dsT, dk, dv};
@@ -887,6 +892,7 @@ int k_attn_bwd(DeviceCtx *c, const float *q, const float *k, const float *v, con
     if (rc) return rc;
     dk_rotated = true;
   } else {
+    TraceScope ts(c, "k_attn_bwd_dkdv");
     mk::attn_bwd_dkdv_kernel<<<B * KV * (T / mk::AT), 256, attn_smem_dkdv(), c->stream>>>(
         q, k, v, dout, lse, Drow, dk, dv, dsT, T, H, KV, hd, scale);
     MK_LAUNCH_CHECK();
@@ -896,6 +902,7 @@ int k_attn_bwd(DeviceCtx *c, const float *q, const float *k, const float *v, con
     if (rc) return rc;
     dq_rotated = true;
   } else {
+    TraceScope ts(c, "k_attn_bwd_dq");
     mk::attn_bwd_dq_kernel<<<B * H * (T / mk::AT), 256, attn_smem_dq(), c->stream>>>(k, dsT, dq, T, H, KV, hd);
     MK_LAUNCH_CHECK();
   }

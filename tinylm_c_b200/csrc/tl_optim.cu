@@ -198,6 +198,7 @@ TL_API int tl_clip_scale(const double *sumsq_dev, float max_norm, float *norm_de
   int rc;
   if ((rc = check_device_ptr(sumsq_dev, "sumsq_dev"))) return rc;
   if (!(max_norm > 0.0f)) return set_error(TL_EINVAL, "max_norm must be > 0");
+  TraceScope ts(c, "clip_scale");
   clip_scale_kernel<<<1, 1, 0, c->stream>>>(sumsq_dev, max_norm, norm_dev, gscale_dev);
   TL_TRY_CUDA(cudaGetLastError());
   return TL_OK;

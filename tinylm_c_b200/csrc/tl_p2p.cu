@@ -393,8 +393,11 @@ TL_API int tl_zero1_step_p2p(float *P, float *G, float *M_shard, float *V_shard,
     TL_TRY_CUDA(cudaGetLastError());
   }
   float *gscale = c->scalars + 1;
-  p2p_clip_kernel<<<1, 32, 0, c->stream>>>(x.own, x.world, ep, max_norm, norm_dev, gscale, lim, c->err_flag);
-  TL_TRY_CUDA(cudaGetLastError());
+  {
+    TraceScope ts(c, "p2p_clip");
+    p2p_clip_kernel<<<1, 32, 0, c->stream>>>(x.own, x.world, ep, max_norm, norm_dev, gscale, lim, c->err_flag);
+    TL_TRY_CUDA(cudaGetLastError());
+  }
   {
     TraceScope ts(c, "p2p_adamw");
     const AdamArgs a = make_adam_args(lr, b1, b2, wd, t, 1.0f, gscale);
