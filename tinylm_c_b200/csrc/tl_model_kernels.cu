@@ -594,6 +594,38 @@ __global__ void attn_rowdot_kernel(const float *__restrict__ dout, const float *
   if (lane == 0) Drow[warp] = acc;
 }
 
+// The same row dot for head_dim 64 and up to 16 heads: a warp per token row
+// covers all H heads with float4 loads (16 lanes per head, two heads per
+// 32-lane pass), all passes' loads issued before the reductions, so a warp
+// has the whole row (2 x 4 KB at H = 16) in flight instead of 2 x 256 B.
+__global__ void __launch_bounds__(256)
+attn_rowdot64_kernel(const float4 *__restrict__ dout, const float4 *__restrict__ out, float *__restrict__ Drow,
+                     int B, int T, int H) {
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (row >= B * T) return;
+  const int b = row / T, t = row % T;
+  const int n4 = H * 16;                       // float4 per token row (<= 256)
+  const size_t o = (size_t)row * n4;
+  float part[8];
+#pragma unroll
+  for (int k = 0; k < 8; k++) {
+    const int i = k * 32 + lane;
+    part[k] = 0.0f;
+    if (i < n4) {
+      const float4 x = __ldg(dout + o + i), y = __ldg(out + o + i);
+      part[k] = x.x * y.x + x.y * y.y + x.z * y.z + x.w * y.w;
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 8; k++) {
+    float acc = part[k];
+#pragma unroll
+    for (int m = 8; m > 0; m >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, m);
+    const int h = 2 * k + (lane >> 4);
+    if ((lane & 15) == 0 && h < H) Drow[((size_t)b * H + h) * T + t] = acc;
+  }
+}
+
 // Backward, key side: CTA per (b, kv head, key tile); loops over the group's
 // query heads and the query tiles at or after the key tile:
 //   S^T = K Q^T and dP^T = V dO^T in one k loop, P^T, dS^T as above,
@@ -880,7 +912,11 @@ int k_attn_bwd(DeviceCtx *c, const float *q, const float *k, const float *v, con
   const int rows = B * H * T;
   {
     TraceScope ts(c, "k_attn_rowdot");
-    mk::attn_rowdot_kernel<<<(rows + 7) / 8, 256, 0, c->stream>>>(dout, out, Drow, B, T, H, hd);
+    if (hd == 64 && H <= 16 && ((reinterpret_cast<uintptr_t>(dout) | reinterpret_cast<uintptr_t>(out)) & 15) == 0)
+      mk::attn_rowdot64_kernel<<<(B * T + 7) / 8, 256, 0, c->stream>>>(
+          reinterpret_cast<const float4 *>(dout), reinterpret_cast<const float4 *>(out), Drow, B, T, H);
+    else
+      mk::attn_rowdot_kernel<<<(rows + 7) / 8, 256, 0, c->stream>>>(dout, out, Drow, B, T, H, hd);
     MK_LAUNCH_CHECK();
   }
   // The tensor-core kernels apply RoPE's backward to dK / dQ as they store
