@@ -835,7 +835,6 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
 // 256 x 200 = 512 x 128, the launch's own total.
 constexpr int WS_THREADS = 512;
 constexpr int WS_CONV_WARPS = 6;
-constexpr int WS_CONV_THREADS = 32 * WS_CONV_WARPS;
 constexpr int WS_DRAIN_WARPS = 8;
 constexpr int WS_REG_SMALL = 56, WS_REG_ACC = 200;
 static_assert(128 * WS_REG_SMALL * 2 + 256 * WS_REG_ACC == WS_THREADS * 128, "register split must match the launch");

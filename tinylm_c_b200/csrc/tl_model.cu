@@ -41,7 +41,7 @@ struct Model {
   float *x_final, *fn, *fn_rinv, *logits;
   float *dact, *dgb, *du, *dout, *dfnorm, *dfin, *datt, *dq, *dnorm, *dain, *dfn, *dk, *dv, *Drow, *dsT;
   float *t1, *hk, *dhk, *dt1;
-  float *rms_part;
+  float *rms_part, *rms_tmp;   // gain-gradient partial rows and their middle level
   double *loss_rows, *loss_acc;
   // CUDA graph of one whole training step (tl_model_graph_step): the buffers
   // it was captured with, and the per-step scalars it reads on the device
@@ -160,7 +160,7 @@ static int micro_step(DeviceCtx *c, Model &m, const float *P, float *G, const in
     TRY(gemm(c, GemmOp::NT, m.dfn, m.dt1, Wk, N, D, D));
   }
   TRY(k_rmsnorm_bwd(c, m.x_final, P + m.o_nf, m.fn_rinv, m.dfn, nullptr, m.dout, G + m.o_nf, m.rms_part,
-                    RMS_PART_ROWS, N, D));
+                    RMS_PART_ROWS, N, D, m.rms_tmp));
   if (ov) TRY(overlap_ready(c, ov, m.o_nf));            // final norm and MTP heads are done
   for (int l = m.L - 1; l >= 0; l--) {
     // FFN
@@ -176,7 +176,7 @@ static int micro_step(DeviceCtx *c, Model &m, const float *P, float *G, const in
     TRY(gemm(c, GemmOp::TN, G + m.o_w3[l], m.f_norm[l], m.du, N, D, F));
     // dfin = dout + rmsnorm2 backward
     TRY(k_rmsnorm_bwd(c, m.f_in[l], P + m.o_an2[l], m.rinv2[l], m.dfnorm, m.dout, m.dfin, G + m.o_an2[l],
-                      m.rms_part, RMS_PART_ROWS, N, D));
+                      m.rms_part, RMS_PART_ROWS, N, D, m.rms_tmp));
     // attention output projection
     TRY(gemm_add(c, GemmOp::NT, m.datt, m.dfin, P + m.o_wo[l], N, D, D, nullptr));
     TRY(gemm(c, GemmOp::TN, G + m.o_wo[l], m.att[l], m.dfin, N, D, D));
@@ -193,7 +193,7 @@ static int micro_step(DeviceCtx *c, Model &m, const float *P, float *G, const in
     TRY(gemm(c, GemmOp::TN, G + m.o_wv[l], m.a_norm[l], m.dv, N, D, KD));
     // dain = dfin + rmsnorm1 backward; becomes the next layer's dout
     TRY(k_rmsnorm_bwd(c, m.a_in[l], P + m.o_an1[l], m.rinv1[l], m.dnorm, m.dfin, m.dain, G + m.o_an1[l],
-                      m.rms_part, RMS_PART_ROWS, N, D));
+                      m.rms_part, RMS_PART_ROWS, N, D, m.rms_tmp));
     std::swap(m.dout, m.dain);
     if (ov) TRY(overlap_ready(c, ov, m.o_an1[l]));       // layers l..L-1 are done
   }
@@ -256,6 +256,7 @@ static int alloc_model(Model &m) {
   slots.push_back({&m.Drow, take(att_rows)});
   slots.push_back({&m.dsT, take(att_rows * m.T)});
   slots.push_back({&m.rms_part, take((size_t)RMS_PART_ROWS * D)});
+  slots.push_back({&m.rms_tmp, take(8 * D)});
   const size_t o_loss = take(2 * N + 2);  // doubles: N rows + accumulator
   TL_TRY_CUDA(cudaMalloc(&m.arena, floats * sizeof(float)));
   float *base = static_cast<float *>(m.arena);

@@ -12,9 +12,10 @@ int k_embed_fwd(DeviceCtx *c, const float *emb, const int *tok, float *out, int 
 int k_embed_bwd(DeviceCtx *c, float *gemb, const int *tok, const float *dout, int N, int D, int V);
 int k_rmsnorm_fwd(DeviceCtx *c, const float *x, const float *g, float *out, float *rinv, int rows, int D);
 // dx = dres + RMSNorm backward of dy (dres: nullptr, dx itself, or another
-// array); dg += the gain gradient (fixed-order two-stage reduction).
+// array); dg += the gain gradient (fixed-order reduction of per-block partial
+// rows `part`; tmp, 8 x D floats or nullptr, holds its middle level).
 int k_rmsnorm_bwd(DeviceCtx *c, const float *x, const float *g, const float *rinv, const float *dy,
-                  const float *dres, float *dx, float *dg, float *part, int part_rows, int rows, int D);
+                  const float *dres, float *dx, float *dg, float *part, int part_rows, int rows, int D, float *tmp);
 int k_rope(DeviceCtx *c, float *buf, const float *cosT, const float *sinT, int rows, int nh, int hd, int T, int back);
 int k_add(DeviceCtx *c, float *y, const float *x, size_t n);
 int k_swiglu_fwd(DeviceCtx *c, const float *g, const float *u, float *act, size_t n);

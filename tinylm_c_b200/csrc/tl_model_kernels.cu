@@ -117,6 +117,34 @@ __global__ void rmsnorm_fwd_kernel(const float *__restrict__ x, const float *__r
   for (int i = lane; i < D; i += 32) orow[i] = xr[i] * s * g[i];
 }
 
+// The same with the row held in registers: D = 128 * NV, float4 loads, x read
+// once (one warp per row).
+template <int NV>
+__global__ void __launch_bounds__(256)
+rmsnorm_fwd_reg_kernel(const float4 *__restrict__ x, const float4 *__restrict__ g, float4 *__restrict__ out,
+                       float *__restrict__ rinv, int rows) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  constexpr int D = 128 * NV;
+  const float4 *xr = x + (size_t)warp * (D / 4);
+  float4 v[NV];
+  float ms = 0.0f;
+#pragma unroll
+  for (int k = 0; k < NV; k++) {
+    v[k] = __ldg(xr + k * 32 + lane);
+    ms += v[k].x * v[k].x + v[k].y * v[k].y + v[k].z * v[k].z + v[k].w * v[k].w;
+  }
+  ms = warp_sum_f(ms);
+  const float s = 1.0f / sqrtf(ms / D + 1e-5f);
+  if (lane == 0) rinv[warp] = s;
+  float4 *orow = out + (size_t)warp * (D / 4);
+#pragma unroll
+  for (int k = 0; k < NV; k++) {
+    const float4 gg = __ldg(g + k * 32 + lane);
+    orow[k * 32 + lane] = make_float4(v[k].x * s * gg.x, v[k].y * s * gg.y, v[k].z * s * gg.z, v[k].w * s * gg.w);
+  }
+}
+
 // dx += s*g*dy - (s^3/D * sum(x*g*dy)) * x ; per-block partial of dg = sum_rows x*s*dy.
 // (tinylm.c:568-588; the per-thread buffers + critical section become a fixed-
 // order two-stage reduction.)  Block b handles rows b*8+w, stepping gridDim*8.
@@ -221,6 +249,39 @@ colsum_add_kernel(const float *__restrict__ part, int nparts, int D, float *__re
     for (int k = 1; k < 8; k++) t += ws[k][lane];
     dg[i] += t;
   }
+}
+
+// The gain gradient's column sums in two fixed-order levels: block (cx, cy)
+// sums partial rows [cy * per, (cy + 1) * per) of columns cx * 32 .. + 31
+// into tmp[cy]; colsum_final_kernel adds the COLSUM_SPLIT sums in cy order
+// into dg.  (The one-level kernel above runs only D / 32 blocks.)
+constexpr int COLSUM_SPLIT = 8;
+__global__ void __launch_bounds__(256)
+colsum_split_kernel(const float *__restrict__ part, int nparts, int D, float *__restrict__ tmp) {
+  __shared__ float ws[8][32];
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int i = blockIdx.x * 32 + lane;
+  const int per = (nparts + COLSUM_SPLIT - 1) / COLSUM_SPLIT;
+  const int r0 = blockIdx.y * per, r1 = min(nparts, r0 + per);
+  float acc = 0.0f;
+  if (i < D)
+    for (int b = r0 + w; b < r1; b += 8) acc += part[(size_t)b * D + i];
+  ws[w][lane] = acc;
+  __syncthreads();
+  if (w == 0 && i < D) {
+    float t = ws[0][lane];
+#pragma unroll
+    for (int k = 1; k < 8; k++) t += ws[k][lane];
+    tmp[(size_t)blockIdx.y * D + i] = t;
+  }
+}
+__global__ void colsum_final_kernel(const float *__restrict__ tmp, int D, float *__restrict__ dg) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= D) return;
+  float t = tmp[i];
+#pragma unroll
+  for (int k = 1; k < COLSUM_SPLIT; k++) t += tmp[(size_t)k * D + i];
+  dg[i] += t;
 }
 
 // ------------------------------------------------------------------- RoPE
@@ -794,12 +855,21 @@ int k_embed_bwd(DeviceCtx *c, float *gemb, const int *tok, const float *dout, in
 }
 int k_rmsnorm_fwd(DeviceCtx *c, const float *x, const float *g, float *out, float *rinv, int rows, int D) {
   TraceScope ts(c, "k_rmsnorm_fwd");
-  mk::rmsnorm_fwd_kernel<<<(rows + 7) / 8, 256, 0, c->stream>>>(x, g, out, rinv, rows, D);
+  const bool al = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(g) |
+                    reinterpret_cast<uintptr_t>(out)) & 15) == 0;
+  const unsigned grid = (unsigned)((rows + 7) / 8);
+  const float4 *x4 = reinterpret_cast<const float4 *>(x), *g4 = reinterpret_cast<const float4 *>(g);
+  float4 *o4 = reinterpret_cast<float4 *>(out);
+  if (al && D == 1024) mk::rmsnorm_fwd_reg_kernel<8><<<grid, 256, 0, c->stream>>>(x4, g4, o4, rinv, rows);
+  else if (al && D == 512) mk::rmsnorm_fwd_reg_kernel<4><<<grid, 256, 0, c->stream>>>(x4, g4, o4, rinv, rows);
+  else if (al && D == 256) mk::rmsnorm_fwd_reg_kernel<2><<<grid, 256, 0, c->stream>>>(x4, g4, o4, rinv, rows);
+  else if (al && D == 128) mk::rmsnorm_fwd_reg_kernel<1><<<grid, 256, 0, c->stream>>>(x4, g4, o4, rinv, rows);
+  else mk::rmsnorm_fwd_kernel<<<grid, 256, 0, c->stream>>>(x, g, out, rinv, rows, D);
   MK_LAUNCH_CHECK();
   return TL_OK;
 }
 int k_rmsnorm_bwd(DeviceCtx *c, const float *x, const float *g, const float *rinv, const float *dy,
-                  const float *dres, float *dx, float *dg, float *part, int part_rows, int rows, int D) {
+                  const float *dres, float *dx, float *dg, float *part, int part_rows, int rows, int D, float *tmp) {
   int nb = (rows + 7) / 8;
   if (nb > part_rows) nb = part_rows;
   const bool vec = D % 4 == 0 &&
@@ -814,7 +884,13 @@ int k_rmsnorm_bwd(DeviceCtx *c, const float *x, const float *g, const float *rin
     MK_LAUNCH_CHECK();
   }
   TraceScope ts(c, "k_colsum_add");
-  mk::colsum_add_kernel<<<(D + 31) / 32, 256, 0, c->stream>>>(part, nb, D, dg);
+  if (tmp && nb >= 8 * mk::COLSUM_SPLIT) {
+    mk::colsum_split_kernel<<<dim3((D + 31) / 32, mk::COLSUM_SPLIT), 256, 0, c->stream>>>(part, nb, D, tmp);
+    MK_LAUNCH_CHECK();
+    mk::colsum_final_kernel<<<(D + 255) / 256, 256, 0, c->stream>>>(tmp, D, dg);
+  } else {
+    mk::colsum_add_kernel<<<(D + 31) / 32, 256, 0, c->stream>>>(part, nb, D, dg);
+  }
   MK_LAUNCH_CHECK();
   return TL_OK;
 }
