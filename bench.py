@@ -38,8 +38,10 @@ sys.path.insert(0, ROOT)
 # NCCL's communicator set-up lines (rank count, transports, NVLS) go to the log;
 # descriptor 1 is redirected to stderr for the run (run_as_script), so they
 # cannot precede the JSON line.
-os.environ.setdefault("NCCL_DEBUG", "INFO")
-os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+# Set unconditionally: an NCCL_DEBUG=WARN inherited from the environment
+# would hide the lines that show each communicator's rank count.
+os.environ["NCCL_DEBUG"] = "INFO"
+os.environ["NCCL_DEBUG_SUBSYS"] = "INIT"
 _JSON_OUT = 1   # file descriptor the JSON line is written to (see the end of the file)
 
 T_CTX = 256
