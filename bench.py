@@ -175,6 +175,57 @@ def measured_peaks():
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
 
 
+def tf32_probe(n=8192, burst_iters=10, sustain_s=3.0):
+    """The tf32 tensor-core rate of this GPU, measured with a cuBLAS fp32
+    matmul that may use tf32 (n^3 products, 2n^3 flop): the best of
+    `burst_iters` single calls, and the mean over back-to-back calls for
+    `sustain_s` seconds.  A denominator only: the product never runs through
+    cuBLAS.  3xTF32 needs three tf32 passes per fp32 product, so its ceiling
+    is a third of this."""
+    import torch
+    prev = torch.get_float32_matmul_precision()
+    torch.set_float32_matmul_precision("high")
+    try:
+        a = torch.randn(n, n, device="cuda")
+        b = torch.randn(n, n, device="cuda")
+        c = torch.empty(n, n, device="cuda")
+        flop = 2.0 * n ** 3
+        for _ in range(3):
+            torch.matmul(a, b, out=c)
+        torch.cuda.synchronize()
+        best = 0.0
+        for _ in range(burst_iters):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(); torch.matmul(a, b, out=c); e1.record(); e1.synchronize()
+            best = max(best, flop / (e0.elapsed_time(e1) * 1e-3) / 1e12)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        calls, t0 = 0, time.time()
+        e0.record()
+        while time.time() - t0 < sustain_s:
+            for _ in range(8):
+                torch.matmul(a, b, out=c)
+            calls += 8
+            e1.record(); e1.synchronize()
+        sustained = flop * calls / (e0.elapsed_time(e1) * 1e-3) / 1e12
+        del a, b, c
+        torch.cuda.empty_cache()
+        return {"tf32_tflops": round(best, 1), "tf32_tflops_sustained": round(sustained, 1),
+                "how": f"torch.matmul fp32 with tf32 allowed (cuBLAS), {n}^3: best of {burst_iters} calls and "
+                       f"{calls} calls back to back ({sustain_s:g} s)"}
+    finally:
+        torch.set_float32_matmul_precision(prev)
+
+
+_TF32_PROBE = None
+
+
+def cached_tf32_probe():
+    global _TF32_PROBE
+    if _TF32_PROBE is None:
+        _TF32_PROBE = tf32_probe()
+    return _TF32_PROBE
+
+
 def gemm_ceiling(engine):
     """Divisor of the bf16 peak giving the GEMM engine's fp32-product ceiling,
     the kernel's name and the reason."""
@@ -462,6 +513,12 @@ def run_train(args, rk):
     if world > 1:
         z.close()
     torch.cuda.empty_cache()
+    if world == 1 and roofline.get("achieved"):
+        # the tf32 rate probed on this GPU after the timed region: 3xTF32's
+        # ceiling is a third of it (sustained: the step runs for seconds)
+        pr = cached_tf32_probe()
+        roofline["tf32_probe"] = pr
+        roofline["frac_of_probed_tf32"] = round(roofline["achieved"] / (pr["tf32_tflops_sustained"] / 3.0), 4)
 
     out = None
     if rank == 0:
@@ -644,6 +701,8 @@ def run_gemm(args, rk, shapes=None):
     peak = bf16 / div
     agg = tot_flop / (tot_ms * 1e-3) / 1e12
     best = max(results, key=lambda r: r["tflops"])
+    # the tf32 rate probed on this GPU (burst: the sweep's calls are short)
+    probe = cached_tf32_probe() if rk.world == 1 and args.gemm_engine in (0, 2, 3) else None
     return {"metric": GEMM_METRIC, "value": round(agg, 2), "unit": "TFLOP/s", "n_gpus": rk.world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(tot_ms / max(1, len(results)), 4),
             "higher_is_better": True, "scaling": "replicas", "vs_baseline": None, "dtype": "f32",
@@ -656,7 +715,9 @@ def run_gemm(args, rk, shapes=None):
             "roofline": {"kernel": kname, "bound": "tensor", "unit": "TFLOP/s",
                          "achieved": round(agg, 2), "best_shape": best, "peak": round(peak, 1),
                          "peak_source": f"{peak_kind} bf16 burst {bf16} TFLOP/s / {div:g} ({why})",
-                         "frac": round(agg / peak, 4) if peak else None, "traffic": None},
+                         "frac": round(agg / peak, 4) if peak else None, "traffic": None,
+                         "tf32_probe": probe,
+                         "frac_of_probed_tf32": round(agg / (probe["tf32_tflops"] / 3.0), 4) if probe else None},
             "clocks": clocks_all[-1] if clocks_all else {}, "gpu_launches": launches, "sweep": results}
 
 

@@ -450,59 +450,84 @@ __device__ __forceinline__ void rope_back_row(float (&v)[HD], const float *cs, c
 }
 
 // ------------------------------------------------------------- dQ = dS K
-// The query-side product of the backward (tinylm.c:772-777, dq += dsc * k) for
-// one (sequence, query head, query half r): M = 128 queries, N = 64, the
-// reduction over keys [0, 128(r+1)) in blocks of 32.  A = dS comes from the
-// key-side kernel's dS^T scratch ([b][h][key][query], queries contiguous, so
-// the MN-major A operand), B = K (MN-major B), both by TMA with the 32-byte
-// atom swizzle; one CTA (cta_group::1), two 48 KB stages, so two CTAs share
-// an SM.  Key blocks 0-3 accumulate in TMEM columns 0..63 and 4-7 in 64..127
-// (each sum kept short in the truncating TMEM adds), added in fp32 by the
-// epilogue.  The scratch's tiles above the diagonal are never written by the
-// key-side kernel and stay zero from the model's set-up, which covers the
-// 64-key tile above the diagonal inside each 128 x 128 block read here.
-// Roles (192 threads): warp 0 TMA producer, warp 1 TMEM owner and MMA
-// issuer, warps 2-5 lo split, then the epilogue (warp w: rows 32*(w%4)..).
+// The query-side product of the backward (tinylm.c:772-777, dq += dsc * k).
+// An item is one (sequence, query head, query half r): M = 128 queries,
+// N = 64, the reduction over keys [0, 128(r+1)) in blocks of 32.  A = dS
+// comes from the key-side kernel's dS^T scratch ([b][h][key][query], queries
+// contiguous, so the MN-major A operand), B = K (MN-major B), both by TMA
+// with the 32-byte atom swizzle.  The scratch's tiles above the diagonal are
+// never written by the key-side kernel and stay zero from the model's set-up,
+// which covers the 64-key tile above the diagonal inside each 128 x 128 block
+// read here.
+// Persistent: one CTA per SM walks items it, it + grid, ... (the halves with
+// 8 key blocks first, then those with 4), through a ring of four stages that
+// runs on across items, so the next item's loads and products overlap this
+// item's epilogue.  Key blocks 0-3 accumulate in TMEM columns 0..63 of the
+// item's buffer and 4-7 in 64..127 (each sum kept short in the truncating
+// TMEM adds), added in fp32 by the epilogue; items alternate between two
+// buffers of 128 columns.
+// Roles (320 threads): warp 0 TMA producer, warp 1 TMEM owner and MMA issuer,
+// warps 2-5 lo split of every stage, warps 6-9 the epilogue (warp w: rows
+// 32*(w%4)..).  Every wait is bounded; on expiry the CTA records an error
+// code (tl_device_status) and winds down.
 constexpr int DQ_KB = 32;
 constexpr int DQ_TILE_A = QR * DQ_KB * 4;                       // 16 KB: 4 boxes of 32 queries x 32 keys
 constexpr int DQ_TILE_B = HD * DQ_KB * 4;                       // 8 KB: 2 boxes of 32 columns x 32 keys
 constexpr int DQ_OFF_AHI = 0, DQ_OFF_ALO = DQ_TILE_A, DQ_OFF_BHI = 2 * DQ_TILE_A,
               DQ_OFF_BLO = 2 * DQ_TILE_A + DQ_TILE_B;
 constexpr int DQ_STAGE_BYTES = 2 * (DQ_TILE_A + DQ_TILE_B);     // 48 KB
-constexpr int DQ_STAGES = 2;
-constexpr int DQ_THREADS = 192;
-constexpr int DQ_SMEM_BYTES = DQ_STAGES * DQ_STAGE_BYTES + 1024 + 128;
-constexpr int DQ_TMEM_COLS = 128;
+constexpr int DQ_STAGES = 4;
+constexpr int DQ_THREADS = 320;
+constexpr int DQ_NBARS = 3 * DQ_STAGES + 5;
+constexpr int DQ_SMEM_BYTES = DQ_STAGES * DQ_STAGE_BYTES + 1024 + DQ_NBARS * 8 + 16;
+constexpr int DQ_TMEM_COLS = 256;                               // two item accumulators of 128 columns
 constexpr uint32_t DQ_IDESC = (1u << 4) | (2u << 7) | (2u << 10) | (1u << 15) | (1u << 16) |
                               ((uint32_t)(HD >> 3) << 17) | ((uint32_t)(QR >> 4) << 24);
-static_assert(2 * DQ_SMEM_BYTES <= 228 * 1024, "two dQ CTAs per SM");
+static_assert(DQ_SMEM_BYTES <= 232448, "dQ kernel exceeds the opt-in shared memory");
 
 struct DqArgs {
   float *dq;
   const float *cosT, *sinT;   // RoPE table [T][HD/2]: the inverse rotation is applied to dQ; nullptr: none
-  int H, KV, D;
+  int B, H, KV, D;
   int *err;
 };
 
-__global__ void __launch_bounds__(DQ_THREADS)
+// Item it of 2 * B * H: the halves with 8 key blocks (r = 1) first.
+struct DqItem {
+  int r, bh, b, h, kvh, nk;
+};
+__device__ __forceinline__ DqItem dq_item(const DqArgs &a, int it) {
+  DqItem d;
+  const int BH = a.B * a.H;
+  d.r = it < BH ? 1 : 0;
+  d.bh = it < BH ? it : it - BH;
+  d.b = d.bh / a.H;
+  d.h = d.bh % a.H;
+  d.kvh = d.h / (a.H / a.KV);
+  d.nk = 4 * (d.r + 1);
+  return d;
+}
+
+__global__ void __launch_bounds__(DQ_THREADS, 1)
 attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmK, DqArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + DQ_STAGES * DQ_STAGE_BYTES);
   // bars: full[S] (TMA landed), ready[S] (lo parts written), empty[S] (MMAs
-  // done with the stage), acc (every MMA done)
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * DQ_STAGES + 1);
+  // done with the stage), accf[2] (item's products in buffer b done),
+  // acce[2] (epilogue done reading buffer b), fin (every MMA done)
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + DQ_NBARS);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
   const uint32_t base = smem_u32(smem);
   auto bar_full = [&](int s) { return smem_u32(&bars[s]); };
   auto bar_ready = [&](int s) { return smem_u32(&bars[DQ_STAGES + s]); };
   auto bar_empty = [&](int s) { return smem_u32(&bars[2 * DQ_STAGES + s]); };
-  const uint32_t bar_acc = smem_u32(&bars[3 * DQ_STAGES]);
+  auto bar_accf = [&](int b) { return smem_u32(&bars[3 * DQ_STAGES + b]); };
+  auto bar_acce = [&](int b) { return smem_u32(&bars[3 * DQ_STAGES + 2 + b]); };
+  const uint32_t bar_fin = smem_u32(&bars[3 * DQ_STAGES + 4]);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int r = 1 - (int)(blockIdx.x & 1);     // the half with 8 key blocks first in launch order
-  const int bh = blockIdx.x >> 1, b = bh / a.H, h = bh % a.H, kvh = h / (a.H / a.KV);
-  const int nk = 4 * (r + 1);
+  const int nitems = 2 * a.B * a.H;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < DQ_STAGES; s++) {
@@ -510,7 +535,11 @@ attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmS, const __grid_cons
       mbar_init(bar_ready(s), 4);
       mbar_init(bar_empty(s), 1);
     }
-    mbar_init(bar_acc, 1);
+    for (int b = 0; b < 2; b++) {
+      mbar_init(bar_accf(b), 1);
+      mbar_init(bar_acce(b), 4);
+    }
+    mbar_init(bar_fin, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -528,25 +557,29 @@ attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmS, const __grid_cons
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      int issued = 0;
-      for (int kb = 0; kb < nk; kb++) {
-        const int s = kb % DQ_STAGES, u = kb / DQ_STAGES;
-        if (u > 0 && !mbar_wait(bar_empty(s), (u - 1) & 1, abort_flag, a.err, 51)) break;
-        issued = kb + 1;
-        const uint32_t st = base + s * DQ_STAGE_BYTES;
-        mbar_arrive_expect_tx(bar_full(s), DQ_TILE_A + DQ_TILE_B);
-        const int key0 = kb * DQ_KB;
+      int g = 0;
+      bool live = true;
+      for (int it = blockIdx.x; live && it < nitems; it += gridDim.x) {
+        const DqItem d = dq_item(a, it);
+        for (int kb = 0; kb < d.nk; kb++, g++) {
+          const int s = g % DQ_STAGES, u = g / DQ_STAGES;
+          if (u > 0 && !mbar_wait(bar_empty(s), (u - 1) & 1, abort_flag, a.err, 51)) { live = false; break; }
+          const uint32_t st = base + s * DQ_STAGE_BYTES;
+          mbar_arrive_expect_tx(bar_full(s), DQ_TILE_A + DQ_TILE_B);
+          const int key0 = kb * DQ_KB;
 #pragma unroll
-        for (int x = 0; x < QR / 32; x++)
-          tma_load_2d(st + DQ_OFF_AHI + x * 4096, &tmS, bar_full(s), QR * r + 32 * x, bh * T + key0);
+          for (int x = 0; x < QR / 32; x++)
+            tma_load_2d(st + DQ_OFF_AHI + x * 4096, &tmS, bar_full(s), QR * d.r + 32 * x, d.bh * T + key0);
 #pragma unroll
-        for (int x = 0; x < HD / 32; x++)
-          tma_load_2d(st + DQ_OFF_BHI + x * 4096, &tmK, bar_full(s), kvh * HD + 32 * x, b * T + key0);
+          for (int x = 0; x < HD / 32; x++)
+            tma_load_2d(st + DQ_OFF_BHI + x * 4096, &tmK, bar_full(s), d.kvh * HD + 32 * x, d.b * T + key0);
+        }
       }
-      // No copy may still be landing when the CTA exits.
-      for (int kb = issued > DQ_STAGES ? issued - DQ_STAGES : 0; kb < issued; kb++) {
+      // No copy may still be landing when the CTA exits: the last
+      // min(g, stages) issued stages.
+      for (int q = g > DQ_STAGES ? g - DQ_STAGES : 0; q < g; q++) {
         const long long t0 = clock64();
-        while (!mbar_try_wait(bar_full(kb % DQ_STAGES), (kb / DQ_STAGES) & 1)) {
+        while (!mbar_try_wait(bar_full(q % DQ_STAGES), (q / DQ_STAGES) & 1)) {
           if (clock64() - t0 > WAIT_LIMIT_CYCLES) { atomicExch(a.err, 56); break; }
         }
       }
@@ -554,88 +587,112 @@ attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmS, const __grid_cons
   } else if (warp == 1) {
     // ---------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      for (int kb = 0; kb < nk; kb++) {
-        const int s = kb % DQ_STAGES, u = kb / DQ_STAGES;
-        if (!mbar_wait(bar_ready(s), u & 1, abort_flag, a.err, 52)) break;
-        tc_fence_after();
-        const uint32_t st = base + s * DQ_STAGE_BYTES;
-        const uint32_t d = tmem + (uint32_t)((kb >> 2) * HD);
+      int g = 0, j = 0;
+      bool live = true;
+      for (int it = blockIdx.x; live && it < nitems; it += gridDim.x, j++) {
+        const DqItem d = dq_item(a, it);
+        const int b = j & 1;
+        if (j >= 2 && !mbar_wait(bar_acce(b), ((j >> 1) - 1) & 1, abort_flag, a.err, 57)) break;
+        for (int kb = 0; kb < d.nk; kb++, g++) {
+          const int s = g % DQ_STAGES, u = g / DQ_STAGES;
+          if (!mbar_wait(bar_ready(s), u & 1, abort_flag, a.err, 52)) { live = false; break; }
+          tc_fence_after();
+          const uint32_t st = base + s * DQ_STAGE_BYTES;
+          const uint32_t dt = tmem + (uint32_t)(b * 2 * HD + (kb >> 2) * HD);
 #pragma unroll
-        for (int kk = 0; kk < DQ_KB / 8; kk++) {
-          const uint32_t off = kk * 1024;        // eight key rows per MMA step
-          const uint64_t a_hi = smem_desc(st + DQ_OFF_AHI + off, 4096, 512, LAYOUT_SW128_BASE32B);
-          const uint64_t a_lo = smem_desc(st + DQ_OFF_ALO + off, 4096, 512, LAYOUT_SW128_BASE32B);
-          const uint64_t b_hi = smem_desc(st + DQ_OFF_BHI + off, 4096, 512, LAYOUT_SW128_BASE32B);
-          const uint64_t b_lo = smem_desc(st + DQ_OFF_BLO + off, 4096, 512, LAYOUT_SW128_BASE32B);
-          tc_mma(d, a_lo, b_hi, DQ_IDESC, ((kb & 3) > 0 || kk > 0) ? 1u : 0u);
-          tc_mma(d, a_hi, b_lo, DQ_IDESC, 1);
-          tc_mma(d, a_hi, b_hi, DQ_IDESC, 1);
+          for (int kk = 0; kk < DQ_KB / 8; kk++) {
+            const uint32_t off = kk * 1024;        // eight key rows per MMA step
+            const uint64_t a_hi = smem_desc(st + DQ_OFF_AHI + off, 4096, 512, LAYOUT_SW128_BASE32B);
+            const uint64_t a_lo = smem_desc(st + DQ_OFF_ALO + off, 4096, 512, LAYOUT_SW128_BASE32B);
+            const uint64_t b_hi = smem_desc(st + DQ_OFF_BHI + off, 4096, 512, LAYOUT_SW128_BASE32B);
+            const uint64_t b_lo = smem_desc(st + DQ_OFF_BLO + off, 4096, 512, LAYOUT_SW128_BASE32B);
+            tc_mma(dt, a_lo, b_hi, DQ_IDESC, ((kb & 3) > 0 || kk > 0) ? 1u : 0u);
+            tc_mma(dt, a_hi, b_lo, DQ_IDESC, 1);
+            tc_mma(dt, a_hi, b_hi, DQ_IDESC, 1);
+          }
+          tc_commit(bar_empty(s));
         }
-        tc_commit(bar_empty(s));
+        if (!live) break;
+        tc_commit(bar_accf(b));
       }
-      // Every issued MMA finished (also on the abort path) before the
-      // epilogue reads TMEM and before it is released.
-      tc_commit(bar_acc);
+      // Every issued MMA finished (also on the abort path) before TMEM is
+      // released and the CTA exits.
+      tc_commit(bar_fin);
       const long long t0 = clock64();
-      while (!mbar_try_wait(bar_acc, 0)) {
+      while (!mbar_try_wait(bar_fin, 0)) {
         if (clock64() - t0 > WAIT_LIMIT_CYCLES) { *abort_flag = 1; atomicExch(a.err, 55); break; }
       }
     }
-  } else {
-    // -------------------------------------- lo split, then the epilogue
+  } else if (warp < 6) {
+    // ------------------------------------------------- lo split (warps 2-5)
     const int t = threadIdx.x - 64;            // 0..127
-    bool ok = true;
-    if (a.cosT) {
-      // the epilogue's RoPE table rows (128 bytes each) into L1 meanwhile
-      const size_t trow = (size_t)(QR * r + (warp & 3) * 32 + lane) * (HD / 2);
-      asm volatile("prefetch.global.L1 [%0];" ::"l"(a.cosT + trow));
-      asm volatile("prefetch.global.L1 [%0];" ::"l"(a.sinT + trow));
-    }
-    for (int kb = 0; kb < nk; kb++) {
-      const int s = kb % DQ_STAGES, u = kb / DQ_STAGES;
-      if (!mbar_wait(bar_full(s), u & 1, abort_flag, a.err, 53)) { ok = false; break; }
-      uint8_t *st = smem + s * DQ_STAGE_BYTES;
-      // A then B: 1024 + 512 float4 of raw data, 12 per thread; lo lands at
-      // the same offset of the lo tile (same swizzled layout).
+    int g = 0;
+    bool live = true;
+    for (int it = blockIdx.x; live && it < nitems; it += gridDim.x) {
+      const int nk = 4 * ((it < a.B * a.H ? 1 : 0) + 1);
+      for (int kb = 0; kb < nk; kb++, g++) {
+        const int s = g % DQ_STAGES, u = g / DQ_STAGES;
+        const bool landed = mbar_wait(bar_full(s), u & 1, abort_flag, a.err, 53);
+        if (!__all_sync(0xffffffffu, landed)) { live = false; break; }
+        uint8_t *st = smem + s * DQ_STAGE_BYTES;
+        // A then B: 1024 + 512 float4 of raw data, 12 per thread; lo lands at
+        // the same offset of the lo tile (same swizzled layout).
 #pragma unroll 4
-      for (int e = 0; e < 12; e++) {
-        const int idx = e * 128 + t;
-        const int off = idx < 1024 ? DQ_OFF_AHI + idx * 16 : DQ_OFF_BHI + (idx - 1024) * 16;
-        const int lo_off = off + (idx < 1024 ? DQ_TILE_A : DQ_TILE_B);
-        const float4 x = *reinterpret_cast<const float4 *>(st + off);
-        float4 lo;
-        lo.x = x.x - tf32_trunc(x.x); lo.y = x.y - tf32_trunc(x.y);
-        lo.z = x.z - tf32_trunc(x.z); lo.w = x.w - tf32_trunc(x.w);
-        *reinterpret_cast<float4 *>(st + lo_off) = lo;
+        for (int e = 0; e < 12; e++) {
+          const int idx = e * 128 + t;
+          const int off = idx < 1024 ? DQ_OFF_AHI + idx * 16 : DQ_OFF_BHI + (idx - 1024) * 16;
+          const int lo_off = off + (idx < 1024 ? DQ_TILE_A : DQ_TILE_B);
+          const float4 x = *reinterpret_cast<const float4 *>(st + off);
+          float4 lo;
+          lo.x = x.x - tf32_trunc(x.x); lo.y = x.y - tf32_trunc(x.y);
+          lo.z = x.z - tf32_trunc(x.z); lo.w = x.w - tf32_trunc(x.w);
+          *reinterpret_cast<float4 *>(st + lo_off) = lo;
+        }
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_ready(s));
       }
-      fence_proxy_async();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar_ready(s));
     }
-    const bool landed = ok && mbar_wait(bar_acc, 0, abort_flag, a.err, 54);
-    if (__all_sync(0xffffffffu, landed) && !*abort_flag) {
+  } else {
+    // ------------------------------------------------- epilogue (warps 6-9)
+    const int q4 = warp & 3, row = q4 * 32 + lane;
+    const uint32_t lane_addr = (uint32_t)(q4 * 32) << 16;
+    int j = 0;
+    for (int it = blockIdx.x; it < nitems; it += gridDim.x, j++) {
+      const DqItem d = dq_item(a, it);
+      const int b = j & 1;
+      const bool landed = mbar_wait(bar_accf(b), (j >> 1) & 1, abort_flag, a.err, 54);
+      if (!__all_sync(0xffffffffu, landed) || *abort_flag) break;
+      const int qpos = QR * d.r + row;
+      if (a.cosT) {
+        // this row's RoPE table entries into L1 while TMEM is read
+        asm volatile("prefetch.global.L1 [%0];" ::"l"(a.cosT + (size_t)qpos * (HD / 2)));
+        asm volatile("prefetch.global.L1 [%0];" ::"l"(a.sinT + (size_t)qpos * (HD / 2)));
+      }
       tc_fence_after();
-      const int q4 = warp & 3, row = q4 * 32 + lane;
-      const uint32_t lane_addr = (uint32_t)(q4 * 32) << 16;
-      const int qpos = QR * r + row;
-      float *dst = a.dq + ((size_t)b * T + qpos) * a.D + (size_t)h * HD;
       float o[HD];
+      const uint32_t tb = tmem + lane_addr + (uint32_t)(b * 2 * HD);
 #pragma unroll
       for (int cc = 0; cc < HD / 32; cc++) {
         uint32_t v0[32];
-        tmem_ld32(tmem + lane_addr + cc * 32, v0);
+        tmem_ld32(tb + cc * 32, v0);
 #pragma unroll
         for (int e = 0; e < 32; e++) o[32 * cc + e] = __uint_as_float(v0[e]);
-        if (r == 1) {
+        if (d.r == 1) {
           uint32_t v1[32];
-          tmem_ld32(tmem + lane_addr + HD + cc * 32, v1);
+          tmem_ld32(tb + HD + cc * 32, v1);
 #pragma unroll
           for (int e = 0; e < 32; e++) o[32 * cc + e] += __uint_as_float(v1[e]);
         }
       }
+      // The buffer is free for the item after next as soon as it is read.
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_acce(b));
       // The gradient through RoPE (tinylm.c:1132-1133): the transposed
       // rotation of each (i, i + HD/2) pair at this query's position.
       if (a.cosT) rope_back_row(o, a.cosT + (size_t)qpos * (HD / 2), a.sinT + (size_t)qpos * (HD / 2));
+      float *dst = a.dq + ((size_t)d.b * T + qpos) * a.D + (size_t)d.h * HD;
 #pragma unroll
       for (int e = 0; e < HD; e += 4)
         *reinterpret_cast<float4 *>(dst + e) = make_float4(o[e], o[e + 1], o[e + 2], o[e + 3]);
@@ -1151,9 +1208,11 @@ int attn_bwd_dq_tc(DeviceCtx *c, const float *dsT, const float *k, float *dq, in
     return rc;
   if ((rc = atc::map2d(&mk, k, KD, (uint64_t)B * atc::T, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))) return rc;
   atc::DqArgs a;
-  a.dq = dq; a.cosT = cosT; a.sinT = sinT; a.H = H; a.KV = KV; a.D = H * atc::HD; a.err = c->err_flag;
+  a.dq = dq; a.cosT = cosT; a.sinT = sinT; a.B = B; a.H = H; a.KV = KV; a.D = H * atc::HD; a.err = c->err_flag;
+  // persistent: one CTA per SM (or per item, when there are fewer)
+  const int grid = std::min(2 * B * H, std::max(1, c->num_sms));
   TraceScope ts(c, "k_attn_bwd_dq_tc");
-  atc::attn_bwd_dq_tc_kernel<<<2 * B * H, atc::DQ_THREADS, atc::DQ_SMEM_BYTES, c->stream>>>(ms, mk, a);
+  atc::attn_bwd_dq_tc_kernel<<<grid, atc::DQ_THREADS, atc::DQ_SMEM_BYTES, c->stream>>>(ms, mk, a);
   TL_TRY_CUDA(cudaGetLastError());
   return TL_OK;
 }
