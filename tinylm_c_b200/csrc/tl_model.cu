@@ -42,6 +42,7 @@ struct Model {
   float *dact, *dgb, *du, *dout, *dfnorm, *dfin, *datt, *dq, *dnorm, *dain, *dfn, *dk, *dv, *Drow, *dsT;
   float *t1, *hk, *dhk, *dt1;
   float *rms_part, *rms_tmp;   // gain-gradient partial rows and their middle level
+  float *emb_idx;              // embedding backward: token positions by vocabulary row (ints)
   double *loss_rows, *loss_acc;
   // CUDA graph of one whole training step (tl_model_graph_step): the buffers
   // it was captured with, and the per-step scalars it reads on the device
@@ -197,7 +198,7 @@ static int micro_step(DeviceCtx *c, Model &m, const float *P, float *G, const in
     std::swap(m.dout, m.dain);
     if (ov) TRY(overlap_ready(c, ov, m.o_an1[l]));       // layers l..L-1 are done
   }
-  TRY(k_embed_bwd(c, gemb, tok, m.dout, N, D, V));
+  TRY(k_embed_bwd(c, gemb, tok, m.dout, N, D, V, reinterpret_cast<int *>(m.emb_idx)));
   return TL_OK;
 }
 
@@ -257,6 +258,7 @@ static int alloc_model(Model &m) {
   slots.push_back({&m.dsT, take(att_rows * m.T)});
   slots.push_back({&m.rms_part, take((size_t)RMS_PART_ROWS * D)});
   slots.push_back({&m.rms_tmp, take(8 * D)});
+  slots.push_back({&m.emb_idx, take(3 * (size_t)V + 2 * (size_t)N)});
   const size_t o_loss = take(2 * N + 2);  // doubles: N rows + accumulator
   TL_TRY_CUDA(cudaMalloc(&m.arena, floats * sizeof(float)));
   float *base = static_cast<float *>(m.arena);

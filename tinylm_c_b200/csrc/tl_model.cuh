@@ -9,7 +9,8 @@ constexpr int ATT_HDMAX = 64;
 
 int mk_setup(int device);
 int k_embed_fwd(DeviceCtx *c, const float *emb, const int *tok, float *out, int N, int D, int V);
-int k_embed_bwd(DeviceCtx *c, float *gemb, const int *tok, const float *dout, int N, int D, int V);
+// scratch: 3 * V + 2 * N ints (nullptr: the token-scanning kernel)
+int k_embed_bwd(DeviceCtx *c, float *gemb, const int *tok, const float *dout, int N, int D, int V, int *scratch);
 int k_rmsnorm_fwd(DeviceCtx *c, const float *x, const float *g, float *out, float *rinv, int rows, int D);
 // dx = dres + RMSNorm backward of dy (dres: nullptr, dx itself, or another
 // array); dg += the gain gradient (fixed-order reduction of per-block partial

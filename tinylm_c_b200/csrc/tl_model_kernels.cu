@@ -101,6 +101,105 @@ embed_bwd_kernel(float *__restrict__ gemb, const int *__restrict__ tok, const fl
   }
 }
 
+// The same sums without scanning every token per vocabulary row: the
+// positions of each row's tokens are gathered first.  cnt[v] counts the
+// tokens equal to v (atomic counts: order-free), off[v] is their exclusive
+// prefix sum, cur[v] a cursor from off[v] that places each position into
+// list (in any order), and each bucket is then written to sorted in
+// increasing position order (a position's rank is the number of smaller
+// ones in its bucket; positions are distinct).  The sum over a row then runs
+// over its bucket in that order: the same bits as embed_bwd_kernel.
+__global__ void emb_count_kernel(const int *__restrict__ tok, int N, int V, int *__restrict__ cnt) {
+  for (int n = blockIdx.x * blockDim.x + threadIdx.x; n < N; n += gridDim.x * blockDim.x) {
+    const int t = tok[n];
+    if (t >= 0 && t < V) atomicAdd(cnt + t, 1);
+  }
+}
+
+// One block of 1024 threads: each takes a contiguous run of entries.
+__global__ void __launch_bounds__(1024)
+emb_scan_kernel(const int *__restrict__ cnt, int V, int *__restrict__ off, int *__restrict__ cur) {
+  __shared__ int wsum[32];
+  const int per = (V + 1023) / 1024, v0 = threadIdx.x * per, v1 = min(V, v0 + per);
+  int s = 0;
+  for (int v = v0; v < v1; v++) s += cnt[v];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  int x = s;                                 // inclusive scan over the warp
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) wsum[w] = x;
+  __syncthreads();
+  if (w == 0) {
+    int y = wsum[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int z = __shfl_up_sync(0xffffffffu, y, o);
+      if (lane >= o) y += z;
+    }
+    wsum[lane] = y;                          // inclusive over warps
+  }
+  __syncthreads();
+  int run = x - s + (w > 0 ? wsum[w - 1] : 0);   // exclusive start of this thread's run
+  for (int v = v0; v < v1; v++) {
+    off[v] = run;
+    cur[v] = run;
+    run += cnt[v];
+  }
+}
+
+__global__ void emb_place_kernel(const int *__restrict__ tok, int N, int V, int *__restrict__ cur,
+                                 int *__restrict__ list) {
+  for (int n = blockIdx.x * blockDim.x + threadIdx.x; n < N; n += gridDim.x * blockDim.x) {
+    const int t = tok[n];
+    if (t >= 0 && t < V) list[atomicAdd(cur + t, 1)] = n;
+  }
+}
+
+__global__ void __launch_bounds__(256)
+embed_bwd_sorted_kernel(float *__restrict__ gemb, const float *__restrict__ dout, const int *__restrict__ cnt,
+                        const int *__restrict__ off, const int *__restrict__ list, int *__restrict__ sorted, int D,
+                        int V) {
+  const int lane = threadIdx.x & 31;
+  const int nwarps = (gridDim.x * blockDim.x) >> 5;
+  for (int v = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; v < V; v += nwarps) {
+    const int c = cnt[v];
+    if (c == 0) continue;
+    const int o = off[v];
+    for (int i = lane; i < c; i += 32) {
+      const int x = list[o + i];
+      int r = 0;
+      for (int j = 0; j < c; j++) r += list[o + j] < x ? 1 : 0;
+      sorted[o + r] = x;
+    }
+    __syncwarp();
+    float *row = gemb + (size_t)v * D;
+    for (int c0 = 0; c0 < D; c0 += 32 * EMB_CHUNK) {
+      float acc[EMB_CHUNK];
+#pragma unroll
+      for (int e = 0; e < EMB_CHUNK; e++) {
+        const int d = c0 + e * 32 + lane;
+        acc[e] = d < D ? row[d] : 0.0f;
+      }
+      for (int i = 0; i < c; i++) {
+        const float *src = dout + (size_t)sorted[o + i] * D;
+#pragma unroll
+        for (int e = 0; e < EMB_CHUNK; e++) {
+          const int d = c0 + e * 32 + lane;
+          if (d < D) acc[e] += src[d];
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < EMB_CHUNK; e++) {
+        const int d = c0 + e * 32 + lane;
+        if (d < D) row[d] = acc[e];
+      }
+    }
+  }
+}
+
 // ---------------------------------------------------------------- RMSNorm
 // out = x * s * g, s = 1/sqrt(mean(x^2) + 1e-5); one warp per row.  (539-566)
 __global__ void rmsnorm_fwd_kernel(const float *__restrict__ x, const float *__restrict__ g,
@@ -458,6 +557,66 @@ __global__ void softmax_ce_kernel(float *__restrict__ logits, const int *__restr
   for (int i = threadIdx.x; i < V; i += blockDim.x) l[i] = l[i] * inv * scale;
   __syncthreads();
   if (threadIdx.x == 0 && t >= 0 && t < V) l[t] -= scale;
+}
+
+// The same row operation with the row held in registers: NV4 float4 per
+// thread, V = 1024 * NV4, so the row is read once and written once.  Per
+// element the arithmetic is the kernel above's; the sums run over a fixed
+// partition (thread, then warp, then the block's warps in order), so the
+// result is deterministic.
+template <int NV4>
+__global__ void __launch_bounds__(256)
+softmax_ce_reg_kernel(float *__restrict__ logits, const int *__restrict__ tgt, float scale,
+                      double *__restrict__ loss_rows) {
+  constexpr int V = 1024 * NV4;
+  __shared__ float red[8];
+  const int n = blockIdx.x, lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  float4 *l4 = reinterpret_cast<float4 *>(logits + (size_t)n * V);
+  float4 x[NV4];
+  float mx = -1e30f;
+#pragma unroll
+  for (int k = 0; k < NV4; k++) {
+    x[k] = l4[threadIdx.x + 256 * k];
+    mx = fmaxf(mx, fmaxf(fmaxf(x[k].x, x[k].y), fmaxf(x[k].z, x[k].w)));
+  }
+  mx = warp_max_f(mx);
+  if (lane == 0) red[w] = mx;
+  __syncthreads();
+  mx = red[0];
+#pragma unroll
+  for (int i = 1; i < 8; i++) mx = fmaxf(mx, red[i]);
+  float sum = 0.0f;
+#pragma unroll
+  for (int k = 0; k < NV4; k++) {
+    x[k].x = expf(x[k].x - mx); x[k].y = expf(x[k].y - mx);
+    x[k].z = expf(x[k].z - mx); x[k].w = expf(x[k].w - mx);
+    sum += x[k].x; sum += x[k].y; sum += x[k].z; sum += x[k].w;
+  }
+  sum = warp_sum_f(sum);
+  __syncthreads();                       // every thread has read red[] as maxima
+  if (lane == 0) red[w] = sum;
+  __syncthreads();
+  float tot = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; i++) tot += red[i];
+  const float inv = 1.0f / tot;
+  const int t = tgt[n];
+  const int tq = (t >= 0 && t < V) ? t >> 2 : -1;    // the float4 holding the target
+#pragma unroll
+  for (int k = 0; k < NV4; k++) {
+    const int q = threadIdx.x + 256 * k;
+    float4 o;
+    o.x = x[k].x * inv * scale; o.y = x[k].y * inv * scale;
+    o.z = x[k].z * inv * scale; o.w = x[k].w * inv * scale;
+    if (q == tq) {
+      const int c = t & 3;
+      const float e = c == 0 ? x[k].x : c == 1 ? x[k].y : c == 2 ? x[k].z : x[k].w;
+      if (loss_rows) loss_rows[n] = -log((double)(e * inv) + 1e-12);
+      if (c == 0) o.x -= scale; else if (c == 1) o.y -= scale; else if (c == 2) o.z -= scale; else o.w -= scale;
+    }
+    l4[q] = o;
+  }
+  if (loss_rows && threadIdx.x == 0 && tq < 0) loss_rows[n] = -log(1e-12);
 }
 
 // acc[0] += sum(loss_rows[0..N)) in index order (one block).
@@ -847,9 +1006,22 @@ int k_embed_fwd(DeviceCtx *c, const float *emb, const int *tok, float *out, int 
   MK_LAUNCH_CHECK();
   return TL_OK;
 }
-int k_embed_bwd(DeviceCtx *c, float *gemb, const int *tok, const float *dout, int N, int D, int V) {
+int k_embed_bwd(DeviceCtx *c, float *gemb, const int *tok, const float *dout, int N, int D, int V, int *scratch) {
   TraceScope ts(c, "k_embed_bwd");
-  mk::embed_bwd_kernel<<<(unsigned)((V + 7) / 8), 256, 0, c->stream>>>(gemb, tok, dout, N, D, V);
+  if (!scratch) {
+    mk::embed_bwd_kernel<<<(unsigned)((V + 7) / 8), 256, 0, c->stream>>>(gemb, tok, dout, N, D, V);
+    MK_LAUNCH_CHECK();
+    return TL_OK;
+  }
+  // scratch: cnt[V], off[V], cur[V], list[N], sorted[N]
+  int *cnt = scratch, *off = cnt + V, *cur = off + V, *list = cur + V, *sorted = list + N;
+  const unsigned g = (unsigned)std::min((N + 255) / 256, 4 * c->num_sms);
+  TL_TRY_CUDA(cudaMemsetAsync(cnt, 0, sizeof(int) * V, c->stream));
+  mk::emb_count_kernel<<<g, 256, 0, c->stream>>>(tok, N, V, cnt);
+  mk::emb_scan_kernel<<<1, 1024, 0, c->stream>>>(cnt, V, off, cur);
+  mk::emb_place_kernel<<<g, 256, 0, c->stream>>>(tok, N, V, cur, list);
+  mk::embed_bwd_sorted_kernel<<<(unsigned)((V + 7) / 8), 256, 0, c->stream>>>(gemb, dout, cnt, off, list, sorted,
+                                                                               D, V);
   MK_LAUNCH_CHECK();
   return TL_OK;
 }
@@ -941,7 +1113,15 @@ int k_mtp_bwd(DeviceCtx *c, const float *t1, const float *dhk, float *dfn, float
 }
 int k_softmax_ce(DeviceCtx *c, float *logits, const int *tgt, int N, int V, float scale, double *loss_rows) {
   TraceScope ts(c, "k_softmax_ce");
-  mk::softmax_ce_kernel<<<N, 256, 0, c->stream>>>(logits, tgt, V, scale, loss_rows);
+  const bool al = (reinterpret_cast<uintptr_t>(logits) & 15) == 0;
+  if (al && V == 8192)
+    mk::softmax_ce_reg_kernel<8><<<N, 256, 0, c->stream>>>(logits, tgt, scale, loss_rows);
+  else if (al && V == 4096)
+    mk::softmax_ce_reg_kernel<4><<<N, 256, 0, c->stream>>>(logits, tgt, scale, loss_rows);
+  else if (al && V == 2048)
+    mk::softmax_ce_reg_kernel<2><<<N, 256, 0, c->stream>>>(logits, tgt, scale, loss_rows);
+  else
+    mk::softmax_ce_kernel<<<N, 256, 0, c->stream>>>(logits, tgt, V, scale, loss_rows);
   MK_LAUNCH_CHECK();
   return TL_OK;
 }
