@@ -84,9 +84,9 @@ def parse():
                     help="train workloads at N=1: launch the step eagerly instead of replaying a CUDA graph")
     ap.add_argument("--no-overlap", action="store_true",
                     help="N>1, nccl exchange: reduce-scatter after the backward instead of per-shard reductions during it")
-    ap.add_argument("--gemm-engine", type=int, default=0, choices=[0, 1, 2, 3, 4],
+    ap.add_argument("--gemm-engine", type=int, default=0, choices=[0, 1, 2, 3, 4, 5],
                     help="GEMM engine: 0 automatic, 1 CUDA-core, 2 tensor-core one CTA, 3 tensor-core CTA pair, "
-                         "4 CTA pair with the fp16 split")
+                         "4 CTA pair with the fp16 split, 5 CTA pair with the hybrid split")
     return ap.parse_args()
 
 
@@ -226,11 +226,15 @@ def cached_tf32_probe():
     return _TF32_PROBE
 
 
-def gemm_ceiling(engine):
+def gemm_ceiling(engine, training=False):
     """Divisor of the bf16 peak giving the GEMM engine's fp32-product ceiling,
-    the kernel's name and the reason."""
+    the kernel's name and the reason.  `training`: the GEMMs of the device
+    training step, which the automatic choice runs with the hybrid split."""
     if engine == 4:
         return 3.0, "gemm_tc (tcgen05 fp16 split)", "3 fp16 MMAs per fp32 product, fp16 = bf16 rate"
+    if engine == 5 or (engine == 0 and training):
+        return 4.0, "gemm_tc (tcgen05 hybrid split: tf32 hi*hi + bf16 cross terms)", \
+            "one tf32 MMA (bf16/2 rate) + one bf16 MMA over twice the K per fp32 product"
     return 6.0, "gemm_tc (tcgen05 3xTF32)", "tf32 = bf16/2; 3 tf32 MMAs per fp32 product"
 
 
@@ -488,12 +492,14 @@ def run_train(args, rk):
     flops_rank = gflop_tok * N
     achieved = flops_rank / (gemm["ms_per_step"] * 1e-3) / 1e12 if gemm["ms_per_step"] else None
     bf16 = peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops"))
-    div, kname, why = gemm_ceiling(args.gemm_engine)
+    div, kname, why = gemm_ceiling(args.gemm_engine, training=True)
     peak = bf16 / div
     roofline = {"kernel": kname, "bound": "tensor", "unit": "TFLOP/s",
                 "achieved": round(achieved, 2) if achieved else None, "peak": round(peak, 1),
                 "peak_source": f"{peak_kind} bf16 sustained {bf16} TFLOP/s / {div:g} ({why})",
                 "frac": round(achieved / peak, 4) if achieved else None,
+                # against the ceiling of the 3xTF32 algorithm (bf16 sustained / 6)
+                "frac_of_3xtf32_ceiling": round(achieved * 6.0 / bf16, 4) if achieved else None,
                 "traffic": None, "algorithmic_flops_per_step": flops_rank,
                 "gemm_share_of_step": round(gemm["ms_per_step"] / (eager_ms or ms_step), 4) if ms_step else None}
     tr = committed_traffic(f"{args.workload}:gemm_tc")
@@ -515,7 +521,8 @@ def run_train(args, rk):
     torch.cuda.empty_cache()
     if world == 1 and roofline.get("achieved"):
         # the tf32 rate probed on this GPU after the timed region: 3xTF32's
-        # ceiling is a third of it (sustained: the step runs for seconds)
+        # ceiling is a third of it (sustained: the step runs for seconds), the
+        # mark the hybrid split is measured against too
         pr = cached_tf32_probe()
         roofline["tf32_probe"] = pr
         roofline["frac_of_probed_tf32"] = round(roofline["achieved"] / (pr["tf32_tflops_sustained"] / 3.0), 4)

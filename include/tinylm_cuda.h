@@ -116,17 +116,21 @@ int tl_matmul_at(float *dW, const float *X, const float *dY, int M, int K, int N
 int tl_matmul_bt_sum(float *dX, int nprod, const float *const *dY, const float *const *W, const int *N, int M,
                      int K);
 
-/* GEMM engine selection, for tests and benchmarks: 0 = automatic (tensor-core
- * 3xTF32 where the shape allows, else CUDA-core fp32), 1 = CUDA-core fp32 only,
- * 2 = tensor-core 3xTF32, one CTA per 128 x 128 tile, 3 = tensor-core 3xTF32,
- * a CTA pair (two SMs, cta_group::2) per 256 x 256 tile, 4 = the CTA pair with
- * each operand scaled by a power of two and split into fp16 hi + lo (fp16
- * MMAs at twice the tf32 rate, at least the same accuracy) (2-4: TL_EINVAL
- * where the shape does not allow the tensor-core engine).
+/* GEMM engine selection, for tests and benchmarks: 0 = automatic (tensor
+ * cores where the shape allows, else CUDA-core fp32; the CTA pair uses the
+ * tf32 split for these calls and the hybrid split for the GEMMs of the device
+ * training step, tl_model_*), 1 = CUDA-core fp32 only, 2 = tensor-core 3xTF32,
+ * one CTA per 128 x 128 tile, 3 = tensor-core 3xTF32, a CTA pair (two SMs,
+ * cta_group::2) per 256 x 256 tile, 4 = the CTA pair with each operand scaled
+ * by a power of two and split into fp16 hi + lo (fp16 MMAs at twice the tf32
+ * rate, at least the same accuracy), 5 = the CTA pair with the hybrid split:
+ * one tf32 MMA for hi*hi and the two cross terms as one bf16 chain over
+ * [hi | lo] x [lo | hi] (no scaling; within the same 1e-4 bound)
+ * (2-5: TL_EINVAL where the shape does not allow the tensor-core engine).
  * No counterpart in the reference (its only engine switch is USE_BLAS,
  * tinylm.c:29-31). */
 int tl_set_gemm_engine(int engine);
-/* Engine the last GEMM call on this thread ran on (1 to 4), 0 if none. */
+/* Engine the last GEMM call on this thread ran on (1 to 5), 0 if none. */
 int tl_last_gemm_engine(void);
 
 /* -------------------------------------------------------------- optimizer */

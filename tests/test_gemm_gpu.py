@@ -98,7 +98,7 @@ def test_gemm_rejects_host_memory(cuda):
         ops.mm(torch.zeros(4, device=cuda), X.ctypes.data, X.ctypes.data, 2, 2, 2)
 
 
-TC_ENGINES = {"tc_1cta": 2, "tc_pair": 3, "tc_pair_f16": 4}
+TC_ENGINES = {"tc_1cta": 2, "tc_pair": 3, "tc_pair_f16": 4, "tc_pair_hyb": 5}
 
 
 @pytest.mark.parametrize("tc_engine", list(TC_ENGINES))
@@ -139,7 +139,7 @@ def test_tensor_core_engine_forced(cuda, tc_engine, M, K, N):
     assert gemm_rel(dW.cpu().numpy(), dW64) <= GEMM_REL_TOL
 
 
-@pytest.mark.parametrize("eng", [0, 1, 3, 4])
+@pytest.mark.parametrize("eng", [0, 1, 3, 4, 5])
 @pytest.mark.parametrize("M,K,Ns", [(512, 384, (96, 40, 72)), (300, 260, (256, 512)), (256, 256, (2048, 1024, 1024)),
                                     (100, 64, (64, 64, 64)), (384, 256, (64, 0, 32)), (257, 1024, (2816,))])
 def test_mm_bt_sum(cuda, eng, M, K, Ns):
@@ -160,20 +160,22 @@ def test_mm_bt_sum(cuda, eng, M, K, Ns):
         device_ok()
     finally:
         ops.set_gemm_engine(0)
-    if eng in (3, 4):
+    if eng in (3, 4, 5):
         assert last == eng
     elif eng == 0 and M > 128 and K > 128:
-        assert last in (3, 4)
+        assert last == 3
     want = np.zeros((M, K))
     for a, w, n in zip(dYs, Ws, Ns):
         want += a.astype(np.float64).reshape(M, n) @ w.astype(np.float64).reshape(K, n).T
     assert gemm_rel(dX.cpu().numpy(), want.ravel()) <= GEMM_REL_TOL
 
 
+@pytest.mark.parametrize("eng", [4, 5])
 @pytest.mark.parametrize("sa,sb", [(1e5, 1e-7), (1e-20, 1e15), (3e4, 3e4), (0.0, 1.0)])
-def test_f16_split_operand_scales(cuda, sa, sb):
-    """The fp16-split pair kernel scales each operand by a power of two from
-    its max |x|: operands far outside fp16's range, tiny ones, a product
+def test_f16_split_operand_scales(cuda, eng, sa, sb):
+    """The fp16-split pair kernel (engine 4) scales each operand by a power of
+    two from its max |x|; the hybrid split (engine 5) keeps fp32's exponent
+    range in bf16.  Operands far outside fp16's range, tiny ones, a product
     whose scales differ by 2^90, and an all-zero operand keep the 1e-4
     bound, on all three primitives and on a summed mm_bt whose products have
     different magnitudes."""
@@ -187,7 +189,7 @@ def test_f16_split_operand_scales(cuda, sa, sb):
     W2 = (rng.standard_normal(K * 64) * sa).astype(np.float32)
     dY2 = (rng.standard_normal(M * 64)).astype(np.float32)
     dXs = torch.full((M * K,), float("nan"), device=cuda)
-    ops.set_gemm_engine(4)
+    ops.set_gemm_engine(eng)
     try:
         ops.mm(Y, dev(X, cuda), dev(W, cuda), M, K, N)
         ops.mm_bt(dX, dev(dY, cuda), dev(W, cuda), M, K, N)
@@ -212,7 +214,7 @@ def test_f16_split_operand_scales(cuda, sa, sb):
             assert gemm_rel(g, want) <= GEMM_REL_TOL
 
 
-@pytest.mark.parametrize("eng", [0, 4])
+@pytest.mark.parametrize("eng", [0, 4, 5])
 @pytest.mark.parametrize("M,K,Ns,accumulate", [(16384, 1024, (1024, 256, 256), False), (16384, 1024, (2816, 2816), False),
                                                (16384, 1024, (1024,), True), (65536, 256, (256,), True),
                                                (16128, 1000, (512,), False)])

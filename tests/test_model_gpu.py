@@ -305,7 +305,9 @@ def test_graph_step_matches_eager_step(cuda):
 def test_scaled_config_one_step(cuda):
     """BASELINE config 5 shape (188.8 M parameters) runs one step at batch 1:
     initial loss near ln(8192) + var(logits)/2 (logit std ~ 0.02*sqrt(1024)),
-    finite gradient norm."""
+    finite gradient norm.  Under the automatic engine choice the step's pair
+    GEMMs use the hybrid split (engine 5) and a direct call afterwards the
+    tf32 split (engine 3)."""
     c = model.cfg8("scaled", 0)
     m = model.Model(c, 1, 0)
     P = model.init_params(c, 0).to(cuda)
@@ -317,12 +319,19 @@ def test_scaled_config_one_step(cuda):
     tgt = torch.randint(0, 8192, (256,), generator=g, device=cuda, dtype=torch.int32)
     loss = torch.zeros(1, device=cuda)
     norm = torch.zeros(1, device=cuda)
+    ops.set_gemm_engine(0)
     m.step(P, G, M, V, tok, tgt, None, 1, 3e-4, 1, 1.0, loss, norm)
     torch.cuda.synchronize()
     _lib.check(_lib.lib().tl_device_status())
+    assert ops.last_gemm_engine() == 5
     m.close()
     assert 9.0 < loss.item() < 9.6
     assert np.isfinite(norm.item()) and norm.item() > 0
+    X = torch.randn(512 * 512, device=cuda)
+    Y = torch.empty(512 * 512, device=cuda)
+    ops.mm(Y, X, X, 512, 512, 512)
+    torch.cuda.synchronize()
+    assert ops.last_gemm_engine() == 3
 
 
 def test_bad_tokens_are_reported(cuda):

@@ -4,11 +4,27 @@
 namespace tl {
 
 // 0 auto, 1 CUDA-core, 2 tensor-core, 3 tensor-core pair (tf32 split),
-// 4 tensor-core pair (fp16 split)
+// 4 tensor-core pair (fp16 split), 5 tensor-core pair (hybrid split)
 static thread_local int g_engine_pref = 0;
-// The split the automatic choice gives the pair kernel.
-static constexpr bool kAutoF16 = false;
 static thread_local int g_engine_last = 0;
+static thread_local int g_sustained = 0;   // open gemm_sustained_scope()s
+
+void gemm_sustained_scope(bool enter) { g_sustained += enter ? 1 : -1; }
+
+// The split the pair kernel gets: the forced engine's, else the hybrid inside
+// a sustained scope and the tf32 split outside one.  In single calls at full
+// clock the tf32 split is the faster (config-3 shapes); over a training step
+// under the power cap the hybrid's bf16 MMAs draw less power and the step
+// runs at a higher clock (config 5: 816.5 against 854.4 ms on one box).
+static GemmSplit pair_split() {
+  if (g_engine_pref == 4) return GemmSplit::F16;
+  if (g_engine_pref == 5) return GemmSplit::HYB;
+  if (g_engine_pref == 3) return GemmSplit::TF32;
+  return g_sustained > 0 ? GemmSplit::HYB : GemmSplit::TF32;
+}
+static int engine_id(bool pair, GemmSplit split) {
+  return !pair ? 2 : split == GemmSplit::F16 ? 4 : split == GemmSplit::HYB ? 5 : 3;
+}
 
 static int gemm_entry(GemmOp op, float *C, const float *A, const float *B, int M, int K, int N,
                       const char *names) {
@@ -58,9 +74,9 @@ int tl::gemm_run_add(DeviceCtx *c, GemmOp op, float *C, const float *A, const fl
     return set_error(TL_EINVAL, "tensor-core engine forced but shape/alignment unsupported (M=%d K=%d N=%d)", M, K, N);
   if (tc_ok && g_engine_pref != 1) {
     const bool pair = g_engine_pref >= 3 || (g_engine_pref == 0 && gemm_tc_prefer_pair(I, J, R));
-    const bool f16 = pair && (g_engine_pref == 4 || (g_engine_pref == 0 && kAutoF16));
-    g_engine_last = f16 ? 4 : pair ? 3 : 2;
-    return gemm_tc(c, op, C, A, B, M, K, N, pair, add, f16);
+    const GemmSplit split = pair ? pair_split() : GemmSplit::TF32;
+    g_engine_last = engine_id(pair, split);
+    return gemm_tc(c, op, C, A, B, M, K, N, pair, add, split);
   }
   g_engine_last = 1;
   return gemm_simt(c, op, C, A, B, M, K, N, add);
@@ -72,9 +88,9 @@ bool tl::gemm_try_rope(DeviceCtx *c, float *C, const float *A, const float *B, i
   if (((reinterpret_cast<uintptr_t>(rope.cosT) | reinterpret_cast<uintptr_t>(rope.sinT)) & 15) != 0) return false;
   if (!gemm_tc_supported(GemmOp::NN, C, A, B, M, K, N)) return false;
   if (g_engine_pref == 0 && !gemm_tc_prefer_pair(M, N, K)) return false;
-  const bool f16 = g_engine_pref == 4 || (g_engine_pref == 0 && kAutoF16);
-  g_engine_last = f16 ? 4 : 3;
-  *rc = gemm_tc(c, GemmOp::NN, C, A, B, M, K, N, true, nullptr, f16, &rope);
+  const GemmSplit split = pair_split();
+  g_engine_last = engine_id(true, split);
+  *rc = gemm_tc(c, GemmOp::NN, C, A, B, M, K, N, true, nullptr, split, &rope);
   return true;
 }
 
@@ -85,9 +101,9 @@ int tl::gemm_run_nt_sum(DeviceCtx *c, float *C, int nprod, const float *const *A
     fused = N[t] > 0 && gemm_tc_supported(GemmOp::NT, C, A[t], B[t], M, K, N[t]) &&
             (g_engine_pref >= 3 || gemm_tc_prefer_pair(M, K, N[t]));
   if (fused) {
-    const bool f16 = g_engine_pref == 4 || (g_engine_pref == 0 && kAutoF16);
-    g_engine_last = f16 ? 4 : 3;
-    return gemm_tc_nt_sum(c, C, nprod, A, B, N, M, K, f16);
+    const GemmSplit split = pair_split();
+    g_engine_last = engine_id(true, split);
+    return gemm_tc_nt_sum(c, C, nprod, A, B, N, M, K, split);
   }
   for (int t = 0; t < nprod; t++) {
     const int rc = gemm_run_add(c, GemmOp::NT, C, A[t], B[t], M, K, N[t], t == 0 ? nullptr : C);
@@ -136,7 +152,7 @@ TL_API int tl_matmul_bt_sum(float *dX, int nprod, const float *const *dY, const 
   return gemm_run_nt_sum(c, dX, n, As, Bs, Ns, M, K);
 }
 TL_API int tl_set_gemm_engine(int engine) {
-  if (engine < 0 || engine > 4) return set_error(TL_EINVAL, "engine must be 0, 1, 2, 3 or 4");
+  if (engine < 0 || engine > 5) return set_error(TL_EINVAL, "engine must be 0, 1, 2, 3, 4 or 5");
   g_engine_pref = engine;
   return TL_OK;
 }

@@ -43,12 +43,20 @@ struct GemmRope {
   const float *cosT, *sinT;
   int T;
 };
+// How the CTA-pair kernel splits each fp32 product: tf32 hi/lo (three tf32
+// MMAs), scaled fp16 hi/lo (three fp16 MMAs, specialised warps), or the
+// hybrid (one tf32 hi*hi MMA and the two cross terms as one bf16 chain).
+enum class GemmSplit { TF32 = 0, F16 = 1, HYB = 2 };
 // pair: the CTA-pair kernel (256 x 256 tiles over two SMs) instead of the
-// one-CTA kernel (128 x 128 tiles); f16 (pair only): operands split into
-// scaled fp16 hi/lo parts instead of tf32 hi/lo; rope (pair only): RoPE on
-// the output rows (no split-K then).
+// one-CTA kernel (128 x 128 tiles); split (pair only): see GemmSplit; rope
+// (pair only): RoPE on the output rows (no split-K then).
 int gemm_tc(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, int M, int K, int N, bool pair,
-            const float *add, bool f16, const GemmRope *rope = nullptr);
+            const float *add, GemmSplit split, const GemmRope *rope = nullptr);
+// The automatic engine choice gives the pair kernel the hybrid split while a
+// scope is open on this thread (the device training step's GEMMs: long runs
+// under the power cap, where its bf16 MMAs let the clock rise), else the tf32
+// split.  Scopes nest.
+void gemm_sustained_scope(bool enter);
 // C[M,N] = A[M,K] B[K,N] with RoPE on C's rows, in one pair-kernel launch;
 // false (nothing launched) where the engine choice would not give the pair
 // kernel this shape, or N is not whole heads of 64.
@@ -59,7 +67,7 @@ bool gemm_try_rope(DeviceCtx *c, float *C, const float *A, const float *B, int M
 // CTA-pair launch whose reduction walks the products' k-blocks in turn
 // (overwrites C).
 int gemm_tc_nt_sum(DeviceCtx *c, float *C, int nprod, const float *const *A, const float *const *B, const int *N,
-                   int M, int K, bool f16);
+                   int M, int K, GemmSplit split);
 // The same sum through the engine choice: one launch when the pair kernel
 // would take every product, else one NT GEMM per product accumulating in turn.
 int gemm_run_nt_sum(DeviceCtx *c, float *C, int nprod, const float *const *A, const float *const *B, const int *N,

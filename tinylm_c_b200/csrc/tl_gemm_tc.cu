@@ -41,6 +41,7 @@
 // kernel -- and is the default wherever both output sides exceed 128.
 #include <cuda.h>
 #include <cuda_fp16.h>
+#include <cuda_bf16.h>
 #include <algorithm>
 #include <cudaTypedefs.h>
 #include "tl_gemm.cuh"
@@ -420,6 +421,7 @@ __host__ __device__ constexpr uint32_t make_idesc_pair_f16(bool a_mn, bool b_mn)
          ((uint32_t)(PM >> 4) << 24);
 }
 __device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
+__device__ __forceinline__ uint32_t b2_bits(__nv_bfloat162 h) { return *reinterpret_cast<uint32_t *>(&h); }
 // Binary exponent of a max |x| (float bits), limited to +-100 (0 for zero;
 // non-finite and subnormal maxima land on the limits).
 __device__ __forceinline__ int amax_exp(unsigned bits) {
@@ -427,8 +429,17 @@ __device__ __forceinline__ int amax_exp(unsigned bits) {
 }
 __device__ __forceinline__ float exp2i(int k) { return __uint_as_float((uint32_t)(k + 127) << 23); }
 
-
-template <bool A_MN, bool B_MN, bool F16>
+// The hybrid split (HYB): hi*hi stays one tf32 product on the raw tile (the
+// MMA reads the fp32 values and uses their tf32 part), and the two cross
+// terms become one bf16 chain over K-concatenated operands, A as
+// [bf16(hi) | bf16(lo)] and B as [bf16(lo) | bf16(hi)] along K:
+// sum_k hi_a lo_b + lo_a hi_b.  bf16 keeps fp32's exponent range, so no scale
+// is needed; the rounding of hi and lo to bf16 costs at most 2^-18 |a||b| per
+// cross term (the tf32 split's lo*hi terms: 2^-20 each).  Per k-block four
+// tf32 MMAs and four bf16 MMAs (K = 16) replace twelve tf32 MMAs; the split
+// warps write the bf16 halves into the lo ring in the fp16 split's operand
+// layouts below, and the raw slot stays until the tf32 products are done.
+template <bool A_MN, bool B_MN, bool HYB>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
 gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmA1, const __grid_constant__ CUtensorMap tmB1,
@@ -444,9 +455,6 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
   constexpr int NBARS = 2 * RAW_STAGES + 2 * LO_STAGES + 4;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + NBARS);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
-  // F16: scales of A and B of each product [A0, B0, A1, B1, A2, B2], then the
-  // inverse product scale
-  float *scl = reinterpret_cast<float *>(tmem_slot + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
@@ -484,7 +492,7 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
   if (threadIdx.x == 0) {
     for (int s = 0; s < RAW_STAGES; s++) {
       mbar_init(bar_full(s), 1);
-      mbar_init(bar_rempty(s), F16 ? 8 : 1);   // F16: this CTA's split warps, else the pair's MMAs
+      mbar_init(bar_rempty(s), 1);   // the pair's MMAs
     }
     for (int s = 0; s < LO_STAGES; s++) {
       mbar_init(bar_ready(s), PAIR_SIGNALLERS);
@@ -495,26 +503,6 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
       mbar_init(bar_acce(b), PAIR_SIGNALLERS);
     }
     *abort_flag = 0;
-    if (F16) {
-      // Operand scale 2^(14 - e), e = exponent of its max |x|; the products
-      // share the smallest product scale 2^P (A's scale lowered to match).
-      // (P is kept inside the float exponent range; outside it the fp32
-      // result over- or underflows as well.)
-      const int nprod = p.seg_end1 != 0x7fffffff ? 3 : (p.seg_end0 != 0x7fffffff ? 2 : 1);
-      int P = 1 << 20;
-#pragma unroll
-      for (int t = 0; t < 3; t++)
-        if (t < nprod) P = min(P, 28 - amax_exp(p.amax[2 * t]) - amax_exp(p.amax[2 * t + 1]));
-      P = max(-126, min(126, P));
-#pragma unroll
-      for (int t = 0; t < 3; t++) {
-        const int sb = t < nprod ? 14 - amax_exp(p.amax[2 * t + 1]) : 0;
-        const int ea = t < nprod ? max(P - sb, -126) : 0;
-        scl[2 * t] = exp2i(ea);
-        scl[2 * t + 1] = t < nprod ? exp2i(P - ea) : 1.0f;
-      }
-      scl[6] = exp2i(-P);
-    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
@@ -582,27 +570,38 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         tc_fence_after();
         const uint32_t hi = raw_base + rs * RAW_BYTES, lo = lo_base + ls * RAW_BYTES;
         const uint32_t d = tmem + b * PN;
-        if constexpr (F16) {
-          constexpr uint32_t idesc16 = make_idesc_pair_f16(A_MN, B_MN);
+        if constexpr (HYB) {
+          // tf32 hi*hi on the raw tile, then the cross terms: K-major operands
+          // keep [hi | lo] in the two halves of each 128-byte row, MN-major
+          // ones in two planes 8 KB apart (2 KB per K = 16 step).
+          constexpr uint32_t idesc32 = make_idesc_pair(A_MN, B_MN);
+          constexpr uint32_t idescbf = make_idesc_pair_f16(A_MN, B_MN) | (1u << 7) | (1u << 10);   // bf16
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; kk++) {
-            // K-major: hi at 32 bytes per K = 16 step, lo 64 bytes further;
-            // MN-major: planes 8 KB apart, 2 KB (16 K rows) per step.
-            uint64_t op[2][2];   // [A, B][hi, lo]
+          for (int kk = 0; kk < BK / 8; kk++) {
+            const uint32_t a_off = A_MN ? kk * 1024 : kk * 32;
+            const uint32_t b_off = (B_MN ? kk * 1024 : kk * 32) + TILE_A;
+            constexpr uint32_t a_lbo = A_MN ? 4096 : 16, b_lbo = B_MN ? 4096 : 16;
+            constexpr uint32_t a_sbo = A_MN ? 512 : 1024, b_sbo = B_MN ? 512 : 1024;
+            constexpr uint32_t a_lay = A_MN ? LAYOUT_SW128_BASE32B : LAYOUT_SW128;
+            constexpr uint32_t b_lay = B_MN ? LAYOUT_SW128_BASE32B : LAYOUT_SW128;
+            tc_mma_pair(d, smem_desc(hi + a_off, a_lbo, a_sbo, a_lay), smem_desc(hi + b_off, b_lbo, b_sbo, b_lay),
+                        idesc32, (kin > 0 || kk > 0) ? 1u : 0u);
+          }
+#pragma unroll
+          for (int kc = 0; kc < 4; kc++) {
+            const int pl = kc >> 1, kk = kc & 1;   // half (plane) of the concatenated K, step in it
+            uint64_t op[2];
 #pragma unroll
             for (int w = 0; w < 2; w++) {
               const bool mn = w ? B_MN : A_MN;
               const uint32_t t0 = lo + (w ? TILE_A : 0);
-              op[w][0] = mn ? smem_desc(t0 + kk * 2048, 4096, 1024, LAYOUT_SW128)
-                            : smem_desc(t0 + kk * 32, 16, 1024, LAYOUT_SW128);
-              op[w][1] = mn ? smem_desc(t0 + 8192 + kk * 2048, 4096, 1024, LAYOUT_SW128)
-                            : smem_desc(t0 + 64 + kk * 32, 16, 1024, LAYOUT_SW128);
+              op[w] = mn ? smem_desc(t0 + pl * 8192 + kk * 2048, 4096, 1024, LAYOUT_SW128)
+                         : smem_desc(t0 + pl * 64 + kk * 32, 16, 1024, LAYOUT_SW128);
             }
-            tc_mma_pair_f16(d, op[0][1], op[1][0], idesc16, (kin > 0 || kk > 0) ? 1u : 0u);
-            tc_mma_pair_f16(d, op[0][0], op[1][1], idesc16, 1);
-            tc_mma_pair_f16(d, op[0][0], op[1][0], idesc16, 1);
+            tc_mma_pair_f16(d, op[0], op[1], idescbf, 1);
           }
           tc_commit_pair(bar_lempty(ls));
+          tc_commit_pair(bar_rempty(rs));
         } else {
 #pragma unroll
         for (int kk = 0; kk < BK / 8; kk++) {
@@ -701,14 +700,11 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         if (!__all_sync(0xffffffffu, landed)) { ok = false; break; }
         const uint8_t *src = raw_ring + rs * RAW_BYTES;
         uint8_t *dst = lo_ring + ls * RAW_BYTES;
-        if constexpr (F16) {
-          const int kg = kb0 + kb;
-          const int tp = kg >= p.seg_end1 ? 2 : (kg >= p.seg_end0 ? 1 : 0);
+        if constexpr (HYB) {
           // Warps 2-5 convert the A tile, 6-9 this CTA's B half: one raw
           // 128-byte row (32 values) per thread, written as 16-byte chunks.
           const bool is_a = t < 128, mn = is_a ? A_MN : B_MN;
           const int tt = t & 127;
-          const float sc = scl[2 * tp + (is_a ? 0 : 1)];
           const uint8_t *sb = src + (is_a ? 0 : TILE_A);
           uint8_t *db = dst + (is_a ? 0 : TILE_A);
           // Raw row and its swizzle: K-major row r = tt (chunk c at c ^ (r % 8));
@@ -718,19 +714,18 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
           const int rxor = mn ? (k & 3) << 1 : (tt & 7);
 #pragma unroll
           for (int j = 0; j < 4; j++) {
-            // fp16 chunk j of hi (and of lo): raw chunks 2j and 2j + 1
+            // bf16 chunk j of hi (and of lo): raw chunks 2j and 2j + 1
             uint32_t hw[4], lw[4];
 #pragma unroll
             for (int u = 0; u < 2; u++) {
               const float4 x = *reinterpret_cast<const float4 *>(sb + rbase + (((2 * j + u) ^ rxor) << 4));
-              // hi = the scaled value with its low 13 significand bits cleared
-              // (11 bits: exact in fp16), lo = the rest (exact in fp32).
-              const float v0 = x.x * sc, v1 = x.y * sc, v2 = x.z * sc, v3 = x.w * sc;
-              const float h0 = tf32_trunc(v0), h1 = tf32_trunc(v1), h2 = tf32_trunc(v2), h3 = tf32_trunc(v3);
-              hw[2 * u] = h2_bits(__floats2half2_rn(h0, h1));
-              hw[2 * u + 1] = h2_bits(__floats2half2_rn(h2, h3));
-              lw[2 * u] = h2_bits(__floats2half2_rn(v0 - h0, v1 - h1));
-              lw[2 * u + 1] = h2_bits(__floats2half2_rn(v2 - h2, v3 - h3));
+              // hi = the tf32 part the hi*hi product uses, lo = the rest (exact
+              // in fp32), each rounded to bf16
+              const float h0 = tf32_trunc(x.x), h1 = tf32_trunc(x.y), h2 = tf32_trunc(x.z), h3 = tf32_trunc(x.w);
+              hw[2 * u] = b2_bits(__floats2bfloat162_rn(h0, h1));
+              hw[2 * u + 1] = b2_bits(__floats2bfloat162_rn(h2, h3));
+              lw[2 * u] = b2_bits(__floats2bfloat162_rn(x.x - h0, x.y - h1));
+              lw[2 * u + 1] = b2_bits(__floats2bfloat162_rn(x.z - h2, x.w - h3));
             }
             int hoff, loff;
             if (!mn) {
@@ -744,8 +739,10 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
               hoff = blk * 4096 + (k >> 3) * 1024 + (k & 7) * 128 + ((ch ^ (k & 7)) << 4);
               loff = hoff + 8192;
             }
-            *reinterpret_cast<uint4 *>(db + hoff) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-            *reinterpret_cast<uint4 *>(db + loff) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+            // A's concatenated K is [hi | lo], B's [lo | hi]
+            const uint4 H4 = make_uint4(hw[0], hw[1], hw[2], hw[3]), L4 = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+            *reinterpret_cast<uint4 *>(db + hoff) = is_a ? H4 : L4;
+            *reinterpret_cast<uint4 *>(db + loff) = is_a ? L4 : H4;
           }
         } else {
           // A tile then this CTA's B half: 2048 float4 of raw data, 8 per
@@ -764,16 +761,10 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         fence_proxy_async();
         __syncwarp();
         if (lane == 0) mbar_arrive_remote(cluster_map(bar_ready(ls), 0));
-        if (F16 && lane == 0) mbar_arrive(bar_rempty(rs));   // the raw slot is converted
         kb++;
       }
     }
     if (ok && !*abort_flag) {
-      if (F16) {
-        const float inv = scl[6];
-#pragma unroll
-        for (int e = 0; e < BN; e++) acc[e] *= inv;
-      }
       const int row = i0 + q * 32 + lane;
       if (p.rope_cos && row < p.I) {
         // RoPE (tinylm.c:626-640): this thread's 128 columns are two heads;
@@ -1340,16 +1331,18 @@ static int launch(DeviceCtx *c, const CUtensorMap &ma, const CUtensorMap &mb, co
 
 // CTA pairs: grid x runs over the pairs' CTAs (cluster of 2 along x; the
 // kernel maps pairs to output tiles in grouped order), z over K splits.
-template <bool A_MN, bool B_MN, bool F16>
+// SPLIT: the GemmSplit (tf32, fp16 on specialised warps, hybrid).
+template <bool A_MN, bool B_MN, int SPLIT>
 static int launch_pair(DeviceCtx *c, const CUtensorMap &ma, const CUtensorMap &mb, const Params &p, int splits,
                        const CUtensorMap *extra = nullptr) {
+  constexpr bool F16 = SPLIT == (int)GemmSplit::F16, HYB = SPLIT == (int)GemmSplit::HYB;
   static bool attr_set[kMaxDevices] = {};
   if (!attr_set[c->device]) {
     if (F16)
       TL_TRY_CUDA(cudaFuncSetAttribute(gemm_tc_pair_f16ws_kernel<A_MN, B_MN>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, PAIR_SMEM_BYTES));
     else
-      TL_TRY_CUDA(cudaFuncSetAttribute(gemm_tc_pair_kernel<A_MN, B_MN, false>,
+      TL_TRY_CUDA(cudaFuncSetAttribute(gemm_tc_pair_kernel<A_MN, B_MN, HYB>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, PAIR_SMEM_BYTES));
     attr_set[c->device] = true;
   }
@@ -1376,8 +1369,7 @@ static int launch_pair(DeviceCtx *c, const CUtensorMap &ma, const CUtensorMap &m
     gemm_tc_pair_f16ws_kernel<A_MN, B_MN><<<grid, WS_THREADS, PAIR_SMEM_BYTES, c->stream>>>(ma, mb, a1, b1, a2, b2, p);
   }
   else
-    gemm_tc_pair_kernel<A_MN, B_MN, false><<<grid, NUM_THREADS, PAIR_SMEM_BYTES, c->stream>>>(ma, mb, a1, b1, a2, b2,
-                                                                                              p);
+    gemm_tc_pair_kernel<A_MN, B_MN, HYB><<<grid, NUM_THREADS, PAIR_SMEM_BYTES, c->stream>>>(ma, mb, a1, b1, a2, b2, p);
   TL_TRY_CUDA(cudaGetLastError());
   return TL_OK;
 }
@@ -1410,6 +1402,9 @@ int gemm_tc_prepare(DeviceCtx *c) {
   TL_PREP((tc::gemm_tc_pair_kernel<false, true, false>), tc::PAIR_SMEM_BYTES);
   TL_PREP((tc::gemm_tc_pair_kernel<false, false, false>), tc::PAIR_SMEM_BYTES);
   TL_PREP((tc::gemm_tc_pair_kernel<true, true, false>), tc::PAIR_SMEM_BYTES);
+  TL_PREP((tc::gemm_tc_pair_kernel<false, true, true>), tc::PAIR_SMEM_BYTES);
+  TL_PREP((tc::gemm_tc_pair_kernel<false, false, true>), tc::PAIR_SMEM_BYTES);
+  TL_PREP((tc::gemm_tc_pair_kernel<true, true, true>), tc::PAIR_SMEM_BYTES);
   TL_PREP((tc::gemm_tc_pair_f16ws_kernel<false, true>), tc::PAIR_SMEM_BYTES);
   TL_PREP((tc::gemm_tc_pair_f16ws_kernel<false, false>), tc::PAIR_SMEM_BYTES);
   TL_PREP((tc::gemm_tc_pair_f16ws_kernel<true, true>), tc::PAIR_SMEM_BYTES);
@@ -1427,12 +1422,13 @@ bool gemm_tc_prefer_pair(int I, int J, int R) {
 // through the prepared tensor maps.  extra / seg_end0 / seg_end1: the maps
 // and k-block boundaries of a second and third product summed into the same
 // output (pair kernel, NT only).
-// amax: the operand arrays of the fp16-split pair kernel (nullptr: tf32); their
-// max |x| is found first, on the stream, into the context's scratch.
+// amax: the operand arrays of the fp16-split pair kernel (nullptr: another
+// split); their max |x| is found first, on the stream, into the context's
+// scratch.  hyb: the pair kernel with the hybrid split.
 static int gemm_tc_launch(DeviceCtx *c, GemmOp op, float *C, int I, int J, int nk, int out_ldc,
                           const CUtensorMap &ma, const CUtensorMap &mb, const CUtensorMap *extra, int seg_end0,
                           int seg_end1, bool pair, const float *add, const tc::AmaxArgs *amax, int namax,
-                          const GemmRope *rope = nullptr) {
+                          bool hyb, const GemmRope *rope = nullptr) {
   tc::Params p;
   p.C = C; p.I = I; p.J = J; p.R = nk * tc::BK; p.err = c->err_flag;
   p.seg_end0 = seg_end0; p.seg_end1 = seg_end1;
@@ -1521,18 +1517,21 @@ static int gemm_tc_launch(DeviceCtx *c, GemmOp op, float *C, int I, int J, int n
   switch (op) {
     case GemmOp::NN:
       rc = !pair ? tc::launch<false, true>(c, ma, mb, p, splits)
-           : f16 ? tc::launch_pair<false, true, true>(c, ma, mb, p, splits)
-                 : tc::launch_pair<false, true, false>(c, ma, mb, p, splits);
+           : f16 ? tc::launch_pair<false, true, (int)GemmSplit::F16>(c, ma, mb, p, splits)
+           : hyb ? tc::launch_pair<false, true, (int)GemmSplit::HYB>(c, ma, mb, p, splits)
+                 : tc::launch_pair<false, true, (int)GemmSplit::TF32>(c, ma, mb, p, splits);
       break;
     case GemmOp::NT:
       rc = !pair ? tc::launch<false, false>(c, ma, mb, p, splits)
-           : f16 ? tc::launch_pair<false, false, true>(c, ma, mb, p, splits, extra)
-                 : tc::launch_pair<false, false, false>(c, ma, mb, p, splits, extra);
+           : f16 ? tc::launch_pair<false, false, (int)GemmSplit::F16>(c, ma, mb, p, splits, extra)
+           : hyb ? tc::launch_pair<false, false, (int)GemmSplit::HYB>(c, ma, mb, p, splits, extra)
+                 : tc::launch_pair<false, false, (int)GemmSplit::TF32>(c, ma, mb, p, splits, extra);
       break;
     case GemmOp::TN:
       rc = !pair ? tc::launch<true, true>(c, ma, mb, p, splits)
-           : f16 ? tc::launch_pair<true, true, true>(c, ma, mb, p, splits)
-                 : tc::launch_pair<true, true, false>(c, ma, mb, p, splits);
+           : f16 ? tc::launch_pair<true, true, (int)GemmSplit::F16>(c, ma, mb, p, splits)
+           : hyb ? tc::launch_pair<true, true, (int)GemmSplit::HYB>(c, ma, mb, p, splits)
+                 : tc::launch_pair<true, true, (int)GemmSplit::TF32>(c, ma, mb, p, splits);
       break;
   }
   if (!rc && p.tail_splits > 1) {
@@ -1553,7 +1552,8 @@ static int gemm_tc_launch(DeviceCtx *c, GemmOp op, float *C, int I, int J, int n
 }
 
 int gemm_tc(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, int M, int K, int N, bool pair,
-            const float *add, bool f16, const GemmRope *rope) {
+            const float *add, GemmSplit split, const GemmRope *rope) {
+  const bool f16 = pair && split == GemmSplit::F16, hyb = pair && split == GemmSplit::HYB;
   int rc;
   if ((rc = tc::get_encoder())) return rc;
   int I, J, R;
@@ -1586,11 +1586,12 @@ int gemm_tc(DeviceCtx *c, GemmOp op, float *C, const float *A, const float *B, i
     case GemmOp::TN: am.n[0] = (size_t)M * K; am.n[1] = (size_t)M * N; break;
   }
   return gemm_tc_launch(c, op, C, I, J, nk, out_ldc, ma, mb, nullptr, 0x7fffffff, 0x7fffffff, pair, add,
-                        f16 ? &am : nullptr, 2, rope);
+                        f16 ? &am : nullptr, 2, hyb, rope);
 }
 
 int gemm_tc_nt_sum(DeviceCtx *c, float *C, int nprod, const float *const *A, const float *const *B, const int *N,
-                   int M, int K, bool f16) {
+                   int M, int K, GemmSplit split) {
+  const bool f16 = split == GemmSplit::F16, hyb = split == GemmSplit::HYB;
   if (nprod < 1 || nprod > 3) return set_error(TL_EINVAL, "gemm_tc_nt_sum takes 1 to 3 products, not %d", nprod);
   int rc;
   if ((rc = tc::get_encoder())) return rc;
@@ -1616,7 +1617,7 @@ int gemm_tc_nt_sum(DeviceCtx *c, float *C, int nprod, const float *const *A, con
     am.p[2 * t + 1] = B[t]; am.n[2 * t + 1] = (size_t)K * N[t];
   }
   return gemm_tc_launch(c, GemmOp::NT, C, M, K, nk, K, maps[0], maps[1], maps + 2, end[0], end[1], true, nullptr,
-                        f16 ? &am : nullptr, 2 * nprod);
+                        f16 ? &am : nullptr, 2 * nprod, hyb);
 }
 
 }  // namespace tl

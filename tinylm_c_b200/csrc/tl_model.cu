@@ -202,8 +202,16 @@ static int micro_step(DeviceCtx *c, Model &m, const float *P, float *G, const in
   return TL_OK;
 }
 
+// The step's GEMMs run as one long sequence under the power cap: the
+// automatic engine choice gives them the hybrid split (gemm_sustained_scope).
+struct SustainedGemms {
+  SustainedGemms() { gemm_sustained_scope(true); }
+  ~SustainedGemms() { gemm_sustained_scope(false); }
+};
+
 static int run_batch(DeviceCtx *c, Model &m, const float *P, float *G, const int *tok, const int *tgt,
                      const int *tgt_mtp, int B, float *loss_dev, bool backward, OverlapState *ov = nullptr) {
+  SustainedGemms sustained;
   if (B < 1 || B % m.mb) return set_error(TL_EINVAL, "batch %d must be a positive multiple of the micro-batch %d", B, m.mb);
   const size_t Ntot = (size_t)B * m.T;
   const float scale = 1.0f / (float)Ntot;

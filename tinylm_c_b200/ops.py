@@ -103,7 +103,9 @@ def mm_atb(dW, X, dY, M, K, N):
 def set_gemm_engine(engine):
     """0 automatic, 1 CUDA-core fp32, 2 tensor-core 3xTF32 (one CTA per
     128 x 128 tile), 3 tensor-core 3xTF32 (CTA pair per 256 x 256 tile),
-    4 tensor-core CTA pair with scaled fp16 hi/lo operands (3 fp16 MMAs)."""
+    4 tensor-core CTA pair with scaled fp16 hi/lo operands (3 fp16 MMAs),
+    5 tensor-core CTA pair with the hybrid split (tf32 hi*hi + bf16 cross
+    terms)."""
     check(lib().tl_set_gemm_engine(int(engine)))
 
 
