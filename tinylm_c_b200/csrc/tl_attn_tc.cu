@@ -42,6 +42,7 @@
 // code (tl_device_status) and winds down.  No TMA multicast: the leader's
 // commits use tcgen05.commit multicast, which moves no data.
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cudaTypedefs.h>
 #include <algorithm>
 #include <cstdlib>
@@ -713,9 +714,14 @@ attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmS, const __grid_cons
 // for one (sequence, kv head, key block kb of 128 keys), looping over the
 // group's query heads and the 32-query chunks at or after the key block.
 // M = 128 keys throughout (cta_group::1):
-//   S^T = K Q_c^T, dP^T = V dO_c^T   N = 32 queries, K = 64 in two blocks;
-//        K and V stay resident (K-major, with lo parts), Q_c and dO_c arrive
-//        by TMA as K-major B tiles; into TMEM buffer i % 2 of chunk i.
+//   S^T = K Q_c^T, dP^T = V dO_c^T   N = 32 queries, K = 64 in two blocks,
+//        hybrid split: one tf32 product of the raw tiles (hi*hi) and the two
+//        cross terms as one bf16 chain over K-concatenated tiles, A as
+//        [bf16(hi) | bf16(lo)] and B as [bf16(lo) | bf16(hi)] per 128-byte
+//        row (16 MMAs per product instead of 24, and a third fewer re-reads
+//        of the A tile through shared memory); K and V stay resident
+//        (K-major, raw and concatenated), Q_c and dO_c arrive by TMA as
+//        K-major B tiles; into TMEM buffer i % 2 of chunk i.
 //   P^T = exp(scale s - lse), dS^T = P^T (dP^T - D) scale   (warps 2-5, a key
 //        row per thread): raw and lo parts written back to TMEM (P over S,
 //        dS over dP), and dS^T to the scratch the dQ product reads.
@@ -725,23 +731,24 @@ attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmS, const __grid_cons
 //        which warps 6-9 add into fp32 registers once the head is done.
 // The chunk tiles land in two raw buffers per kind (chunk i in buffer i % 2,
 // so the next chunk's copies are in flight while this one is used) and have
-// one lo buffer per kind, written once the previous chunk's products are
-// done with it.  Roles (384 threads): warp 0 lane 0 loads K, V and the
+// one converted buffer per kind (bf16 halves for the K-major tiles, tf32 lo
+// parts for the MN-major ones), written once the previous chunk's products
+// are done with it.  Roles (384 threads): warp 0 lane 0 loads K, V and the
 // K-major tiles, lane 1 the MN-major tiles; warp 1 owns TMEM and issues the
-// MMAs; warps 2-5 P and dS; warps 6-9 the lo parts of K, V and the MN-major
-// tiles, and the per-head dV / dK sums; warps 10-11 the lo parts of the
-// K-major tiles.  Every wait is bounded.
+// MMAs; warps 2-5 P and dS; warps 6-9 the bf16 halves of K and V, the lo
+// parts of the MN-major tiles, and the per-head dV / dK sums; warps 10-11
+// the bf16 halves of the K-major tiles.  Every wait is bounded.
 constexpr int BW_THREADS = 384;
 constexpr int BW_NQ = 32;                               // queries per chunk
 constexpr int BW_KTILE = QR * 32 * 4;                   // 16 KB: 128 keys x 32 of head_dim
 constexpr int BW_CTILE = BW_NQ * 32 * 4;                // 4 KB: 32 queries x 32 of head_dim
-constexpr int BW_OFF_K = 0, BW_OFF_V = 4 * BW_KTILE;    // raw (2 tiles), then lo (2 tiles): +32 KB
+constexpr int BW_OFF_K = 0, BW_OFF_V = 4 * BW_KTILE;    // raw (2 tiles), then bf16 [hi | lo] (2 tiles): +32 KB
 constexpr int BW_KV_LO = 2 * BW_KTILE;
 // A chunk buffer: Q (2 tiles of 32 head_dim columns), then dO (2 tiles).
 constexpr int BW_CBUF = 4 * BW_CTILE;                   // 16 KB
 constexpr int BW_CB_O = 2 * BW_CTILE;                   // dO's offset in a chunk buffer
 constexpr int BW_OFF_KMR = 8 * BW_KTILE;                // K-major raw buffers 0, 1
-constexpr int BW_OFF_KML = BW_OFF_KMR + 2 * BW_CBUF;    // K-major lo
+constexpr int BW_OFF_KML = BW_OFF_KMR + 2 * BW_CBUF;    // K-major bf16 [lo | hi]
 constexpr int BW_OFF_MNR = BW_OFF_KML + BW_CBUF;        // MN-major raw buffers 0, 1
 constexpr int BW_OFF_MNL = BW_OFF_MNR + 2 * BW_CBUF;    // MN-major lo
 constexpr int BW_DATA = BW_OFF_MNL + BW_CBUF;           // 224 KB
@@ -754,6 +761,8 @@ static_assert(BW_SMEM_BYTES <= 232448, "dK/dV kernel exceeds the opt-in shared m
 constexpr int BW_TMEM_COLS = 512;
 constexpr uint32_t BW_IDESC_SD = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BW_NQ >> 3) << 17) |
                                  ((uint32_t)(QR >> 4) << 24);
+constexpr uint32_t BW_IDESC_SD_BF = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BW_NQ >> 3) << 17) |
+                                    ((uint32_t)(QR >> 4) << 24);   // bf16 x bf16 -> f32
 constexpr uint32_t BW_IDESC_ACC = (1u << 4) | (2u << 7) | (2u << 10) | (1u << 16) | ((uint32_t)(HD >> 3) << 17) |
                                   ((uint32_t)(QR >> 4) << 24);
 
@@ -811,6 +820,45 @@ __device__ __forceinline__ void split_lo(uint8_t *src, int lo_off, int n16, int 
     lo.z = x.z - tf32_trunc(x.z); lo.w = x.w - tf32_trunc(x.w);
     *reinterpret_cast<float4 *>(src + lo_off + idx * 16) = lo;
   }
+}
+
+// The bf16 K-concatenated operand of K-major tiles (rows of 32 floats, 128
+// bytes, 16-byte chunks at c ^ (row % 8)): row r of dst holds bf16(hi) of its
+// 32 values in chunks 0-3 and bf16(lo) in chunks 4-7, or lo first for a B
+// operand; hi is the tf32 part the hi*hi product uses, lo = x - hi.  A task
+// (row, j) turns raw chunks 2j, 2j + 1 into chunks j and 4 + j.
+__device__ __forceinline__ uint32_t bf2_bits(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t *>(&h);
+}
+__device__ __forceinline__ void split_cat(const uint8_t *src, uint8_t *dst, int rows, bool lo_first, int t,
+                                          int nthreads) {
+  for (int task = t; task < rows * 4; task += nthreads) {
+    const int r = task >> 2, j = task & 3, sw = r & 7;
+    uint32_t hw[4], lw[4];
+#pragma unroll
+    for (int u = 0; u < 2; u++) {
+      const float4 x = *reinterpret_cast<const float4 *>(src + r * 128 + (((2 * j + u) ^ sw) << 4));
+      const float h0 = tf32_trunc(x.x), h1 = tf32_trunc(x.y), h2 = tf32_trunc(x.z), h3 = tf32_trunc(x.w);
+      hw[2 * u] = bf2_bits(h0, h1);
+      hw[2 * u + 1] = bf2_bits(h2, h3);
+      lw[2 * u] = bf2_bits(x.x - h0, x.y - h1);
+      lw[2 * u + 1] = bf2_bits(x.z - h2, x.w - h3);
+    }
+    const uint4 H4 = make_uint4(hw[0], hw[1], hw[2], hw[3]), L4 = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    *reinterpret_cast<uint4 *>(dst + r * 128 + ((j ^ sw) << 4)) = lo_first ? L4 : H4;
+    *reinterpret_cast<uint4 *>(dst + r * 128 + (((4 + j) ^ sw) << 4)) = lo_first ? H4 : L4;
+  }
+}
+
+// D (TMEM) (+)= A (shared memory) * B (shared memory), bf16 operands.
+__device__ __forceinline__ void tc_mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{ .reg .pred p; setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
 }
 
 __global__ void __launch_bounds__(BW_THREADS, 1)
@@ -922,17 +970,24 @@ attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmKk, const __grid_c
         for (int m = 0; m < 2; m++) {            // m = 0: S^T = K Q^T, 1: dP^T = V dO^T
           const uint32_t d = tmem + 64 * b + 32 * m;
           const uint32_t at = base + (m ? BW_OFF_V : BW_OFF_K), bo = m ? BW_CB_O : 0;
+          // hi*hi: tf32 on the raw tiles
 #pragma unroll
           for (int x = 0; x < 2; x++) {
 #pragma unroll
-            for (int kk = 0; kk < 4; kk++) {
-              const uint64_t a_hi = smem_desc(at + x * BW_KTILE + kk * 32, 16, 1024, LAYOUT_SW128);
-              const uint64_t a_lo = smem_desc(at + BW_KV_LO + x * BW_KTILE + kk * 32, 16, 1024, LAYOUT_SW128);
-              const uint64_t b_hi = smem_desc(craw + bo + x * BW_CTILE + kk * 32, 16, 1024, LAYOUT_SW128);
-              const uint64_t b_lo = smem_desc(clo + bo + x * BW_CTILE + kk * 32, 16, 1024, LAYOUT_SW128);
-              tc_mma(d, a_lo, b_hi, BW_IDESC_SD, (x > 0 || kk > 0) ? 1u : 0u);
-              tc_mma(d, a_hi, b_lo, BW_IDESC_SD, 1);
-              tc_mma(d, a_hi, b_hi, BW_IDESC_SD, 1);
+            for (int kk = 0; kk < 4; kk++)
+              tc_mma(d, smem_desc(at + x * BW_KTILE + kk * 32, 16, 1024, LAYOUT_SW128),
+                     smem_desc(craw + bo + x * BW_CTILE + kk * 32, 16, 1024, LAYOUT_SW128), BW_IDESC_SD,
+                     (x > 0 || kk > 0) ? 1u : 0u);
+          }
+          // hi*lo + lo*hi: bf16 over the concatenated rows (two K = 16 steps
+          // per 64-byte half)
+#pragma unroll
+          for (int x = 0; x < 2; x++) {
+#pragma unroll
+            for (int kc = 0; kc < 4; kc++) {
+              const int off = (kc >> 1) * 64 + (kc & 1) * 32;
+              tc_mma_bf16(d, smem_desc(at + BW_KV_LO + x * BW_KTILE + off, 16, 1024, LAYOUT_SW128),
+                          smem_desc(clo + bo + x * BW_CTILE + off, 16, 1024, LAYOUT_SW128), BW_IDESC_SD_BF, 1);
             }
           }
         }
@@ -1041,7 +1096,7 @@ attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmKk, const __grid_c
       if (i >= 1 && !__all_sync(0xffffffffu, mbar_wait(bar(KM_EMPTY + (r ^ 1)), ((i - 1) >> 1) & 1, abort_flag,
                                                         a.err, 76)))
         break;
-      split_lo(smem + BW_OFF_KMR + r * BW_CBUF, BW_OFF_KML - (BW_OFF_KMR + r * BW_CBUF), BW_CBUF / 16, t, 64);
+      split_cat(smem + BW_OFF_KMR + r * BW_CBUF, smem + BW_OFF_KML, BW_CBUF / 128, true, t, 64);
       fence_proxy_async();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(KM_READY));
@@ -1055,8 +1110,8 @@ attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmKk, const __grid_c
     for (int e = 0; e < HD; e++) { accv[e] = 0.0f; acck[e] = 0.0f; }
     bool ok = __all_sync(0xffffffffu, mbar_wait(bar(KV_FULL), 0, abort_flag, a.err, 72));
     if (ok) {
-      split_lo(smem + BW_OFF_K, BW_KV_LO, 2 * BW_KTILE / 16, t, 128);
-      split_lo(smem + BW_OFF_V, BW_KV_LO, 2 * BW_KTILE / 16, t, 128);
+      split_cat(smem + BW_OFF_K, smem + BW_OFF_K + BW_KV_LO, 2 * BW_KTILE / 128, false, t, 128);
+      split_cat(smem + BW_OFF_V, smem + BW_OFF_V + BW_KV_LO, 2 * BW_KTILE / 128, false, t, 128);
       fence_proxy_async();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(KV_READY));
