@@ -10,11 +10,13 @@
 // split once per group.  CTA r holds query rows 128r..128r+127 and key rows
 // 128r..128r+127 of the item.
 //
-//   S = Q K^T      M = 256 queries, N = 256 keys, K = 64: 2 k-blocks x 4 x 3
-//                  tf32 MMAs (3xTF32: lo*hi + hi*lo + hi*hi) into TMEM buffer
-//                  x = item % 2 (columns 256x..256x+255); Q and K staged by
-//                  TMA (K-major, 128-byte swizzle), their lo parts written by
-//                  the softmax warps.
+//   S = Q K^T      M = 256 queries, N = 256 keys, K = 64, on the hybrid split:
+//                  hi*hi as 2 k-blocks x 4 tf32 MMAs on the raw tiles, the
+//                  cross terms as 2 x 4 bf16 MMAs over K-concatenated rows
+//                  (Q: [bf16(hi) | bf16(lo)], K: [bf16(lo) | bf16(hi)]), into
+//                  TMEM buffer x = item % 2 (columns 256x..256x+255); Q and K
+//                  staged by TMA (K-major, 128-byte swizzle), their bf16
+//                  halves written by the softmax warps.
 //   softmax        exact, two passes over S in TMEM: row max over the keys
 //                  <= the query (the two column halves exchange partial maxima
 //                  through shared memory), then p = 2^(s*scale*log2 e - max*log2 e)
@@ -76,6 +78,49 @@ __host__ __device__ constexpr uint32_t idesc_m256(int n, bool a_mn, bool b_mn) {
   return (1u << 4) | (2u << 7) | (2u << 10) | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) |
          ((uint32_t)(n >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
 }
+// the same shape with bf16 operands (kind::f16)
+__host__ __device__ constexpr uint32_t idesc_m256_bf16(int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
+}
+
+// The bf16 K-concatenated operand of K-major tiles (rows of 32 floats, 128
+// bytes, 16-byte chunks at c ^ (row % 8)): row r of dst holds bf16(hi) of its
+// 32 values in chunks 0-3 and bf16(lo) in chunks 4-7, or lo first for a B
+// operand; hi is the tf32 part the hi*hi product uses, lo = x - hi.  A task
+// (row, j) turns raw chunks 2j, 2j + 1 into chunks j and 4 + j.
+__device__ __forceinline__ uint32_t bf2_bits(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t *>(&h);
+}
+__device__ __forceinline__ void split_cat(const uint8_t *src, uint8_t *dst, int rows, bool lo_first, int t,
+                                          int nthreads) {
+  for (int task = t; task < rows * 4; task += nthreads) {
+    const int r = task >> 2, j = task & 3, sw = r & 7;
+    uint32_t hw[4], lw[4];
+#pragma unroll
+    for (int u = 0; u < 2; u++) {
+      const float4 x = *reinterpret_cast<const float4 *>(src + r * 128 + (((2 * j + u) ^ sw) << 4));
+      const float h0 = tf32_trunc(x.x), h1 = tf32_trunc(x.y), h2 = tf32_trunc(x.z), h3 = tf32_trunc(x.w);
+      hw[2 * u] = bf2_bits(h0, h1);
+      hw[2 * u + 1] = bf2_bits(h2, h3);
+      lw[2 * u] = bf2_bits(x.x - h0, x.y - h1);
+      lw[2 * u + 1] = bf2_bits(x.z - h2, x.w - h3);
+    }
+    const uint4 H4 = make_uint4(hw[0], hw[1], hw[2], hw[3]), L4 = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    *reinterpret_cast<uint4 *>(dst + r * 128 + ((j ^ sw) << 4)) = lo_first ? L4 : H4;
+    *reinterpret_cast<uint4 *>(dst + r * 128 + (((4 + j) ^ sw) << 4)) = lo_first ? H4 : L4;
+  }
+}
+
+// D (TMEM) (+)= A (shared memory) * B (shared memory), bf16 operands.
+__device__ __forceinline__ void tc_mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{ .reg .pred p; setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 
 struct Args {
   float *out, *lse;
@@ -109,7 +154,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   const uint32_t base = smem_u32(smem);
   auto stage = [&](int s) { return base + STAGE0 + s * STAGE_BYTES; };
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
-  // QK_FULL: Q (+ K) landed; QK_READY: their lo parts written (pair, leader's
+  // QK_FULL: Q (+ K) landed; QK_READY: their bf16 halves written (pair, leader's
   // copy); S_FULL[2]: S in TMEM buffer x complete (its Q/K also free again);
   // ST_FULL / ST_READY / ST_EMPTY [2]: V landed / P and V lo written / PV of
   // the stage done; O_FULL[2]: O in buffer x complete; O_EMPTY[2]: buffer x
@@ -210,6 +255,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     // ------------------------------------------- MMA issuer (leader CTA only)
     if (lane == 0 && rank == 0) {
       constexpr uint32_t idesc_s = idesc_m256(256, false, false);
+      constexpr uint32_t idesc_s_bf = idesc_m256_bf16(256);
       constexpr uint32_t idesc_o = idesc_m256(HD, false, true);
       // S = Q K^T of item jl into TMEM buffer jl % 2.
       auto issue_s = [&](int jl) -> bool {
@@ -219,19 +265,25 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
           return false;
         if (!mbar_wait_pair(bar(QK_READY), jl & 1, abort_flag, peer_flag, a.err, 32)) return false;
         tc_fence_after();
+        const uint32_t d = tmem + 256 * x;
+        // hi*hi: tf32 on the raw tiles; then hi*lo + lo*hi: one bf16 chain
+        // over the concatenated rows ([hi | lo] of Q, [lo | hi] of K)
 #pragma unroll
         for (int kb = 0; kb < 2; kb++) {
 #pragma unroll
           for (int kk = 0; kk < KBLK / 8; kk++) {
             const uint32_t off = kb * TILE + kk * 32;
-            const uint64_t q_hi = smem_desc(base + OFF_QR + off, 16, 1024, LAYOUT_SW128);
-            const uint64_t q_lo = smem_desc(base + OFF_QL + off, 16, 1024, LAYOUT_SW128);
-            const uint64_t k_hi = smem_desc(base + OFF_KR + off, 16, 1024, LAYOUT_SW128);
-            const uint64_t k_lo = smem_desc(base + OFF_KL + off, 16, 1024, LAYOUT_SW128);
-            const uint32_t d = tmem + 256 * x;
-            tc_mma_pair(d, q_lo, k_hi, idesc_s, (kb > 0 || kk > 0) ? 1u : 0u);
-            tc_mma_pair(d, q_hi, k_lo, idesc_s, 1);
-            tc_mma_pair(d, q_hi, k_hi, idesc_s, 1);
+            tc_mma_pair(d, smem_desc(base + OFF_QR + off, 16, 1024, LAYOUT_SW128),
+                        smem_desc(base + OFF_KR + off, 16, 1024, LAYOUT_SW128), idesc_s, (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+        }
+#pragma unroll
+        for (int kb = 0; kb < 2; kb++) {
+#pragma unroll
+          for (int kc = 0; kc < 4; kc++) {
+            const uint32_t off = kb * TILE + (kc >> 1) * 64 + (kc & 1) * 32;
+            tc_mma_pair_f16(d, smem_desc(base + OFF_QL + off, 16, 1024, LAYOUT_SW128),
+                            smem_desc(base + OFF_KL + off, 16, 1024, LAYOUT_SW128), idesc_s_bf, 1);
           }
         }
         tc_commit_pair(bar(S_FULL + x));
@@ -286,22 +338,13 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     const int tl = q4 * 32 + lane;               // 0..127 within the half
     const uint32_t lane_addr = (uint32_t)(q4 * 32) << 16;
     const float c2 = a.scale * 1.4426950408889634f;   // scale * log2(e)
-    // This thread's share of the lo parts of the landed Q (and K) tiles.
+    // This thread's share of the bf16 halves of the landed Q (and K) tiles:
+    // Q (the A operand) as [hi | lo] rows, K (B) as [lo | hi].
     auto split_qk = [&](int jl) -> bool {
       const bool landed = mbar_wait_pair(bar(QK_FULL), jl & 1, abort_flag, peer_flag, a.err, 35);
       if (!__all_sync(0xffffffffu, landed)) return false;
-      const int nq = new_k(jl) ? 16 : 8;
-#pragma unroll 4
-      for (int e = 0; e < nq; e++) {
-        const int idx = e * 256 + t;          // 0..4095: Q then K, 2048 float4 each
-        const int src = (idx < 2048 ? OFF_QR : OFF_KR) + (idx & 2047) * 16;
-        const int dst = (idx < 2048 ? OFF_QL : OFF_KL) + (idx & 2047) * 16;
-        const float4 x = *reinterpret_cast<const float4 *>(smem + src);
-        float4 lo;
-        lo.x = x.x - tf32_trunc(x.x); lo.y = x.y - tf32_trunc(x.y);
-        lo.z = x.z - tf32_trunc(x.z); lo.w = x.w - tf32_trunc(x.w);
-        *reinterpret_cast<float4 *>(smem + dst) = lo;
-      }
+      split_cat(smem + OFF_QR, smem + OFF_QL, 2 * QR, false, t, 256);
+      if (new_k(jl)) split_cat(smem + OFF_KR, smem + OFF_KL, 2 * QR, true, t, 256);
       fence_proxy_async();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(cluster_map(bar(QK_READY), 0));
@@ -822,44 +865,6 @@ __device__ __forceinline__ void split_lo(uint8_t *src, int lo_off, int n16, int 
   }
 }
 
-// The bf16 K-concatenated operand of K-major tiles (rows of 32 floats, 128
-// bytes, 16-byte chunks at c ^ (row % 8)): row r of dst holds bf16(hi) of its
-// 32 values in chunks 0-3 and bf16(lo) in chunks 4-7, or lo first for a B
-// operand; hi is the tf32 part the hi*hi product uses, lo = x - hi.  A task
-// (row, j) turns raw chunks 2j, 2j + 1 into chunks j and 4 + j.
-__device__ __forceinline__ uint32_t bf2_bits(float a, float b) {
-  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-  return *reinterpret_cast<uint32_t *>(&h);
-}
-__device__ __forceinline__ void split_cat(const uint8_t *src, uint8_t *dst, int rows, bool lo_first, int t,
-                                          int nthreads) {
-  for (int task = t; task < rows * 4; task += nthreads) {
-    const int r = task >> 2, j = task & 3, sw = r & 7;
-    uint32_t hw[4], lw[4];
-#pragma unroll
-    for (int u = 0; u < 2; u++) {
-      const float4 x = *reinterpret_cast<const float4 *>(src + r * 128 + (((2 * j + u) ^ sw) << 4));
-      const float h0 = tf32_trunc(x.x), h1 = tf32_trunc(x.y), h2 = tf32_trunc(x.z), h3 = tf32_trunc(x.w);
-      hw[2 * u] = bf2_bits(h0, h1);
-      hw[2 * u + 1] = bf2_bits(h2, h3);
-      lw[2 * u] = bf2_bits(x.x - h0, x.y - h1);
-      lw[2 * u + 1] = bf2_bits(x.z - h2, x.w - h3);
-    }
-    const uint4 H4 = make_uint4(hw[0], hw[1], hw[2], hw[3]), L4 = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-    *reinterpret_cast<uint4 *>(dst + r * 128 + ((j ^ sw) << 4)) = lo_first ? L4 : H4;
-    *reinterpret_cast<uint4 *>(dst + r * 128 + (((4 + j) ^ sw) << 4)) = lo_first ? H4 : L4;
-  }
-}
-
-// D (TMEM) (+)= A (shared memory) * B (shared memory), bf16 operands.
-__device__ __forceinline__ void tc_mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                            uint32_t accumulate) {
-  asm volatile(
-      "{ .reg .pred p; setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
 
 __global__ void __launch_bounds__(BW_THREADS, 1)
 attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmKk, const __grid_constant__ CUtensorMap tmVk,
@@ -1087,7 +1092,7 @@ attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmKk, const __grid_c
       for (int e = 0; e < 32; e += 4) dst[e / 4] = make_float4(dh[e], dh[e + 1], dh[e + 2], dh[e + 3]);
     }
   } else if (warp >= 10) {
-    // ------------------------------------------- lo parts of K-major tiles
+    // ----------------------------------- bf16 halves of the K-major tiles
     const int t = threadIdx.x - 320;             // 0..63
     for (int i = 0; i < n; i++) {
       const int r = i & 1;
