@@ -1,6 +1,8 @@
 // tl_gemm_tc.cu -- tensor-core GEMM engine: tcgen05 (kind::tf32) with 3xTF32
 // split accumulation, TMA-staged tiles, accumulator in TMEM (sm_100a).  (The
-// CTA-pair kernel also has an fp16-split mode, kind::f16, described with it.)
+// CTA-pair kernel also has a hybrid split, tf32 hi*hi plus the cross terms as
+// one bf16 chain, and a specialised-warp kernel an fp16 split; both are
+// described with them.)
 //
 // The three reference primitives (tinylm.c:439-537) in one kernel family:
 //   C[I,J] (=|+=) sum_r A(i,r) B(r,j)
@@ -406,15 +408,17 @@ __host__ __device__ constexpr uint32_t make_idesc_pair(bool a_mn, bool b_mn) {
          ((uint32_t)(PN >> 3) << 17) | ((uint32_t)(PM >> 4) << 24);
 }
 
-// The fp16 split (F16): instead of tf32 hi/lo, each operand is scaled by a
-// power of two (so its largest |x| lies in [2^14, 2^15)) and split into fp16
-// hi = x with its low 13 significand bits cleared (exact in fp16) and
-// lo = rn(x - hi): 11 + 11 significand bits, the accuracy of the tf32 pair,
-// and fp16 MMAs (kind::f16, K = 16) run at twice the tf32 rate.  The split warps write both parts into the lo ring, which then
-// holds the MMA operands: a K-major tile as 128-byte rows [hi 32 | lo 32], an
-// MN-major tile as an hi plane and a lo plane (64 MN elements per 128-byte row,
-// 8-row groups 1 KB apart, 64-element MN blocks 4 KB apart); the raw slot is
-// free once converted.  The epilogue multiplies by the inverse of the product
+// The fp16 split (engine 4, gemm_tc_pair_f16ws_kernel further down): instead
+// of tf32 hi/lo, each operand is scaled by a power of two (so its largest |x|
+// lies in [2^14, 2^15)) and split into fp16 hi = x with its low 13
+// significand bits cleared (exact in fp16) and lo = rn(x - hi): 11 + 11
+// significand bits, the accuracy of the tf32 pair, and fp16 MMAs (kind::f16,
+// K = 16) run at twice the tf32 rate.  The converter warps write both parts
+// into the lo ring, which then holds the MMA operands (the hybrid split uses
+// the same layouts for its bf16 halves): a K-major tile as 128-byte rows
+// [hi 32 | lo 32], an MN-major tile as an hi plane and a lo plane (64 MN
+// elements per 128-byte row, 8-row groups 1 KB apart, 64-element MN blocks
+// 4 KB apart); the raw slot is free once converted.  The epilogue multiplies by the inverse of the product
 // scale (exact).  Products summed into one output share one product scale.
 __host__ __device__ constexpr uint32_t make_idesc_pair_f16(bool a_mn, bool b_mn) {
   return (1u << 4) | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) | ((uint32_t)(PN >> 3) << 17) |
