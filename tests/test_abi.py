@@ -59,6 +59,10 @@ def test_calls_before_init_return_status_not_crash():
     assert rc == _lib.TL_ENOINIT
     assert b"tl_init" in L.tl_last_error()
     assert L.tl_set_gemm_engine(7) == _lib.TL_EINVAL
+    assert L.tl_set_gemm_engine(-1) == _lib.TL_EINVAL
+    for e in range(6):   # 0 automatic ... 5 the hybrid split: per-thread settings, no device needed
+        assert L.tl_set_gemm_engine(e) == _lib.TL_OK
+    assert L.tl_set_gemm_engine(0) == _lib.TL_OK
 
 
 def test_missing_library_fails_loudly(monkeypatch, tmp_path):
