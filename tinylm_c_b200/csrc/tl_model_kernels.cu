@@ -1013,6 +1013,7 @@ int k_embed_bwd(DeviceCtx *c, float *gemb, const int *tok, const float *dout, in
     MK_LAUNCH_CHECK();
     return TL_OK;
   }
+  if (N <= 0 || V <= 0) return TL_OK;   // no tokens: the gradient is unchanged
   // scratch: cnt[V], off[V], cur[V], list[N], sorted[N]
   int *cnt = scratch, *off = cnt + V, *cur = off + V, *list = cur + V, *sorted = list + N;
   const unsigned g = (unsigned)std::min((N + 255) / 256, 4 * c->num_sms);
