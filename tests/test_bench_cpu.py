@@ -45,3 +45,34 @@ def test_library_output_on_fd1_goes_to_stderr():
     assert r.returncode == 0, r.stderr[-2000:]
     assert "BANNER" not in r.stdout and "BANNER" in r.stderr
     assert len(r.stdout.splitlines()) == 1
+
+
+def _bench():
+    sys.path.insert(0, ROOT)
+    import bench
+    return bench
+
+
+def test_gemm_ceiling_follows_the_split():
+    """The roofline denominators: 3xTF32 = bf16 / 6 (three tf32 passes at half
+    the bf16 rate); the hybrid split = bf16 / 4 (one tf32 pass, one bf16 pass
+    over twice the K), which the training workloads use under the automatic
+    choice; the fp16 split = bf16 / 3."""
+    b = _bench()
+    assert b.gemm_ceiling(0)[0] == 6.0
+    assert b.gemm_ceiling(3)[0] == 6.0
+    assert b.gemm_ceiling(3, training=True)[0] == 6.0
+    assert b.gemm_ceiling(0, training=True)[0] == 4.0
+    assert b.gemm_ceiling(5)[0] == 4.0
+    assert b.gemm_ceiling(4)[0] == 3.0
+    assert "hybrid" in b.gemm_ceiling(0, training=True)[1]
+
+
+def test_gemm_flops_per_token_config5():
+    """6 x the GEMM-held parameters per token: 1.1325 GFLOP for the scaled
+    tiny Llama (V 8192, D 1024, 16 layers, 16 / 4 heads, F 2816, no MTP), and
+    the m1 preset's 8.99 MFLOP with two MTP heads."""
+    b = _bench()
+    assert b.gemm_flops_per_token((8192, 1024, 16, 16, 4, 2816, 256, 0)) == 1132462080
+    m1 = b.gemm_flops_per_token((2048, 128, 4, 4, 1, 336, 256, 2))
+    assert abs(m1 / 1e6 - 8.99) < 0.01
